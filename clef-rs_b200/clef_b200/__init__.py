@@ -1,0 +1,356 @@
+"""Python host mirror of the clef-rs prefill backend's C ABI (libclef_b200.so).
+
+Every compute call goes through the shared library built from csrc/ for
+sm_100a; there is no CPU or framework fallback. If the library is missing or
+cannot be loaded, importing this package raises.
+
+The operator functions take torch CUDA tensors (torch is only the device
+allocator and stream provider here) and mirror the reference engine's Candle
+custom ops (crates/core/src/models/{metal,pointwise,neural}.rs): each validates
+shapes before launch and raises ClefError carrying the library's message.
+"""
+import ctypes
+from pathlib import Path
+
+import numpy as np
+
+from .config import ClefConfig, benchmark_config, from_text_config, weight_shapes  # noqa: F401
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE.parent / "libclef_b200.so"
+
+F32, BF16 = 0, 1
+EPI_BF16, EPI_F32, EPI_ADD_F32 = 0, 1, 2
+STATUS = {0: "OK", 1: "INVALID", 2: "CUDA", 3: "UNSUPPORTED", 4: "NOMEM", 5: "CANCELLED",
+          6: "DEVICE_TIMEOUT"}
+STAGES = ["embed", "norm", "gemm", "delta_prologue", "delta_scan", "delta_epilogue",
+          "attention_prologue", "attention", "head"]
+
+# Every symbol include/clef_b200.h declares.
+EXPORTS = [
+    "clef_last_error", "clef_version", "clef_config_validate", "clef_rmsnorm", "clef_conv4",
+    "clef_delta_prologue", "clef_delta_scan_workspace_size", "clef_delta_scan", "clef_gemm_bf16",
+    "clef_gemm_swiglu", "clef_attention_gqa", "clef_compact_copy", "clef_engine_create",
+    "clef_engine_set_weight", "clef_engine_init_random", "clef_engine_get_weight",
+    "clef_engine_weight_count", "clef_engine_finalize", "clef_engine_prefill", "clef_engine_cancel",
+    "clef_engine_stage_times", "clef_engine_set_profiling", "clef_engine_destroy",
+    "clef_prefix_tokens", "clef_prefix_bytes", "clef_prefix_destroy", "clef_decide",
+]
+
+
+class ClefError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{STATUS.get(code, code)}: {msg}")
+        self.code = code
+
+
+class Decision(ctypes.Structure):
+    _fields_ = [("noul", ctypes.c_float), ("choice", ctypes.c_int32),
+                ("confidence", ctypes.c_float), ("score", ctypes.c_float)]
+
+
+_vp, _i32, _i64, _f32, _sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
+
+
+def _load():
+    if not LIB_PATH.exists():
+        raise ImportError(f"{LIB_PATH} is missing: build it with `python clef-rs_b200/build.py`")
+    L = ctypes.CDLL(str(LIB_PATH))
+    sig = {
+        "clef_last_error": (ctypes.c_char_p, []),
+        "clef_version": (ctypes.c_char_p, []),
+        "clef_config_validate": (ctypes.c_int, [_vp]),
+        "clef_rmsnorm": (ctypes.c_int, [_vp, _vp, _i64, _i32, _f32, _i32, _vp, _vp]),
+        "clef_conv4": (ctypes.c_int, [_vp, _i64, _vp, _i32, _vp, _i64, _i32, _vp, _vp]),
+        "clef_delta_prologue": (ctypes.c_int, [_vp, _i64, _i32, _i32, _vp, _i32, _vp, _vp, _vp, _i64,
+                                               _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp]),
+        "clef_delta_scan_workspace_size": (_sz, [_i64, _i32, _i32, _i32, _i32]),
+        "clef_delta_scan": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _vp,
+                                           _i32, _vp, _i32, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
+        "clef_gemm_bf16": (ctypes.c_int, [_vp, _vp, _i64, _i32, _i32, _i32, _vp, _i64, _vp]),
+        "clef_gemm_swiglu": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i32, _i32, _vp, _vp]),
+        "clef_attention_gqa": (ctypes.c_int, [_vp, _vp, _vp, _i32, _i32, _i64, _i64, _i32, _vp, _vp]),
+        "clef_compact_copy": (ctypes.c_int, [_vp, _i32, _vp, _vp, _i32, _vp, _vp]),
+        "clef_engine_create": (ctypes.c_int, [_vp, _i32, ctypes.POINTER(_vp)]),
+        "clef_engine_set_weight": (ctypes.c_int, [_vp, ctypes.c_char_p, _vp, _sz]),
+        "clef_engine_init_random": (ctypes.c_int, [_vp, ctypes.c_uint64, _f32]),
+        "clef_engine_get_weight": (ctypes.c_int, [_vp, ctypes.c_char_p, _vp, _sz]),
+        "clef_engine_weight_count": (_sz, [_vp, ctypes.c_char_p]),
+        "clef_engine_finalize": (ctypes.c_int, [_vp]),
+        "clef_engine_prefill": (ctypes.c_int, [_vp, _vp, _vp, _i32, _vp, _i64, ctypes.POINTER(_vp),
+                                               _vp, _vp]),
+        "clef_engine_cancel": (ctypes.c_int, [_vp, _i32]),
+        "clef_engine_stage_times": (ctypes.c_int, [_vp, _vp, _i32]),
+        "clef_engine_set_profiling": (ctypes.c_int, [_vp, _i32]),
+        "clef_engine_destroy": (ctypes.c_int, [_vp]),
+        "clef_prefix_tokens": (_i64, [_vp]),
+        "clef_prefix_bytes": (ctypes.c_uint64, [_vp]),
+        "clef_prefix_destroy": (ctypes.c_int, [_vp]),
+        "clef_decide": (ctypes.c_int, [_vp, _i32, _i32, _vp]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    return L
+
+
+lib = _load()
+
+
+def version() -> str:
+    return lib.clef_version().decode()
+
+
+def _check(rc: int) -> None:
+    if rc != 0:
+        raise ClefError(rc, lib.clef_last_error().decode())
+
+
+def _ptr(t) -> int:
+    if t is None:
+        return None
+    return t.data_ptr()
+
+
+def _stream(stream=None):
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+# ---------------------------------------------------------------------------
+# Operators (torch CUDA tensors in, caller-allocated outputs).
+# ---------------------------------------------------------------------------
+def rmsnorm(x, weight, eps=1e-6, out_dtype=F32, out=None, stream=None):
+    """RmsKernel / ops::rms_inner: x F32 [rows, width], weight F32 (1+w for
+    offset norms)."""
+    import torch
+    width = x.shape[-1]
+    rows = x.numel() // width
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.float32 if out_dtype == F32 else torch.bfloat16,
+                          device=x.device)
+    _check(lib.clef_rmsnorm(_ptr(x), _ptr(weight), rows, width, eps, out_dtype, _ptr(out), _stream(stream)))
+    return out
+
+
+def conv4(x, weight, history=None, out=None, stream=None):
+    """ConvKernel / causal_convolution: x F32 [T, width], weight F32 [width, 4]."""
+    import torch
+    T, width = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    hr = 0 if history is None else history.shape[0]
+    _check(lib.clef_conv4(_ptr(x), x.stride(0), _ptr(history), hr, _ptr(weight), T, width, _ptr(out),
+                          _stream(stream)))
+    return out
+
+
+def delta_prologue(proj, a_col, b_col, conv_weight, dt_bias, a_log, Hk, Hv, dk=128, dv=128,
+                   history=None, stream=None):
+    """ConvKernel + DeltaPrepareKernel + gates: returns q, k, v, g, beta."""
+    import torch
+    T = proj.shape[0]
+    dev = proj.device
+    q = torch.empty((T, Hk, dk), dtype=torch.float32, device=dev)
+    k = torch.empty_like(q)
+    v = torch.empty((T, Hv, dv), dtype=torch.float32, device=dev)
+    g = torch.empty((T, Hv), dtype=torch.float32, device=dev)
+    beta = torch.empty_like(g)
+    hr = 0 if history is None else history.shape[0]
+    _check(lib.clef_delta_prologue(_ptr(proj), proj.stride(0), a_col, b_col, _ptr(history), hr,
+                                   _ptr(conv_weight), _ptr(dt_bias), _ptr(a_log), T, Hk, Hv, dk, dv,
+                                   _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _stream(stream)))
+    return q, k, v, g, beta
+
+
+def delta_scan_workspace_size(total_tokens, nseq, Hv, dk=128, dv=128) -> int:
+    return int(lib.clef_delta_scan_workspace_size(total_tokens, nseq, Hv, dk, dv))
+
+
+def delta_scan(q, k, v, g, beta, cu_seqlens=None, init_state=None, init_shared=False, capture=0,
+               final_state=False, workspace=None, stream=None):
+    """DeltaKernel / CachedDelta: chunked scan. q, k [T, Hk, 128] normalised
+    (q scaled), v [T, Hv, 128], g (log decay), beta [T, Hv]. Returns
+    (out [T, Hv, 128], captured state or None, final states or None)."""
+    import torch
+    T, Hk, dk = q.shape
+    Hv, dv = v.shape[1], v.shape[2]
+    dev = q.device
+    if cu_seqlens is None:
+        nseq, cu_arr = 1, None
+    else:
+        cu_np = np.ascontiguousarray(cu_seqlens, dtype=np.int64)
+        nseq = cu_np.size - 1
+        cu_arr = cu_np
+    out = torch.empty((T, Hv, dv), dtype=torch.float32, device=dev)
+    cap = torch.empty((Hv, dk, dv), dtype=torch.float32, device=dev) if capture else None
+    fin = torch.empty((nseq, Hv, dk, dv), dtype=torch.float32, device=dev) if final_state else None
+    if workspace is None:
+        size = delta_scan_workspace_size(T, nseq, Hv, dk, dv)
+        workspace = torch.empty(size, dtype=torch.uint8, device=dev)
+    _check(lib.clef_delta_scan(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), T, Hk, Hv, dk, dv,
+                               cu_arr.ctypes.data if cu_arr is not None else None, nseq,
+                               _ptr(init_state), int(bool(init_shared)), int(capture), _ptr(cap),
+                               _ptr(fin), _ptr(out), _ptr(workspace), workspace.numel(),
+                               _stream(stream)))
+    return out, cap, fin
+
+
+def gemm(x, w, epilogue=EPI_BF16, out=None, stream=None):
+    """GemmKernel / Projection::forward: x BF16 [M, K], w BF16 [N, K]."""
+    import torch
+    M, K = x.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16 if epilogue == EPI_BF16 else torch.float32,
+                          device=x.device)
+    _check(lib.clef_gemm_bf16(_ptr(x), _ptr(w), M, N, K, epilogue, _ptr(out), out.stride(0),
+                              _stream(stream)))
+    return out
+
+
+def gemm_swiglu(x, wg, wu, out=None, stream=None):
+    """gated TileKernel / Projection::gated_forward: silu(x wg^T) * (x wu^T)."""
+    import torch
+    M, K = x.shape
+    N = wg.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    _check(lib.clef_gemm_swiglu(_ptr(x), _ptr(wg), _ptr(wu), M, N, K, _ptr(out), _stream(stream)))
+    return out
+
+
+def attention_gqa(q, k, v, out=None, stream=None):
+    """AttentionKernel / ops::attention: q BF16 [Hq, Tq, 256], k, v BF16
+    [Hkv, Tk, 256], causal lower-right; returns F32 [Hq, Tq, 256]."""
+    import torch
+    Hq, Tq, d = q.shape
+    Hkv, Tk = k.shape[0], k.shape[1]
+    if out is None:
+        out = torch.empty((Hq, Tq, d), dtype=torch.float32, device=q.device)
+    _check(lib.clef_attention_gqa(_ptr(q), _ptr(k), _ptr(v), Hq, Hkv, Tq, Tk, d, _ptr(out),
+                                  _stream(stream)))
+    return out
+
+
+def compact_copy(src, out=None, stream=None):
+    """CompactCopy: contiguous copy of a strided view (<= 4 dims)."""
+    import torch
+    if out is None:
+        out = torch.empty(src.shape, dtype=src.dtype, device=src.device)
+    nd = src.dim()
+    dims = (ctypes.c_int64 * nd)(*src.shape)
+    strides = (ctypes.c_int64 * nd)(*src.stride())
+    _check(lib.clef_compact_copy(_ptr(src), nd, dims, strides, src.element_size(), _ptr(out),
+                                 _stream(stream)))
+    return out
+
+
+def decide(logits: np.ndarray):
+    """answers (types.rs:728-802) over [n, 7] logits -> list of Decision."""
+    lg = np.ascontiguousarray(logits, dtype=np.float32).reshape(-1, 7)
+    out = (Decision * lg.shape[0])()
+    _check(lib.clef_decide(lg.ctypes.data, lg.shape[0], 7, out))
+    return list(out)
+
+
+# ---------------------------------------------------------------------------
+# Engine (Backbone::load / forward / prefill).
+# ---------------------------------------------------------------------------
+class Prefix:
+    """Captured prefix state (PrefixState) owned by the library."""
+
+    def __init__(self, handle):
+        self.handle = handle
+
+    @property
+    def tokens(self) -> int:
+        return int(lib.clef_prefix_tokens(self.handle))
+
+    def bytes(self) -> int:
+        return int(lib.clef_prefix_bytes(self.handle))
+
+    def close(self):
+        if self.handle:
+            lib.clef_prefix_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.close()
+
+
+class Engine:
+    def __init__(self, cfg: ClefConfig, device: int = 0):
+        self.cfg = cfg
+        h = ctypes.c_void_p()
+        _check(lib.clef_engine_create(ctypes.byref(cfg), device, ctypes.byref(h)))
+        self.handle = h
+
+    def count(self, name: str) -> int:
+        return int(lib.clef_engine_weight_count(self.handle, name.encode()))
+
+    def set_weight(self, name: str, data) -> None:
+        a = np.ascontiguousarray(data, dtype=np.float32).reshape(-1)
+        _check(lib.clef_engine_set_weight(self.handle, name.encode(), a.ctypes.data, a.size))
+
+    def get_weight(self, name: str) -> np.ndarray:
+        n = self.count(name)
+        out = np.empty(n, np.float32)
+        _check(lib.clef_engine_get_weight(self.handle, name.encode(), out.ctypes.data, n))
+        return out
+
+    def init_random(self, seed: int, std: float = 0.02) -> None:
+        _check(lib.clef_engine_init_random(self.handle, seed, std))
+
+    def finalize(self) -> None:
+        _check(lib.clef_engine_finalize(self.handle))
+
+    def set_profiling(self, on: bool) -> None:
+        _check(lib.clef_engine_set_profiling(self.handle, int(on)))
+
+    def stage_times(self) -> dict:
+        buf = (ctypes.c_float * len(STAGES))()
+        n = lib.clef_engine_stage_times(self.handle, buf, len(STAGES))
+        return {STAGES[i]: float(buf[i]) for i in range(n)}
+
+    def cancel(self, on: bool = True) -> None:
+        _check(lib.clef_engine_cancel(self.handle, int(on)))
+
+    def prefill(self, seqs, initial: Prefix = None, capture: int = 0, logits: bool = True,
+                hidden: bool = False):
+        """seqs: list of int arrays (token ids). Returns (logits [n, outputs]
+        or None, hidden or None, captured Prefix or None)."""
+        lens = [len(s) for s in seqs]
+        offsets = np.zeros(len(seqs) + 1, np.int64)
+        offsets[1:] = np.cumsum(lens)
+        ids = np.ascontiguousarray(np.concatenate([np.asarray(s, dtype=np.int32) for s in seqs]))
+        return self.prefill_packed(ids, offsets, initial, capture, logits, hidden)
+
+    def prefill_packed(self, ids: np.ndarray, offsets: np.ndarray, initial: Prefix = None,
+                       capture: int = 0, logits: bool = True, hidden: bool = False,
+                       logits_out: np.ndarray = None):
+        nseq = offsets.size - 1
+        lg = None
+        if logits and self.cfg.head_outputs:
+            lg = logits_out if logits_out is not None else np.empty((nseq, self.cfg.head_outputs), np.float32)
+        hid = None
+        if hidden:
+            pre = initial.tokens if (initial is not None and nseq == 1) else 0
+            hid = np.empty((pre + int(offsets[-1]), self.cfg.hidden_size), np.float32)
+        cap = ctypes.c_void_p()
+        _check(lib.clef_engine_prefill(self.handle, ids.ctypes.data, offsets.ctypes.data, nseq,
+                                       initial.handle if initial is not None else None, int(capture),
+                                       ctypes.byref(cap) if capture else None,
+                                       lg.ctypes.data if lg is not None else None,
+                                       hid.ctypes.data if hid is not None else None))
+        return lg, hid, (Prefix(cap.value) if cap.value else None)
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib.clef_engine_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.close()

@@ -1,0 +1,98 @@
+// kernels.cuh — launchers shared between the operator entry points and the
+// engine. All take device pointers and a stream and return a clef_status.
+#pragma once
+
+#include "common.cuh"
+
+namespace clef {
+
+// Packed-sequence description used by the varlen kernels: cu_seqlens holds
+// nseq + 1 token offsets (device memory, int64).
+// When cu_seqlens is set, the int32 query-block offsets (64-row blocks) of
+// the attention kernel follow it in the same buffer:
+// (const int32_t*)(cu_seqlens + nseq + 1), nseq + 1 entries, total `qblocks`.
+struct SeqPack {
+  const int64_t* cu_seqlens = nullptr;  // device, nseq + 1 entries; NULL = one sequence
+  int32_t nseq = 1;
+  int64_t total = 0;
+  int64_t qblocks = 0;
+};
+
+// ---- pointwise.cu ----------------------------------------------------------
+int launch_rmsnorm(const float* x, const float* w, int64_t rows, int width, float eps,
+                   int out_dtype, void* out, cudaStream_t s);
+int launch_conv4(const float* x, int64_t ldx, const float* hist, int hist_rows, const float* w,
+                 int64_t T, int width, float* out, cudaStream_t s);
+// DeltaNet prologue over packed sequences; `hist` [hist_rows, qkv width] is
+// the conv history every sequence continues from (NULL = zeros).
+int launch_delta_prologue(const float* proj, int64_t ldp, int a_col, int b_col, const float* hist,
+                          int hist_rows, const float* conv_w, const float* dt_bias,
+                          const float* a_log, const SeqPack& pack, int Hk, int Hv, int dk, int dv,
+                          float* q, float* k, float* v, float* g, float* beta, cudaStream_t s);
+// y[t, h*dv + i] = bf16(bf16(rms(bf16(o))*w) * silu(bf16(z))) for each v-head.
+int launch_delta_epilogue(const float* o, const float* z, int64_t ldz, const float* w, float eps,
+                          int64_t T, int Hv, int dv, uint16_t* y, cudaStream_t s);
+// Attention prologue: q/k RMSNorm (offset weights already +1) and partial
+// RoPE from the fused BF16 projection; positions = offset + index in sequence.
+int launch_attention_prologue(const uint16_t* proj, int64_t ldp, const float* qw, const float* kw,
+                              float eps, const SeqPack& pack, int64_t pos_offset, int H, int Hkv,
+                              int d, int rot, const float* inv_freq_dev, uint16_t* q_out,
+                              uint16_t* k_out, cudaStream_t s);
+int launch_embed(const uint16_t* table, const int32_t* ids, int64_t T, int hidden, float* h,
+                 cudaStream_t s);
+// Final RMSNorm of each sequence's last row and the linear schema head.
+int launch_head(const float* h, const float* norm_w, float eps, const SeqPack& pack, int hidden,
+                const float* head_w, int n_out, float* logits, cudaStream_t s);
+// Gathers rows [r0, r0+count) of a [T, ncols] BF16/F32 matrix (row stride ld)
+// into dst [count, ncols].
+int launch_copy_rows(const void* src, int64_t ld, int64_t r0, int64_t count, int64_t ncols,
+                     int elem, void* dst, int64_t ldd, cudaStream_t s);
+
+// ---- delta_scan.cu ----------------------------------------------------------
+size_t delta_scan_workspace(int64_t total_tokens, int nseq, int Hv, int dk, int dv);
+// cu_host: host int64 [nseq+1].
+int launch_delta_scan(const float* q, const float* k, const float* v, const float* g,
+                      const float* beta, const int64_t* cu_host, int nseq, int Hk, int Hv, int dk,
+                      int dv, const float* init, int init_shared, int64_t capture,
+                      float* capture_state, float* final_state, float* out, void* ws,
+                      size_t ws_bytes, cudaStream_t s);
+
+// ---- rng.cu -----------------------------------------------------------------
+// Philox4x32-10 counter-based normal / uniform generator, deterministic in
+// (seed, stream, element index) on host and device.
+uint64_t name_stream(const char* name);
+int launch_fill_normal_bf16(uint16_t* dst, int64_t n, uint64_t seed, uint64_t stream, float mean,
+                            float std, cudaStream_t s);
+void host_fill(float* dst, int64_t n, uint64_t seed, uint64_t stream, int kind, float a, float b);
+enum HostFill { kFillNormal = 0, kFillUniform = 1 };
+
+// ---- gemm.cu ----------------------------------------------------------------
+enum GemmEpi { kEpiBF16 = 0, kEpiF32 = 1, kEpiAddF32 = 2, kEpiSwiGLU = 3 };
+// out[M, N] (ldo) = epilogue(X[M, K] * W[N, K]^T). For kEpiSwiGLU, W2 is the
+// up matrix and W the gate matrix (both [N, K]); out is BF16.
+int launch_gemm(const uint16_t* X, const uint16_t* W, const uint16_t* W2, int64_t M, int N, int K,
+                int epi, void* out, int64_t ldo, cudaStream_t s);
+
+// ---- attention.cu -----------------------------------------------------------
+struct AttnArgs {
+  const uint16_t* q = nullptr;  // token-major: q[t*q_ts + h*q_hs + e]
+  int64_t q_ts = 0, q_hs = 0;
+  const uint16_t* k = nullptr;  // own keys:  k[t*k_ts + h*k_hs + e]
+  const uint16_t* v = nullptr;
+  int64_t k_ts = 0, k_hs = 0, v_ts = 0, v_hs = 0;
+  const uint16_t* pk = nullptr;  // shared prefix keys (prefix_len rows), same for all seqs
+  const uint16_t* pv = nullptr;
+  int64_t p_ts = 0, p_hs = 0;
+  int64_t prefix_len = 0;
+  int H = 0, Hkv = 0, d = 256;
+  float scale = 0.0625f;
+  // Output: F32 [t*o_ts + h*o_hs + e] when gate == nullptr, else BF16
+  // o * sigmoid(gate[t*g_ts + h*g_hs + e]).
+  void* out = nullptr;
+  int64_t o_ts = 0, o_hs = 0;
+  const uint16_t* gate = nullptr;
+  int64_t g_ts = 0, g_hs = 0;
+};
+int launch_attention(const AttnArgs& a, const SeqPack& pack, cudaStream_t s);
+
+}  // namespace clef

@@ -1,0 +1,506 @@
+// pointwise.cu — HBM-bound kernels of the prefill: RMSNorm, causal conv,
+// the DeltaNet prologue (conv + SiLU + L2 + gates) and epilogue
+// (RMSNorm_128 * silu(z)), the attention prologue (q/k norm + partial RoPE),
+// the embedding gather and the schema head.
+//
+// Every kernel reads and writes with 16-byte vectors where the layout allows
+// and reduces with warp shuffles; one warp owns one normalisation row, so no
+// shared-memory reduction or block barrier sits on the hot path.
+#include <cmath>
+
+#include "kernels.cuh"
+
+namespace clef {
+
+namespace {
+
+__device__ __forceinline__ int64_t seq_of(const int64_t* cu, int nseq, int64_t t) {
+  int lo = 0, hi = nseq - 1;
+  while (lo < hi) {  // largest s with cu[s] <= t
+    int mid = (lo + hi + 1) >> 1;
+    if (cu[mid] <= t) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+// ---- RMSNorm (ops::rms_inner, ops.rs:24-32; clef_rms, pointwise.metal:7-43) --
+// One warp per row: sum of squares, inverse = 1 / sqrt(sum / width + eps),
+// out = (x * inverse) * w.
+template <int OUT_BF16>
+__global__ void rms_kernel(const float* __restrict__ x, const float* __restrict__ w, int64_t rows,
+                           int width, float eps, void* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float* xr = x + row * width;
+  float s = 0.f;
+  const bool vec = (width & 3) == 0;
+  if (vec) {
+    for (int i = lane * 4; i < width; i += 128) {
+      float4 a = *reinterpret_cast<const float4*>(xr + i);
+      s += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
+    }
+  } else {
+    for (int i = lane; i < width; i += 32) s += xr[i] * xr[i];
+  }
+  s = warp_sum(s);
+  const float inv = 1.f / sqrtf(s / (float)width + eps);
+  if (vec) {
+    for (int i = lane * 4; i < width; i += 128) {
+      float4 a = *reinterpret_cast<const float4*>(xr + i);
+      float4 b = *reinterpret_cast<const float4*>(w + i);
+      float r0 = __fmul_rn(__fmul_rn(a.x, inv), b.x), r1 = __fmul_rn(__fmul_rn(a.y, inv), b.y);
+      float r2 = __fmul_rn(__fmul_rn(a.z, inv), b.z), r3 = __fmul_rn(__fmul_rn(a.w, inv), b.w);
+      if (OUT_BF16) {
+        uint2 p = make_uint2(pack_bf16x2(r0, r1), pack_bf16x2(r2, r3));
+        *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(out) + row * width + i) = p;
+      } else {
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + row * width + i) =
+            make_float4(r0, r1, r2, r3);
+      }
+    }
+  } else {
+    for (int i = lane; i < width; i += 32) {
+      float r = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+      if (OUT_BF16) reinterpret_cast<uint16_t*>(out)[row * width + i] = f2bf(r);
+      else reinterpret_cast<float*>(out)[row * width + i] = r;
+    }
+  }
+}
+
+// ---- causal conv (causal_convolution, qwen.rs:765-796) -----------------------
+// value = ((((0 + x[t-3] w0) + x[t-2] w1) + x[t-1] w2) + x[t] w3), rows before
+// the first input come from `hist` (right-aligned) or are zero.
+__device__ __forceinline__ float conv_tap_row(const float* x, int64_t ldx, const float* hist,
+                                              int hist_rows, int width, int64_t seq_start,
+                                              int64_t pos, int delay, int c) {
+  const int64_t r = pos - delay;
+  if (r >= 0) return x[(seq_start + r) * ldx + c];
+  const int64_t hr = hist_rows + r;
+  if (hist && hr >= 0) return hist[hr * width + c];
+  return 0.f;
+}
+
+__global__ void conv4_kernel(const float* __restrict__ x, int64_t ldx, const float* __restrict__ hist,
+                             int hist_rows, const float* __restrict__ w, int64_t T, int width,
+                             float* __restrict__ out) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= T * width) return;
+  const int64_t t = idx / width;
+  const int c = (int)(idx % width);
+  float acc = 0.f;
+#pragma unroll
+  for (int tap = 0; tap < 4; ++tap) {
+    const int delay = 3 - tap;
+    const int64_t r = t - delay;
+    if (r < 0 && !(hist && hist_rows + r >= 0)) continue;
+    const float xv = conv_tap_row(x, ldx, hist, hist_rows, width, 0, t, delay, c);
+    acc = __fadd_rn(acc, __fmul_rn(xv, w[c * 4 + tap]));
+  }
+  out[t * width + c] = acc;
+}
+
+// ---- DeltaNet prologue -------------------------------------------------------
+// One CTA of 256 threads per token; each thread owns 4 consecutive channels,
+// so one warp covers exactly one 128-wide q/k head and reduces its L2 norm
+// with shuffles (clef_delta_prepare, pointwise.metal:69-114; l2 and scaling,
+// qwen.rs:837-845; gates, qwen.rs:619-627).
+__global__ void __launch_bounds__(256) delta_prologue_kernel(
+    const float* __restrict__ proj, int64_t ldp, int a_col, int b_col,
+    const float* __restrict__ hist, int hist_rows, const float* __restrict__ conv_w,
+    const float* __restrict__ dt_bias, const float* __restrict__ a_log,
+    const int64_t* __restrict__ cu, int nseq, int Hk, int Hv, float qscale,
+    float* __restrict__ q, float* __restrict__ k, float* __restrict__ v, float* __restrict__ g,
+    float* __restrict__ beta) {
+  const int64_t t = blockIdx.x;
+  const int64_t start = cu ? cu[seq_of(cu, nseq, t)] : 0;  // cu == NULL: one sequence
+  const int64_t pos = t - start;
+  const int key = Hk * 128;
+  const int width = 2 * key + Hv * 128;
+  const int lane = threadIdx.x & 31;
+  for (int base = threadIdx.x * 4; base < width; base += 1024) {
+    // Four causal taps for four channels.
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int tap = 0; tap < 4; ++tap) {
+      const int delay = 3 - tap;
+      const int64_t r = pos - delay;
+      float4 xv;
+      if (r >= 0) {
+        xv = *reinterpret_cast<const float4*>(proj + (start + r) * ldp + base);
+      } else if (hist && hist_rows + r >= 0) {
+        xv = *reinterpret_cast<const float4*>(hist + (hist_rows + r) * width + base);
+      } else {
+        continue;
+      }
+      const float4 wv0 = *reinterpret_cast<const float4*>(conv_w + (base + 0) * 4);
+      const float4 wv1 = *reinterpret_cast<const float4*>(conv_w + (base + 1) * 4);
+      const float4 wv2 = *reinterpret_cast<const float4*>(conv_w + (base + 2) * 4);
+      const float4 wv3 = *reinterpret_cast<const float4*>(conv_w + (base + 3) * 4);
+      const float w0 = tap == 0 ? wv0.x : tap == 1 ? wv0.y : tap == 2 ? wv0.z : wv0.w;
+      const float w1 = tap == 0 ? wv1.x : tap == 1 ? wv1.y : tap == 2 ? wv1.z : wv1.w;
+      const float w2 = tap == 0 ? wv2.x : tap == 1 ? wv2.y : tap == 2 ? wv2.z : wv2.w;
+      const float w3 = tap == 0 ? wv3.x : tap == 1 ? wv3.y : tap == 2 ? wv3.z : wv3.w;
+      acc.x = __fadd_rn(acc.x, __fmul_rn(xv.x, w0));
+      acc.y = __fadd_rn(acc.y, __fmul_rn(xv.y, w1));
+      acc.z = __fadd_rn(acc.z, __fmul_rn(xv.z, w2));
+      acc.w = __fadd_rn(acc.w, __fmul_rn(xv.w, w3));
+    }
+    float4 m = make_float4(silu_f(acc.x), silu_f(acc.y), silu_f(acc.z), silu_f(acc.w));
+    if (base < 2 * key) {
+      // The whole warp sits in one head (base aligned to 1024, heads of 128).
+      float ss = m.x * m.x + m.y * m.y + m.z * m.z + m.w * m.w;
+      ss = warp_sum(ss);
+      const float n = sqrtf(ss + 1e-6f);
+      float4 r = make_float4(m.x / n, m.y / n, m.z / n, m.w / n);
+      if (base < key) {
+        r = make_float4(__fmul_rn(r.x, qscale), __fmul_rn(r.y, qscale), __fmul_rn(r.z, qscale),
+                        __fmul_rn(r.w, qscale));
+        *reinterpret_cast<float4*>(q + t * key + base) = r;
+      } else {
+        *reinterpret_cast<float4*>(k + t * key + (base - key)) = r;
+      }
+    } else {
+      *reinterpret_cast<float4*>(v + t * (Hv * 128) + (base - 2 * key)) = m;
+    }
+    (void)lane;
+  }
+  for (int h = threadIdx.x; h < Hv; h += blockDim.x) {
+    const float a = __fadd_rn(proj[t * ldp + a_col + h], dt_bias[h]);
+    const float sp = __fadd_rn(fmaxf(a, 0.f), logf(__fadd_rn(expf(-fabsf(a)), 1.f)));
+    g[t * Hv + h] = __fmul_rn(sp, -expf(a_log[h]));
+    beta[t * Hv + h] = sigmoid_f(proj[t * ldp + b_col + h]);
+  }
+}
+
+// ---- DeltaNet epilogue (qwen.rs:671-676) -------------------------------------
+// Rounding points follow the reference run in the BF16 projection dtype:
+// o -> P, norm output -> P, z in P, product -> P.
+__global__ void delta_epilogue_kernel(const float* __restrict__ o, const float* __restrict__ z,
+                                      int64_t ldz, const float* __restrict__ w, float eps,
+                                      int64_t rows, int Hv, uint16_t* __restrict__ y) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);  // t*Hv + h
+  if (row >= rows) return;
+  const int64_t t = row / Hv;
+  const int h = (int)(row % Hv);
+  float4 a = *reinterpret_cast<const float4*>(o + row * 128 + lane * 4);
+  a = make_float4(bf16_round(a.x), bf16_round(a.y), bf16_round(a.z), bf16_round(a.w));
+  float ss = a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
+  ss = warp_sum(ss);
+  const float inv = 1.f / sqrtf(ss / 128.f + eps);
+  const float4 wv = *reinterpret_cast<const float4*>(w + lane * 4);
+  const float4 zv = *reinterpret_cast<const float4*>(z + t * ldz + h * 128 + lane * 4);
+  float n0 = bf16_round(__fmul_rn(__fmul_rn(a.x, inv), wv.x));
+  float n1 = bf16_round(__fmul_rn(__fmul_rn(a.y, inv), wv.y));
+  float n2 = bf16_round(__fmul_rn(__fmul_rn(a.z, inv), wv.z));
+  float n3 = bf16_round(__fmul_rn(__fmul_rn(a.w, inv), wv.w));
+  float y0 = __fmul_rn(n0, silu_f(bf16_round(zv.x)));
+  float y1 = __fmul_rn(n1, silu_f(bf16_round(zv.y)));
+  float y2 = __fmul_rn(n2, silu_f(bf16_round(zv.z)));
+  float y3 = __fmul_rn(n3, silu_f(bf16_round(zv.w)));
+  *reinterpret_cast<uint2*>(y + t * (int64_t)Hv * 128 + h * 128 + lane * 4) =
+      make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y2, y3));
+}
+
+// ---- attention prologue (qwen.rs:463-490; rotary, ops.rs:144-188) ------------
+// One warp per (token, head) row of 256 features, 8 per lane. Rows [0, H) are
+// query heads (projection columns h*2d .. h*2d+d), rows [H, H+Hkv) key heads
+// (columns 2*H*d + j*d). The norm output is rounded to BF16 (the projection
+// dtype) before the rotation, and the rotated features again after it.
+__global__ void attention_prologue_kernel(const uint16_t* __restrict__ proj, int64_t ldp,
+                                          const float* __restrict__ qw, const float* __restrict__ kw,
+                                          float eps, const int64_t* __restrict__ cu, int nseq,
+                                          int64_t pos_offset, int H, int Hkv, int rot,
+                                          const float* __restrict__ inv_freq,
+                                          uint16_t* __restrict__ q_out, uint16_t* __restrict__ k_out,
+                                          int64_t T) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int per = H + Hkv;
+  if (row >= T * per) return;
+  const int64_t t = row / per;
+  const int hh = (int)(row % per);
+  const bool isq = hh < H;
+  const int d = 256;
+  const uint16_t* src = isq ? proj + t * ldp + (int64_t)hh * 2 * d
+                            : proj + t * ldp + (int64_t)2 * H * d + (int64_t)(hh - H) * d;
+  const float* w = isq ? qw : kw;
+  uint4 raw = *reinterpret_cast<const uint4*>(src + lane * 8);
+  float x[8];
+  const uint32_t r32[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    x[2 * i] = __uint_as_float(r32[i] << 16);
+    x[2 * i + 1] = __uint_as_float(r32[i] & 0xffff0000u);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
+  ss = warp_sum(ss);
+  const float inv = 1.f / sqrtf(ss / (float)d + eps);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = bf16_round(__fmul_rn(__fmul_rn(x[i], inv), w[lane * 8 + i]));
+  // Partial NeoX rotation on features [0, rot): pairs (i, i + rot/2).
+  const int half = rot / 2;
+  const int64_t start = cu ? cu[seq_of(cu, nseq, t)] : 0;
+  const float pos = (float)(pos_offset + (t - start));
+  float partner[8];
+  const int lane_half = half / 8;  // lanes covering the first half
+#pragma unroll
+  for (int i = 0; i < 8; ++i) partner[i] = __shfl_xor_sync(0xffffffffu, x[i], lane_half);
+  if (lane * 8 < rot) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int f = lane * 8 + i;
+      const int fi = f < half ? f : f - half;
+      const float ang = __fmul_rn(pos, inv_freq[fi]);
+      const float c = cosf(ang), sn = sinf(ang);
+      // rotation * cos + rotate_half(rotation) * sin
+      const float rotated = f < half ? -partner[i] : partner[i];
+      x[i] = bf16_round(__fadd_rn(__fmul_rn(x[i], c), __fmul_rn(rotated, sn)));
+    }
+  }
+  uint16_t* dst = isq ? q_out + (t * H + hh) * (int64_t)d : k_out + (t * Hkv + (hh - H)) * (int64_t)d;
+  uint4 o;
+  o.x = pack_bf16x2(x[0], x[1]);
+  o.y = pack_bf16x2(x[2], x[3]);
+  o.z = pack_bf16x2(x[4], x[5]);
+  o.w = pack_bf16x2(x[6], x[7]);
+  *reinterpret_cast<uint4*>(dst + lane * 8) = o;
+}
+
+// ---- embedding gather (Backbone::forward, qwen.rs:316-317; F32 cast :373) ----
+__global__ void embed_kernel(const uint16_t* __restrict__ table, const int32_t* __restrict__ ids,
+                             int hidden, float* __restrict__ h) {
+  const int64_t t = blockIdx.x;
+  const uint16_t* src = table + (int64_t)ids[t] * hidden;
+  for (int i = threadIdx.x * 8; i < hidden; i += blockDim.x * 8) {
+    uint4 raw = *reinterpret_cast<const uint4*>(src + i);
+    const uint32_t r32[4] = {raw.x, raw.y, raw.z, raw.w};
+    float4 a = make_float4(__uint_as_float(r32[0] << 16), __uint_as_float(r32[0] & 0xffff0000u),
+                           __uint_as_float(r32[1] << 16), __uint_as_float(r32[1] & 0xffff0000u));
+    float4 b = make_float4(__uint_as_float(r32[2] << 16), __uint_as_float(r32[2] & 0xffff0000u),
+                           __uint_as_float(r32[3] << 16), __uint_as_float(r32[3] & 0xffff0000u));
+    *reinterpret_cast<float4*>(h + t * hidden + i) = a;
+    *reinterpret_cast<float4*>(h + t * hidden + i + 4) = b;
+  }
+}
+
+// ---- final norm + linear schema head at each sequence's last token -----------
+__global__ void head_kernel(const float* __restrict__ h, const float* __restrict__ nw, float eps,
+                            const int64_t* __restrict__ cu, int hidden,
+                            const float* __restrict__ hw, int n_out, float* __restrict__ logits) {
+  extern __shared__ float hn[];  // [hidden]
+  __shared__ float red[32];
+  __shared__ float inv_s;
+  const int s = blockIdx.x;
+  const int64_t row = cu[s + 1] - 1;
+  const float* x = h + row * hidden;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) ss += x[i] * x[i];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) inv_s = 1.f / sqrtf(v / (float)hidden + eps);
+  }
+  __syncthreads();
+  const float inv = inv_s;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) hn[i] = __fmul_rn(__fmul_rn(x[i], inv), nw[i]);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int o = warp; o < n_out; o += blockDim.x >> 5) {
+    float acc = 0.f;
+    for (int i = lane; i < hidden; i += 32) acc += hw[(int64_t)o * hidden + i] * hn[i];
+    acc = warp_sum(acc);
+    if (lane == 0) logits[(int64_t)s * n_out + o] = acc;
+  }
+}
+
+__global__ void copy_rows_kernel(const uint8_t* __restrict__ src, int64_t ld_bytes,
+                                 int64_t row_bytes, uint8_t* __restrict__ dst, int64_t ldd_bytes) {
+  const int64_t r = blockIdx.x;
+  for (int64_t i = threadIdx.x * 4; i < row_bytes; i += blockDim.x * 4)
+    *reinterpret_cast<uint32_t*>(dst + r * ldd_bytes + i) =
+        *reinterpret_cast<const uint32_t*>(src + r * ld_bytes + i);
+}
+
+template <typename T>
+__global__ void compact_copy_kernel(const T* __restrict__ src, int64_t n, int64_t d1, int64_t d2,
+                                    int64_t d3, int64_t s0, int64_t s1, int64_t s2, int64_t s3,
+                                    T* __restrict__ dst) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  int64_t r = i;
+  const int64_t i3 = r % d3;
+  r /= d3;
+  const int64_t i2 = r % d2;
+  r /= d2;
+  const int64_t i1 = r % d1;
+  const int64_t i0 = r / d1;
+  dst[i] = src[i0 * s0 + i1 * s1 + i2 * s2 + i3 * s3];
+}
+
+}  // namespace
+
+int launch_rmsnorm(const float* x, const float* w, int64_t rows, int width, float eps, int out_dtype,
+                   void* out, cudaStream_t s) {
+  if (rows == 0) return CLEF_OK;
+  const int warps = 8;
+  const dim3 grid((unsigned)ceil_div(rows, warps));
+  if (out_dtype == CLEF_BF16)
+    rms_kernel<1><<<grid, warps * 32, 0, s>>>(x, w, rows, width, eps, out);
+  else
+    rms_kernel<0><<<grid, warps * 32, 0, s>>>(x, w, rows, width, eps, out);
+  return launch_status("rmsnorm");
+}
+
+int launch_conv4(const float* x, int64_t ldx, const float* hist, int hist_rows, const float* w,
+                 int64_t T, int width, float* out, cudaStream_t s) {
+  if (T == 0) return CLEF_OK;
+  const int64_t n = T * width;
+  conv4_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(x, ldx, hist, hist_rows, w, T, width, out);
+  return launch_status("conv4");
+}
+
+int launch_delta_prologue(const float* proj, int64_t ldp, int a_col, int b_col, const float* hist,
+                          int hist_rows, const float* conv_w, const float* dt_bias,
+                          const float* a_log, const SeqPack& pack, int Hk, int Hv, int dk, int dv,
+                          float* q, float* k, float* v, float* g, float* beta, cudaStream_t s) {
+  if (pack.total == 0) return CLEF_OK;
+  (void)dk;
+  (void)dv;
+  const float qscale = (float)(1.0 / std::sqrt(128.0));
+  delta_prologue_kernel<<<(unsigned)pack.total, 256, 0, s>>>(
+      proj, ldp, a_col, b_col, hist, hist_rows, conv_w, dt_bias, a_log, pack.cu_seqlens, pack.nseq,
+      Hk, Hv, qscale, q, k, v, g, beta);
+  return launch_status("delta_prologue");
+}
+
+int launch_delta_epilogue(const float* o, const float* z, int64_t ldz, const float* w, float eps,
+                          int64_t T, int Hv, int dv, uint16_t* y, cudaStream_t s) {
+  (void)dv;
+  const int64_t rows = T * Hv;
+  if (rows == 0) return CLEF_OK;
+  delta_epilogue_kernel<<<(unsigned)ceil_div(rows, 8), 256, 0, s>>>(o, z, ldz, w, eps, rows, Hv, y);
+  return launch_status("delta_epilogue");
+}
+
+int launch_attention_prologue(const uint16_t* proj, int64_t ldp, const float* qw, const float* kw,
+                              float eps, const SeqPack& pack, int64_t pos_offset, int H, int Hkv,
+                              int d, int rot, const float* inv_freq_dev, uint16_t* q_out,
+                              uint16_t* k_out, cudaStream_t s) {
+  (void)d;
+  const int64_t rows = pack.total * (H + Hkv);
+  if (rows == 0) return CLEF_OK;
+  attention_prologue_kernel<<<(unsigned)ceil_div(rows, 8), 256, 0, s>>>(
+      proj, ldp, qw, kw, eps, pack.cu_seqlens, pack.nseq, pos_offset, H, Hkv, rot, inv_freq_dev,
+      q_out, k_out, pack.total);
+  return launch_status("attention_prologue");
+}
+
+int launch_embed(const uint16_t* table, const int32_t* ids, int64_t T, int hidden, float* h,
+                 cudaStream_t s) {
+  if (T == 0) return CLEF_OK;
+  embed_kernel<<<(unsigned)T, 128, 0, s>>>(table, ids, hidden, h);
+  return launch_status("embed");
+}
+
+int launch_head(const float* h, const float* norm_w, float eps, const SeqPack& pack, int hidden,
+                const float* head_w, int n_out, float* logits, cudaStream_t s) {
+  head_kernel<<<pack.nseq, 256, hidden * sizeof(float), s>>>(h, norm_w, eps, pack.cu_seqlens, hidden,
+                                                             head_w, n_out, logits);
+  return launch_status("head");
+}
+
+int launch_copy_rows(const void* src, int64_t ld, int64_t r0, int64_t count, int64_t ncols, int elem,
+                     void* dst, int64_t ldd, cudaStream_t s) {
+  if (count == 0) return CLEF_OK;
+  const uint8_t* sp = reinterpret_cast<const uint8_t*>(src) + r0 * ld * elem;
+  copy_rows_kernel<<<(unsigned)count, 256, 0, s>>>(sp, ld * elem, ncols * elem,
+                                                    reinterpret_cast<uint8_t*>(dst), ldd * elem);
+  return launch_status("copy_rows");
+}
+
+}  // namespace clef
+
+using namespace clef;
+
+extern "C" {
+
+int clef_rmsnorm(const float* x, const float* weight, int64_t rows, int32_t width, float eps,
+                 int32_t out_dtype, void* out, void* stream) {
+  CLEF_CHECK(x && weight && out, CLEF_ERR_INVALID, "rmsnorm: null pointer");
+  CLEF_CHECK(rows >= 0 && width > 0 && width <= 65536, CLEF_ERR_INVALID, "rmsnorm: dimensions");
+  CLEF_CHECK(out_dtype == CLEF_F32 || out_dtype == CLEF_BF16, CLEF_ERR_INVALID, "rmsnorm: dtype");
+  CLEF_CHECK(eps > 0.f && eps <= 1.f, CLEF_ERR_INVALID, "rmsnorm: epsilon");
+  CLEF_CHECK(((uintptr_t)x & 15) == 0 && ((uintptr_t)weight & 15) == 0 && ((uintptr_t)out & 15) == 0,
+             CLEF_ERR_INVALID, "rmsnorm: pointers must be 16-byte aligned");
+  return launch_rmsnorm(x, weight, rows, width, eps, out_dtype, out, as_stream(stream));
+}
+
+int clef_conv4(const float* x, int64_t ldx, const float* history, int32_t history_rows,
+               const float* weight, int64_t T, int32_t width, float* out, void* stream) {
+  CLEF_CHECK(x && weight && out, CLEF_ERR_INVALID, "conv4: null pointer");
+  CLEF_CHECK(T >= 0 && width > 0 && ldx >= width, CLEF_ERR_INVALID, "conv4: dimensions");
+  CLEF_CHECK(history_rows >= 0 && history_rows <= 3 && (history_rows == 0 || history),
+             CLEF_ERR_INVALID, "conv4: history");
+  return launch_conv4(x, ldx, history, history_rows, weight, T, width, out, as_stream(stream));
+}
+
+int clef_delta_prologue(const float* proj, int64_t ldp, int32_t a_col, int32_t b_col,
+                        const float* history, int32_t history_rows, const float* conv_weight,
+                        const float* dt_bias, const float* a_log, int64_t T, int32_t Hk, int32_t Hv,
+                        int32_t dk, int32_t dv, float* q, float* k, float* v, float* g, float* beta,
+                        void* stream) {
+  CLEF_CHECK(proj && conv_weight && dt_bias && a_log && q && k && v && g && beta, CLEF_ERR_INVALID,
+             "delta_prologue: null pointer");
+  CLEF_CHECK(dk == 128 && dv == 128, CLEF_ERR_UNSUPPORTED, "delta_prologue: dk and dv must be 128");
+  CLEF_CHECK(Hk > 0 && Hv > 0 && Hv % Hk == 0, CLEF_ERR_INVALID, "delta_prologue: head counts");
+  const int64_t width = 2LL * Hk * dk + (int64_t)Hv * dv;
+  CLEF_CHECK(width % 1024 == 0, CLEF_ERR_UNSUPPORTED,
+             "delta_prologue: q|k|v width must be a multiple of 1024");
+  CLEF_CHECK(T > 0 && T <= (1LL << 31), CLEF_ERR_INVALID, "delta_prologue: T");
+  CLEF_CHECK(ldp >= width && ldp % 4 == 0, CLEF_ERR_INVALID, "delta_prologue: ldp");
+  CLEF_CHECK(a_col >= width && a_col + Hv <= ldp && b_col >= width && b_col + Hv <= ldp,
+             CLEF_ERR_INVALID, "delta_prologue: gate columns");
+  CLEF_CHECK(history_rows >= 0 && history_rows <= 3 && (history_rows == 0 || history),
+             CLEF_ERR_INVALID, "delta_prologue: history");
+  SeqPack pack;  // one sequence: no offsets table
+  pack.nseq = 1;
+  pack.total = T;
+  return launch_delta_prologue(proj, ldp, a_col, b_col, history, history_rows, conv_weight,
+                               dt_bias, a_log, pack, Hk, Hv, dk, dv, q, k, v, g, beta,
+                               as_stream(stream));
+}
+
+int clef_compact_copy(const void* src, int32_t ndim, const int64_t* dims, const int64_t* strides,
+                      int32_t elem_size, void* dst, void* stream) {
+  CLEF_CHECK(src && dst && dims && strides, CLEF_ERR_INVALID, "compact_copy: null pointer");
+  CLEF_CHECK(ndim >= 1 && ndim <= 4, CLEF_ERR_INVALID, "compact_copy: ndim must be 1..4");
+  CLEF_CHECK(elem_size == 2 || elem_size == 4, CLEF_ERR_INVALID, "compact_copy: element size");
+  int64_t d[4] = {1, 1, 1, 1}, st[4] = {0, 0, 0, 0};
+  int64_t n = 1;
+  for (int i = 0; i < ndim; ++i) {
+    CLEF_CHECK(dims[i] >= 0 && strides[i] >= 0, CLEF_ERR_INVALID, "compact_copy: dims/strides");
+    d[4 - ndim + i] = dims[i];
+    st[4 - ndim + i] = strides[i];
+    n *= dims[i];
+  }
+  if (n == 0) return CLEF_OK;
+  const unsigned grid = (unsigned)ceil_div(n, 256);
+  cudaStream_t s = as_stream(stream);
+  if (elem_size == 4)
+    compact_copy_kernel<uint32_t><<<grid, 256, 0, s>>>(
+        (const uint32_t*)src, n, d[1], d[2], d[3], st[0], st[1], st[2], st[3], (uint32_t*)dst);
+  else
+    compact_copy_kernel<uint16_t><<<grid, 256, 0, s>>>(
+        (const uint16_t*)src, n, d[1], d[2], d[3], st[0], st[1], st[2], st[3], (uint16_t*)dst);
+  return launch_status("compact_copy");
+}
+
+}  // extern "C"

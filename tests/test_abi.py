@@ -1,0 +1,155 @@
+"""C-ABI checks that need no GPU: the library loads, exports every symbol the
+header declares, validates before launching (the reference rejects bad
+dispatch shapes before allocation, metal.rs:945-956), and implements the
+decision rule of answers() (crates/core/src/types.rs:728-802)."""
+import ctypes
+import math
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import clef_b200 as cb
+from clef_b200.config import benchmark_config
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def header_functions():
+    text = (ROOT / "include" / "clef_b200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(clef_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    declared = header_functions()
+    assert len(declared) >= 25
+    for name in declared:
+        assert hasattr(cb.lib, name), name
+    assert sorted(cb.EXPORTS) == declared
+    assert "sm_100a" in cb.version()
+
+
+def test_config_validation():
+    cfg = benchmark_config()
+    assert cb.lib.clef_config_validate(ctypes.byref(cfg)) == 0
+    bad = benchmark_config()
+    bad.linear_key_head_dim = 64
+    assert cb.lib.clef_config_validate(ctypes.byref(bad)) == 3
+    bad = benchmark_config()
+    bad.num_attention_heads = 15
+    assert cb.lib.clef_config_validate(ctypes.byref(bad)) == 1
+    assert cb.lib.clef_config_validate(None) == 1
+
+
+FAKE = ctypes.c_void_p(0x10000)  # never dereferenced: every call below fails validation first
+
+
+def test_delta_scan_rejects_before_launch():
+    L = cb.lib
+    args = dict(T=64, Hk=16, Hv=32, dk=128, dv=128)
+    # null pointers
+    assert L.clef_delta_scan(None, FAKE, FAKE, FAKE, FAKE, 64, 16, 32, 128, 128, None, 1, None, 0, 0,
+                             None, None, FAKE, FAKE, 1 << 30, None) == 1
+    # unsupported head dims (metal.rs dimensions(): key must be a power of two <= 128)
+    assert L.clef_delta_scan(FAKE, FAKE, FAKE, FAKE, FAKE, 64, 16, 32, 127, 128, None, 1, None, 0, 0,
+                             None, None, FAKE, FAKE, 1 << 30, None) == 3
+    # head counts that do not divide
+    assert L.clef_delta_scan(FAKE, FAKE, FAKE, FAKE, FAKE, 64, 3, 32, 128, 128, None, 1, None, 0, 0,
+                             None, None, FAKE, FAKE, 1 << 30, None) == 1
+    # empty sequence
+    assert L.clef_delta_scan(FAKE, FAKE, FAKE, FAKE, FAKE, 0, 16, 32, 128, 128, None, 1, None, 0, 0,
+                             None, None, FAKE, FAKE, 1 << 30, None) == 1
+    # capture without a destination
+    assert L.clef_delta_scan(FAKE, FAKE, FAKE, FAKE, FAKE, 64, 16, 32, 128, 128, None, 1, None, 0, 5,
+                             None, None, FAKE, FAKE, 1 << 30, None) == 1
+    # capture past the end
+    assert L.clef_delta_scan(FAKE, FAKE, FAKE, FAKE, FAKE, 64, 16, 32, 128, 128, None, 1, None, 0, 65,
+                             FAKE, None, FAKE, FAKE, 1 << 30, None) == 1
+    # unordered cu_seqlens
+    cu = np.array([0, 40, 30, 64], np.int64)
+    assert L.clef_delta_scan(FAKE, FAKE, FAKE, FAKE, FAKE, 64, 16, 32, 128, 128, cu.ctypes.data, 3,
+                             None, 0, 0, None, None, FAKE, FAKE, 1 << 30, None) == 1
+    # workspace too small (validated before any upload)
+    assert L.clef_delta_scan(FAKE, FAKE, FAKE, FAKE, FAKE, 64, 16, 32, 128, 128, None, 1, None, 0, 0,
+                             None, None, FAKE, ctypes.c_void_p(0x20000), 16, None) == 1
+    assert "workspace" in cb.lib.clef_last_error().decode()
+    assert args
+
+
+def test_workspace_size_grows_with_tokens():
+    a = cb.delta_scan_workspace_size(1024, 1, 32)
+    b = cb.delta_scan_workspace_size(4096, 1, 32)
+    assert 0 < a < b
+    # One (chunk, head) block holds W, U (64x128 each), P (64x64) and 3
+    # vectors; the chunk table adds 16 bytes a chunk (256-byte aligned).
+    blocks = (4096 - 1024) // 64 * 32 * (2 * 64 * 128 + 64 * 64 + 3 * 64) * 4
+    assert blocks <= b - a <= blocks + 4096
+
+
+def test_gemm_rejects_before_launch():
+    L = cb.lib
+    assert L.clef_gemm_bf16(FAKE, FAKE, 128, 256, 100, 0, FAKE, 256, None) == 3  # K % 64
+    assert L.clef_gemm_bf16(FAKE, FAKE, 128, 250, 128, 0, FAKE, 256, None) == 3  # N % 16
+    assert L.clef_gemm_bf16(FAKE, FAKE, 128, 256, 128, 7, FAKE, 256, None) == 1  # epilogue
+    assert L.clef_gemm_bf16(FAKE, FAKE, 128, 256, 128, 0, FAKE, 100, None) == 1  # ldo < N
+    assert L.clef_gemm_bf16(None, FAKE, 128, 256, 128, 0, FAKE, 256, None) == 1
+    assert L.clef_gemm_swiglu(FAKE, FAKE, None, 128, 256, 128, FAKE, None) == 1
+
+
+def test_attention_and_pointwise_reject_before_launch():
+    L = cb.lib
+    assert L.clef_attention_gqa(FAKE, FAKE, FAKE, 16, 4, 10, 10, 128, FAKE, None) == 3
+    assert L.clef_attention_gqa(FAKE, FAKE, FAKE, 16, 5, 10, 10, 256, FAKE, None) == 1
+    assert L.clef_attention_gqa(FAKE, FAKE, FAKE, 16, 4, 11, 10, 256, FAKE, None) == 1
+    assert L.clef_rmsnorm(FAKE, FAKE, 4, 256, 0.0, 0, FAKE, None) == 1
+    assert L.clef_rmsnorm(FAKE, FAKE, 4, 256, 1e-6, 5, FAKE, None) == 1
+    assert L.clef_conv4(FAKE, 8, None, 2, FAKE, 4, 8, FAKE, None) == 1  # history rows without data
+    assert L.clef_delta_prologue(FAKE, 12352, 12288, 12320, None, 0, FAKE, FAKE, FAKE, 8, 16, 32, 64,
+                                 128, FAKE, FAKE, FAKE, FAKE, FAKE, None) == 3
+    assert L.clef_compact_copy(FAKE, 5, FAKE, FAKE, 4, FAKE, None) == 1
+
+
+def test_engine_reports_missing_device_or_bad_config():
+    cfg = benchmark_config()
+    cfg.linear_conv_kernel_dim = 3
+    h = ctypes.c_void_p()
+    assert cb.lib.clef_engine_create(ctypes.byref(cfg), 0, ctypes.byref(h)) == 3
+    assert not h.value
+
+
+def answers_reference(logits):
+    """answers() restated: softmax with max subtraction, first strict max wins."""
+    out = []
+    for l in np.asarray(logits, np.float32).reshape(-1, 7):
+        def softmax(x):
+            m = np.float32(max(x))
+            p = [np.float32(math.exp(np.float32(v - m))) for v in x]
+            s = np.float32(sum(p))
+            return [np.float32(v / s) for v in p]
+        pn, pc = softmax(l[:2]), softmax(l[2:6])
+        best, win = -1.0, -1
+        for i, p in enumerate(pc):
+            if p > best:
+                best, win = p, i
+        out.append((pn[0], win, best, l[6]))
+    return out
+
+
+def test_decide_matches_answers_rule():
+    rng = np.random.default_rng(0)
+    lg = rng.standard_normal((64, 7)).astype(np.float32)
+    lg[5, 2:6] = [1.0, 3.0, 3.0, 0.5]   # tie: the first maximum wins
+    lg[6, 2:6] = [2.0, 2.0, 2.0, 2.0]
+    got = cb.decide(lg)
+    ref = answers_reference(lg)
+    for d, (noul, win, conf, score) in zip(got, ref):
+        assert d.choice == win
+        assert abs(d.noul - noul) < 1e-6 and abs(d.confidence - conf) < 1e-6
+        assert d.score == score
+    assert got[5].choice == 1 and got[6].choice == 0
+    bad = lg.copy()
+    bad[0, 0] = np.inf
+    with pytest.raises(cb.ClefError):
+        cb.decide(bad)

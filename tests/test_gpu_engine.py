@@ -1,0 +1,122 @@
+"""End-to-end prefill on the B200 against the CPU F32 oracle.
+
+The engine draws its seeded BF16 weights on the device; the oracle receives
+exactly those values (exported through clef_engine_get_weight) and runs the
+reference's F32 path. Geometry: the benchmark dimensions (hidden 2560,
+16/32 DeltaNet heads of 128, 16/4 attention heads of 256, intermediate 9216)
+with one [3 x DeltaNet + 1 x attention] block group; a reduced vocabulary
+keeps the oracle's embedding table small (the gather does not depend on it).
+
+Tolerances: final hidden states max-abs <= 5e-2 and relative RMS <= 2e-2
+(BF16 projections vs F32 everywhere); schema-head logits max-abs <= 2e-2
+(the north star's stated bound). Packing requests together is bit-exact.
+"""
+import numpy as np
+import pytest
+
+import oracle
+from clef_b200.config import benchmark_config
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def models():
+    import clef_b200 as cb
+    cfg = benchmark_config(layers=4, head_outputs=7)
+    cfg.vocab_size = 4096
+    eng = cb.Engine(cfg, 0)
+    eng.init_random(2, 0.02)
+    eng.finalize()
+    ref = oracle.Model(cfg)
+    for name in ref.names():
+        ref.set_weight(name, eng.get_weight(name))
+    ref.check()
+    yield cfg, eng, ref
+    eng.close()
+
+
+def ids(n, seed):
+    return np.random.default_rng(seed).integers(0, 4096, n).astype(np.int32)
+
+
+def test_block_group_matches_oracle(models):
+    cfg, eng, ref = models
+    seq = ids(300, 1)
+    lg, hid, _ = eng.prefill([seq], hidden=True)
+    rh, _ = ref.prefill(seq)
+    head_w = eng.get_weight("clef.head.weight").reshape(7, cfg.hidden_size)
+    rl = oracle.head(rh[-1], head_w)
+    err_h = np.abs(hid - rh).max()
+    rel = np.sqrt(((hid - rh) ** 2).mean() / (rh ** 2).mean())
+    err_l = np.abs(lg[0] - rl).max()
+    print(f"hidden max-abs {err_h:.3e} rel-rms {rel:.3e} logits max-abs {err_l:.3e}")
+    assert np.isfinite(hid).all()
+    assert rel <= 2e-2 and err_h <= 5e-2
+    assert err_l <= 2e-2
+
+
+def test_packed_batch_is_bit_exact(models):
+    cfg, eng, _ = models
+    seqs = [ids(n, 10 + n) for n in (1, 64, 65, 300, 129)]
+    lg, _, _ = eng.prefill(seqs)
+    for i, s in enumerate(seqs):
+        single, _, _ = eng.prefill([s])
+        assert np.array_equal(lg[i], single[0]), i
+
+
+@pytest.mark.parametrize("boundary", [1, 3, 100, 200])
+def test_prefix_capture_and_resume(models, boundary):
+    cfg, eng, ref = models
+    seq = ids(200 + 57, 3)
+    full_lg, full_h, _ = eng.prefill([seq], hidden=True)
+    cap_lg, cap_h, prefix = eng.prefill([seq], capture=boundary, hidden=True)
+    assert np.array_equal(cap_h, full_h)
+    assert prefix.tokens == boundary
+    lg, hid, _ = eng.prefill([seq[boundary:]], initial=prefix, hidden=True)
+    assert hid.shape == full_h.shape
+    assert np.array_equal(hid[:boundary], full_h[:boundary])
+    err = np.abs(hid - full_h).max()
+    print(f"resume at {boundary}: hidden max-abs vs full {err:.3e}")
+    assert err <= 2e-2
+    assert np.abs(lg - full_lg).max() <= 2e-2
+    # The oracle's resume on the same weights agrees too.
+    _, rstate = ref.prefill(seq, capture=boundary) if boundary < len(seq) else (None, None)
+    rh, _ = ref.prefill(seq[boundary:], initial=rstate)
+    assert np.abs(hid - rh).max() <= 5e-2
+    # Many suffixes continue from one shared prefix.
+    tails = [ids(n, 40 + n) for n in (5, 80)]
+    lgs, _, _ = eng.prefill(tails, initial=prefix)
+    for i, t in enumerate(tails):
+        one, _, _ = eng.prefill([t], initial=prefix)
+        assert np.array_equal(lgs[i], one[0])
+    prefix.close()
+
+
+def test_decisions_match_oracle(models):
+    import clef_b200 as cb
+    cfg, eng, ref = models
+    head_w = eng.get_weight("clef.head.weight").reshape(7, cfg.hidden_size)
+    seqs = [ids(n, 100 + n) for n in (40, 90, 150)]
+    lg, _, _ = eng.prefill(seqs)
+    ref_lg = np.stack([oracle.head(ref.prefill(s)[0][-1], head_w) for s in seqs])
+    got, want = cb.decide(lg), cb.decide(ref_lg)
+    for i, (a, b) in enumerate(zip(got, want)):
+        margin = np.sort(ref_lg[i, 2:6])[-1] - np.sort(ref_lg[i, 2:6])[-2]
+        if margin > 2 * 2e-2:
+            assert a.choice == b.choice, (i, margin)
+        assert abs(a.noul - b.noul) <= 1e-2
+
+
+def test_cancel_between_layers(models):
+    import clef_b200 as cb
+    cfg, eng, _ = models
+    eng.cancel(True)
+    with pytest.raises(cb.ClefError) as e:
+        eng.prefill([ids(10, 5)])
+    assert e.value.code == 5
+    eng.cancel(False)
+    lg, _, _ = eng.prefill([ids(10, 5)])
+    assert np.isfinite(lg).all()

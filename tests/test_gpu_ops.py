@@ -1,0 +1,165 @@
+"""Operator parity on the B200: RMSNorm, conv, DeltaNet prologue against the
+oracle; the tcgen05 GEMM family against an F32 matmul of the same BF16
+operands; attention against the oracle's tiled F32 attention.
+
+Tolerances (stated per test): conv is bit-exact (same rounding order as the
+reference, pointwise.rs:330-358); RMSNorm 1e-6 relative (pointwise.rs:430-466);
+GEMM F32 outputs 2e-5 relative to max |y| (summation order only), BF16
+outputs 1 BF16 ulp (2^-8 relative); attention 5e-3 max-abs (probabilities are
+rounded to BF16 before the PV product).
+"""
+import numpy as np
+import pytest
+
+import oracle
+from clef_b200 import workloads
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def bf16_round(a):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).bfloat16().float().numpy()
+
+
+@pytest.mark.parametrize("rows,width", [(1, 2560), (37, 2560), (300, 256), (64, 128)])
+def test_rmsnorm(rows, width):
+    import clef_b200 as cb
+    rng = np.random.default_rng(rows)
+    x = rng.standard_normal((rows, width)).astype(np.float32) * 3
+    w = (1 + 0.02 * rng.standard_normal(width)).astype(np.float32)
+    ref = oracle.rms(x, w)
+    out = cb.rmsnorm(dev(x), dev(w)).cpu().numpy()
+    assert np.abs(out - ref).max() <= 1e-6 * np.abs(ref).max() + 1e-7
+    ob = cb.rmsnorm(dev(x), dev(w), out_dtype=cb.BF16).float().cpu().numpy()
+    assert np.array_equal(ob, bf16_round(out))
+
+
+@pytest.mark.parametrize("T,hist", [(1, 0), (5, 0), (70, 0), (5, 3), (2, 2)])
+def test_conv4_bit_exact(T, hist):
+    import clef_b200 as cb
+    rng = np.random.default_rng(T + hist)
+    width = 256
+    x = rng.standard_normal((T, width)).astype(np.float32)
+    h = rng.standard_normal((hist, width)).astype(np.float32)
+    w = (0.3 * rng.standard_normal((width, 4))).astype(np.float32)
+    ref = oracle.conv4(np.concatenate([h, x]), w)[hist:]
+    out = cb.conv4(dev(x), dev(w), history=dev(h) if hist else None).cpu().numpy()
+    assert np.array_equal(out, ref)
+
+
+def test_delta_prologue_matches_reference_steps():
+    import clef_b200 as cb
+    T, Hk, Hv = 37, 16, 32
+    key, value = Hk * 128, Hv * 128
+    width = 2 * key + value
+    ldp = width + value + 2 * Hv
+    rng = np.random.default_rng(4)
+    proj = rng.standard_normal((T, ldp)).astype(np.float32)
+    conv_w = (0.3 * rng.standard_normal((width, 4))).astype(np.float32)
+    dt = (0.1 * rng.standard_normal(Hv)).astype(np.float32)
+    alog = rng.uniform(0, np.log(16), Hv).astype(np.float32)
+    hist = rng.standard_normal((3, width)).astype(np.float32)
+    q, k, v, g, beta = [t.cpu().numpy() for t in cb.delta_prologue(
+        dev(proj), width + value, width + value + Hv, dev(conv_w), dev(dt), dev(alog), Hk, Hv,
+        history=dev(hist))]
+    conv = oracle.conv4(np.concatenate([hist, proj[:, :width]]), conv_w)[3:]
+    mixed = conv / (1 + np.exp(-conv))
+    qs, ks = workloads.scan_operands({"q": mixed[:, :key].reshape(T, Hk, 128),
+                                      "k": mixed[:, key:2 * key].reshape(T, Hk, 128)})
+    a = proj[:, width + value:width + value + Hv] + dt
+    gref = workloads.softplus(a) * -np.exp(alog)
+    bref = 1 / (1 + np.exp(-proj[:, width + value + Hv:width + value + 2 * Hv]))
+    assert np.abs(q - qs).max() <= 1e-6
+    assert np.abs(k - ks).max() <= 1e-6
+    assert np.abs(v - mixed[:, 2 * key:].reshape(T, Hv, 128)).max() <= 1e-6
+    assert np.abs(g - gref).max() <= 1e-5 * np.abs(gref).max()
+    assert np.abs(beta - bref).max() <= 1e-6
+
+
+def gemm_case(M, N, K, seed):
+    rng = np.random.default_rng(seed)
+    x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).cuda().bfloat16()
+    w = torch.from_numpy((0.02 * rng.standard_normal((N, K))).astype(np.float32)).cuda().bfloat16()
+    ref = x.float() @ w.float().T
+    return x, w, ref
+
+
+@pytest.mark.parametrize("M", [512, 2048, 8192])
+@pytest.mark.parametrize("shape", ["gate_up", "down", "qkv", "qkv_gate"])
+def test_gemm_config2_sweep(M, shape):
+    import clef_b200 as cb
+    N, K = workloads.GEMM_SHAPES[shape]
+    x, w, ref = gemm_case(M, N, K, 1)
+    y = cb.gemm(x, w, epilogue=cb.EPI_F32)
+    scale = ref.abs().max().item()
+    err = (y - ref).abs().max().item()
+    print(f"M={M} {shape}: rel {err / scale:.2e}")
+    assert err <= 2e-5 * scale
+    yb = cb.gemm(x, w, epilogue=cb.EPI_BF16).float()
+    assert ((yb - ref).abs() <= ref.abs() * 2 ** -8 + 1e-6 * scale).all()
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 256, 64), (127, 272, 128), (129, 1040, 2560), (1000, 32, 256),
+                                   (300, 12352, 2560)])
+def test_gemm_ragged_shapes(M, N, K):
+    import clef_b200 as cb
+    x, w, ref = gemm_case(M, N, K, M + N)
+    y = cb.gemm(x, w, epilogue=cb.EPI_F32)
+    assert (y - ref).abs().max().item() <= 2e-5 * ref.abs().max().item() + 1e-6
+
+
+def test_gemm_residual_add():
+    import clef_b200 as cb
+    x, w, ref = gemm_case(333, 2560, 4096, 7)
+    h = torch.randn(333, 2560, device="cuda")
+    h0 = h.clone()
+    cb.gemm(x, w, epilogue=cb.EPI_ADD_F32, out=h)
+    assert (h - (h0 + ref)).abs().max().item() <= 2e-5 * ref.abs().max().item() + 1e-6
+
+
+@pytest.mark.parametrize("M", [64, 700])
+def test_gemm_swiglu(M):
+    import clef_b200 as cb
+    rng = np.random.default_rng(M)
+    K, N = 2560, 9216
+    x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).cuda().bfloat16()
+    wg = torch.from_numpy((0.02 * rng.standard_normal((N, K))).astype(np.float32)).cuda().bfloat16()
+    wu = torch.from_numpy((0.02 * rng.standard_normal((N, K))).astype(np.float32)).cuda().bfloat16()
+    ref = torch.nn.functional.silu(x.float() @ wg.float().T) * (x.float() @ wu.float().T)
+    y = cb.gemm_swiglu(x, wg, wu).float()
+    scale = ref.abs().max().item()
+    assert ((y - ref).abs() <= ref.abs() * 2 ** -8 + 1e-5 * scale).all()
+
+
+@pytest.mark.parametrize("Hq,Hkv,Tq,prefix", [(2, 1, 1, 0), (2, 1, 17, 0), (16, 4, 64, 0),
+                                              (16, 4, 257, 0), (2, 1, 1, 256), (2, 1, 17, 256),
+                                              (16, 4, 257, 256), (4, 1, 1000, 37)])
+def test_attention_gqa(Hq, Hkv, Tq, prefix):
+    import clef_b200 as cb
+    d = 256
+    Tk = Tq + prefix
+    q = bf16_round(np.sin(np.arange(Hq * Tq * d, dtype=np.float32) * np.float32(0.017)).reshape(Hq, Tq, d))
+    k = bf16_round(np.cos(np.arange(Hkv * Tk * d, dtype=np.float32) * np.float32(0.031)).reshape(Hkv, Tk, d))
+    rng = np.random.default_rng(Tq)
+    v = bf16_round(rng.standard_normal((Hkv, Tk, d)).astype(np.float32))
+    ref = oracle.attention(q, k, v, causal=True)
+    out = cb.attention_gqa(dev(q).bfloat16(), dev(k).bfloat16(), dev(v).bfloat16()).cpu().numpy()
+    err = np.abs(out - ref).max()
+    print(f"attention {Hq}/{Hkv} Tq={Tq} prefix={prefix}: {err:.3e}")
+    assert err <= 5e-3
+
+
+def test_compact_copy_of_strided_view():
+    import clef_b200 as cb
+    src = torch.arange(4 * 8 * 128, dtype=torch.float32, device="cuda").reshape(4, 8, 128)
+    view = src[:, 1:4, :]
+    out = cb.compact_copy(view)
+    assert torch.equal(out, view.contiguous())
+    half = src.to(torch.bfloat16)[:, 2:7, :].transpose(0, 1)
+    assert torch.equal(cb.compact_copy(half), half.contiguous())

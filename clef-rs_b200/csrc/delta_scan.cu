@@ -1,27 +1,36 @@
-// delta_scan.cu — chunked gated-DeltaNet scan (chunk C = 64, dk = dv = 128).
+// delta_scan.cu — chunked gated-DeltaNet scan on the tensor cores
+// (chunk C = 64, dk = dv = 128).
 //
 // The reference recurrence, per v-head (delta_recurrence_prefill,
 // crates/core/src/models/qwen.rs:867-880; clef_delta, delta.metal:62-130):
 //   S <- S e^{g_t};  d_t = (v_t - S^T k_t) beta_t;  S <- S + k_t d_t^T;  o_t = S^T q_t
 // is evaluated a chunk at a time in the WY / UT form that the reference states
-// in its chunkwise candidate (chunk.rs:16-149, chunk.metal:10-164):
-//   G_i   = sum_{s<=i} g_s (chunk-relative, accumulated in FP64)
-//   A_ij  = beta_i e^{G_i-G_j} k_i.k_j           (j < i)
-//   W     = (I + A)^{-1} diag(beta e^G) K,   U = (I + A)^{-1} diag(beta) V
-//   D     = U - W S_prev                          (the chunk's delta rows)
-//   O     = diag(e^G) Q S_prev + (M o Q K^T) D,   M_ij = e^{G_i-G_j} (j <= i)
-//   S_new = e^{G_last} S_prev + (diag(e^{G_last-G}) K)^T D
+// in its chunkwise candidate (chunk.rs:16-149, chunk.metal:10-164). With
+//   G_i  = sum_{s<=i} g_s (chunk-relative, accumulated in FP64),
+//   A_ij = beta_i e^{G_i-G_j} k_i.k_j (j < i),   T = (I + A)^{-1},
+//   P_ij = e^{G_i-G_j} q_i.k_j (j <= i),
+// and the state kept transposed (S^T, rows = value columns):
+//   R^T  = V^T - (S^T K^T) diag(e^G)                 residual of the old state
+//   D^T  = R^T (T diag(beta))^T                       the chunk's delta rows
+//   O^T  = (S^T Q^T) diag(e^G) + D^T P^T
+//   S^T <- e^{G_last} S^T + (D^T diag(e^{G_last-G})) K
 // Every decay factor is the exponential of a non-positive difference of
-// chunk-relative cumulative log-decays, so nothing is divided by an
-// underflowed prefix product (a per-token decay of -1000 is exact).
+// chunk-relative cumulative log-decays, so nothing divides by an underflowed
+// prefix product (a per-token decay of -1000 is exact).
 //
-// Phase 1 (delta_chunk_prep): one CTA per (chunk, v-head), all in parallel:
-//   Gram matrices, the unit-lower-triangular solve by forward substitution
-//   (each thread owns one of the 256 right-hand-side columns of [W | U] in
-//   registers), and the decay vectors; results go to the workspace.
-// Phase 2 (delta_chunk_carry): one CTA per (sequence, v-head, 16-column
-//   slice of dv); walks the sequence's chunks in order carrying its
-//   128 x 16 slice of S in shared memory.
+// One CTA per (sequence, v-head), 8 warps; warp w owns value rows
+// [16w, 16w+16) of S^T as 64 F32 mma accumulators in registers for the whole
+// sequence. The accumulators are re-packed in registers as the A operand of the
+// next product (the C-fragment -> A-fragment identity of m16n8k16), so S never
+// leaves the SM between chunks. Products use BF16 mma.sync with F32
+// accumulation and a two-term BF16 split of both operands
+// (x = hi + lo; x*y ~ hi*hi + hi*lo + lo*hi), which keeps ~16 mantissa bits:
+// the result tracks the F32 per-token recurrence to ~1e-5.
+// The triangular inverse T is computed in F32 by blocked forward substitution
+// (four 16 x 16 diagonal blocks, then the off-diagonal blocks).
+// A capture point inside a chunk does not change the chunking: the state at
+// the capture token is formed from the same chunk quantities, so a prefill with
+// capture is bit-identical to one without.
 #include <vector>
 
 #include "kernels.cuh"
@@ -30,348 +39,530 @@ namespace clef {
 
 namespace {
 
-constexpr int C = 64;        // chunk length
-constexpr int DK = 128;      // key dim
-constexpr int DV = 128;      // value dim
-constexpr int DVS = 16;      // value columns per carry CTA
-constexpr int SLICES = DV / DVS;
+constexpr int C = 64;    // chunk length
+constexpr int DK = 128;  // key dim
+constexpr int DV = 128;  // value dim
+constexpr int WARPS = 8;
+constexpr int THREADS = WARPS * 32;
 
-struct ScanSeq {
-  int32_t chunk0;
-  int32_t nchunks;
-  int32_t capture_chunk;  // relative index of the chunk that ends at the capture point, -1 none
-  int32_t pad;
-};
-struct ScanChunk {
-  int64_t t0;
-  int32_t n;
-  int32_t seq;
-};
+// ---- shared-memory layout (bytes) -------------------------------------------
+constexpr int KQ_BYTES = C * DK * 2;   // one [64][128] BF16 tile (16 KB)
+constexpr int SQ_BYTES = C * C * 2;    // one [64][64] BF16 tile (8 KB)
+constexpr int OFF_KHI = 0;
+constexpr int OFF_KLO = OFF_KHI + KQ_BYTES;
+constexpr int OFF_QHI = OFF_KLO + KQ_BYTES;
+constexpr int OFF_QLO = OFF_QHI + KQ_BYTES;
+constexpr int OFF_PHI = OFF_QLO + KQ_BYTES;
+constexpr int OFF_PLO = OFF_PHI + SQ_BYTES;
+constexpr int OFF_THI = OFF_PLO + SQ_BYTES;
+constexpr int OFF_TLO = OFF_THI + SQ_BYTES;
+constexpr int AP = 65;                               // F32 pitch of A and T
+constexpr int OFF_A = OFF_TLO + SQ_BYTES;            // F32 [64][65]
+constexpr int OFF_T = OFF_A + C * AP * 4;            // F32 [64][65]
+constexpr int OFF_M = OFF_T + C * AP * 4;            // F32 [3][16][17] scratch
+constexpr int OFF_G = OFF_M + 3 * 16 * 17 * 4;       // double [64]
+constexpr int OFF_EG = OFF_G + C * 8;                // F32 [64] e^{G}
+constexpr int OFF_EGD = OFF_EG + C * 4;              // F32 [64] e^{G_last - G}
+constexpr int OFF_BETA = OFF_EGD + C * 4;            // F32 [64]
+constexpr int OFF_ECAP = OFF_BETA + C * 4;           // F32 [64] e^{G_c - G} (capture)
+constexpr int SMEM = OFF_ECAP + C * 4 + 16;
 
-// Per (chunk, head) block in the workspace (floats).
-constexpr int64_t kW = 0;                 // [C][DK]
-constexpr int64_t kU = kW + C * DK;       // [C][DV]
-constexpr int64_t kP = kU + C * DV;       // [C][C] lower (incl. diagonal) M o QK^T
-constexpr int64_t kEG = kP + C * C;       // [C] e^{G_i}
-constexpr int64_t kEGD = kEG + C;         // [C] e^{G_last - G_i}
-constexpr int64_t kEGL = kEGD + C;        // [C] e^{G_last} in slot 0
-constexpr int64_t kBlock = kEGL + C;
-
-size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
-
-struct Layout {
-  size_t seq_off, chunk_off, data_off, total;
-  int64_t max_chunks;
-};
-
-Layout layout(int64_t total_tokens, int nseq, int Hv) {
-  Layout l;
-  l.max_chunks = ceil_div(total_tokens, C) + nseq + 1;
-  l.seq_off = 0;
-  l.chunk_off = align256(sizeof(ScanSeq) * (size_t)nseq);
-  l.data_off = align256(l.chunk_off + sizeof(ScanChunk) * (size_t)l.max_chunks);
-  l.total = l.data_off + sizeof(float) * (size_t)kBlock * (size_t)l.max_chunks * (size_t)Hv;
-  return l;
+// Byte offset of element (row, col) in a BF16 tile whose rows hold `cpr`
+// 16-byte chunks; the chunk index is XOR-swizzled with row & 7 so that the
+// eight rows an ldmatrix phase reads hit distinct banks.
+__device__ __forceinline__ uint32_t swz(int row, int col, int cpr) {
+  return (uint32_t)(row * cpr * 16 + ((((col >> 3) ^ (row & 7))) << 4) + ((col & 7) << 1));
 }
 
-// ---------------------------------------------------------------------------
-// Phase 1.
-// ---------------------------------------------------------------------------
-constexpr int KP = 129;  // Gram-stage pitch (conflict-free row-strided reads)
-constexpr int AP = 68;   // A pitch (16-byte aligned rows for float4 broadcasts)
-
-__global__ void __launch_bounds__(256) delta_chunk_prep(
-    const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
-    const float* __restrict__ g, const float* __restrict__ beta,
-    const ScanChunk* __restrict__ chunks, int Hk, int Hv, float* __restrict__ data) {
-  extern __shared__ __align__(16) float sm[];
-  float* Ks = sm;                       // [C][KP]
-  float* Qs = Ks + C * KP;              // [C][KP]
-  float* As = Qs + C * KP;              // [C][AP]
-  float* bs = As + C * AP;              // [C] beta
-  float* egs = bs + C;                  // [C] e^{G}
-  double* Gs = reinterpret_cast<double*>(egs + C);  // [C]
-
-  const int tid = threadIdx.x;
-  const int h = blockIdx.y;
-  const ScanChunk ch = chunks[blockIdx.x];
-  const int n = ch.n;
-  const int kh = h / (Hv / Hk);
-  float* blk = data + ((int64_t)blockIdx.x * Hv + h) * kBlock;
-
-  // Load K, Q rows of the chunk (zero rows past n).
-  for (int idx = tid; idx < C * (DK / 4); idx += 256) {
-    const int i = idx / (DK / 4), c4 = (idx % (DK / 4)) * 4;
-    float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), qv = kv;
-    if (i < n) {
-      const int64_t off = ((ch.t0 + i) * Hk + kh) * DK + c4;
-      kv = *reinterpret_cast<const float4*>(k + off);
-      qv = *reinterpret_cast<const float4*>(q + off);
-    }
-    float* kr = Ks + i * KP + c4;
-    float* qr = Qs + i * KP + c4;
-    kr[0] = kv.x; kr[1] = kv.y; kr[2] = kv.z; kr[3] = kv.w;
-    qr[0] = qv.x; qr[1] = qv.y; qr[2] = qv.z; qr[3] = qv.w;
-  }
-  // Chunk-relative inclusive cumsum of g in FP64 (warp 0, two tokens a lane).
-  if (tid < 32) {
-    const int i0 = 2 * tid, i1 = 2 * tid + 1;
-    const double g0 = i0 < n ? (double)g[(ch.t0 + i0) * Hv + h] : 0.0;
-    const double g1 = i1 < n ? (double)g[(ch.t0 + i1) * Hv + h] : 0.0;
-    double pair = g0 + g1, run = pair;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const double up = __shfl_up_sync(0xffffffffu, run, o);
-      if (tid >= o) run += up;
-    }
-    const double excl = run - pair;
-    Gs[i0] = excl + g0;
-    Gs[i1] = excl + g0 + g1;
-    bs[i0] = i0 < n ? beta[(ch.t0 + i0) * Hv + h] : 0.f;
-    bs[i1] = i1 < n ? beta[(ch.t0 + i1) * Hv + h] : 0.f;
-  }
-  __syncthreads();
-  const double Glast = Gs[n - 1];
-  if (tid < C) {
-    const float eg = tid < n ? expf((float)Gs[tid]) : 0.f;
-    egs[tid] = eg;
-    blk[kEG + tid] = eg;
-    blk[kEGD + tid] = tid < n ? expf((float)(Glast - Gs[tid])) : 0.f;
-    blk[kEGL + tid] = tid == 0 ? expf((float)Glast) : 0.f;
-  }
-
-  // A (strictly lower) and P = M o QK^T (lower incl. diagonal): each thread a
-  // 4 x 4 block, rows ti*4 + a, columns tj + 16 b.
-  {
-    const int ti = tid >> 4, tj = tid & 15;
-    float akk[4][4], aqk[4][4];
-#pragma unroll
-    for (int a = 0; a < 4; ++a)
-#pragma unroll
-      for (int b = 0; b < 4; ++b) akk[a][b] = aqk[a][b] = 0.f;
-#pragma unroll 4
-    for (int kk = 0; kk < DK; ++kk) {
-      float ki[4], qi[4], kj[4];
-#pragma unroll
-      for (int a = 0; a < 4; ++a) {
-        ki[a] = Ks[(ti * 4 + a) * KP + kk];
-        qi[a] = Qs[(ti * 4 + a) * KP + kk];
-      }
-#pragma unroll
-      for (int b = 0; b < 4; ++b) kj[b] = Ks[(tj + 16 * b) * KP + kk];
-#pragma unroll
-      for (int a = 0; a < 4; ++a)
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          akk[a][b] = fmaf(ki[a], kj[b], akk[a][b]);
-          aqk[a][b] = fmaf(qi[a], kj[b], aqk[a][b]);
-        }
-    }
-#pragma unroll
-    for (int a = 0; a < 4; ++a) {
-      const int i = ti * 4 + a;
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const int j = tj + 16 * b;
-        const bool valid = i < n && j <= i;
-        const float decay = valid ? expf((float)(Gs[i] - Gs[j])) : 0.f;
-        As[i * AP + j] = (valid && j < i) ? bs[i] * (decay * akk[a][b]) : 0.f;
-        blk[kP + i * C + j] = valid ? decay * aqk[a][b] : 0.f;
-      }
-    }
-  }
-  __syncthreads();
-
-  // Forward substitution (I + A) X = B for the 256 columns of [W | U].
-  {
-    const int c = tid;
-    float x[C];
-    if (c < DK) {
-#pragma unroll
-      for (int i = 0; i < C; ++i) x[i] = bs[i] * (egs[i] * Ks[i * KP + c]);
-    } else {
-      const int cv = c - DK;
-#pragma unroll
-      for (int i = 0; i < C; ++i)
-        x[i] = i < n ? bs[i] * v[((ch.t0 + i) * Hv + h) * DV + cv] : 0.f;
-    }
-#pragma unroll
-    for (int i = 1; i < C; ++i) {
-      const float* arow = As + i * AP;
-      float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-#pragma unroll
-      for (int j4 = 0; j4 < i; j4 += 4) {
-        const float4 a4 = *reinterpret_cast<const float4*>(arow + j4);
-        s0 = fmaf(a4.x, x[j4], s0);
-        if (j4 + 1 < i) s1 = fmaf(a4.y, x[j4 + 1], s1);
-        if (j4 + 2 < i) s2 = fmaf(a4.z, x[j4 + 2], s2);
-        if (j4 + 3 < i) s3 = fmaf(a4.w, x[j4 + 3], s3);
-      }
-      x[i] = x[i] - ((s0 + s1) + (s2 + s3));
-    }
-    float* dst = blk + (c < DK ? kW + c : kU + (c - DK));
-#pragma unroll
-    for (int i = 0; i < C; ++i) dst[i * DK] = x[i];
-  }
+__device__ __forceinline__ void split(float x, __nv_bfloat16& hi, __nv_bfloat16& lo) {
+  hi = __float2bfloat16_rn(x);
+  lo = __float2bfloat16_rn(x - __bfloat162float(hi));
+}
+__device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  __nv_bfloat16 h0, l0, h1, l1;
+  split(x0, h0, l0);
+  split(x1, h1, l1);
+  hi = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+  lo = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
 }
 
-// ---------------------------------------------------------------------------
-// Phase 2.
-// ---------------------------------------------------------------------------
-constexpr int WP = 132;  // row pitch of W / Q / K tiles (float4-aligned, conflict-free)
-constexpr int PP = 68;
+__device__ __forceinline__ void ldsm4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm4t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// c += a * b with both operands split: hi*hi + hi*lo + lo*hi.
+__device__ __forceinline__ void mma3(float (&c)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4],
+                                     uint32_t bh0, uint32_t bh1, uint32_t bl0, uint32_t bl1) {
+  mma(c, al, bh0, bh1);
+  mma(c, ah, bl0, bl1);
+  mma(c, ah, bh0, bh1);
+}
 
-__global__ void __launch_bounds__(256) delta_chunk_carry(
-    const float* __restrict__ q, const float* __restrict__ k, const ScanSeq* __restrict__ seqs,
-    const ScanChunk* __restrict__ chunks, const float* __restrict__ data, int Hk, int Hv,
-    const float* __restrict__ init, int init_shared, float* __restrict__ capture_state,
-    float* __restrict__ final_state, float* __restrict__ out) {
-  extern __shared__ __align__(16) float sm[];
-  float* Ws = sm;                 // [C][WP]
-  float* Qs = Ws + C * WP;        // [C][WP]
-  float* Ks = Qs + C * WP;        // [C][WP]
-  float* Ps = Ks + C * WP;        // [C][PP]
-  float* Ss = Ps + C * PP;        // [DK][DVS]
-  float* Ds = Ss + DK * DVS;      // [C][DVS]
-  float* Us = Ds + C * DVS;       // [C][DVS]
-  float* eg = Us + C * DVS;       // [C]
-  float* egd = eg + C;            // [C]
-  float* egl = egd + C;           // [4]
+// A fragments (k-step of 16) from two accumulator n-tiles of a 16-row block.
+__device__ __forceinline__ void acc_to_a(const float (&c0)[4], const float (&c1)[4], uint32_t (&ah)[4],
+                                         uint32_t (&al)[4]) {
+  split2(c0[0], c0[1], ah[0], al[0]);
+  split2(c0[2], c0[3], ah[1], al[1]);
+  split2(c1[0], c1[1], ah[2], al[2]);
+  split2(c1[2], c1[3], ah[3], al[3]);
+}
 
-  const int tid = threadIdx.x;
-  const int slice = blockIdx.x % SLICES;
-  const int h = (blockIdx.x / SLICES) % Hv;
-  const int s = blockIdx.x / (SLICES * Hv);
-  const int kh = h / (Hv / Hk);
-  const int c0 = slice * DVS;
-  const ScanSeq sq = seqs[s];
+// B fragments for two n-tiles (rows n0..n0+15 of a row-major [n][k] tile) at
+// k-step k0: out[0..1] = n-tile n0, out[2..3] = n-tile n0+8.
+__device__ __forceinline__ void ldb_nk(uint32_t base, int n0, int k0, int cpr, int lane,
+                                       uint32_t (&r)[4]) {
+  const int row = n0 + (lane & 7) + ((lane >> 4) << 3);
+  const int col = k0 + ((lane >> 3) & 1) * 8;
+  ldsm4(base + swz(row, col, cpr), r);
+}
+// B fragments from a row-major [k][n] tile (transposed load): n-tiles n0 and
+// n0+8 at k-step k0.
+__device__ __forceinline__ void ldb_kn(uint32_t base, int n0, int k0, int cpr, int lane,
+                                       uint32_t (&r)[4]) {
+  const int row = k0 + (lane & 7) + (((lane >> 3) & 1) << 3);
+  const int col = n0 + ((lane >> 4) << 3);
+  ldsm4t(base + swz(row, col, cpr), r);
+}
+// A fragments from a row-major [m][k] tile: rows m0..m0+15 at k-step k0.
+__device__ __forceinline__ void lda(uint32_t base, int m0, int k0, int cpr, int lane, uint32_t (&r)[4]) {
+  ldsm4(base + swz(m0 + (lane & 15), k0 + (lane >> 4) * 8, cpr), r);
+}
 
-  // Initial state slice.
-  for (int idx = tid; idx < DK * DVS; idx += 256) {
-    const int kk = idx / DVS, c = idx % DVS;
-    float v0 = 0.f;
-    if (init) {
-      const int64_t base = init_shared ? 0 : (int64_t)s * Hv * DK * DV;
-      v0 = init[base + ((int64_t)h * DK + kk) * DV + c0 + c];
+struct ScanArgs {
+  const float* q;  // [T, Hk, 128] normalised, scaled
+  const float* k;  // [T, Hk, 128] normalised
+  const float* v;  // [T, Hv, 128]
+  const float* g;  // [T, Hv]
+  const float* beta;
+  const int64_t* cu;  // device [nseq + 1] or null (one sequence of T)
+  int64_t T;
+  int Hk, Hv;
+  const float* init;  // [nseq or 1, Hv, 128, 128] or null
+  int init_shared;
+  int64_t capture;       // tokens before the captured state (0 = none); nseq == 1
+  float* capture_state;  // [Hv, 128, 128]
+  float* final_state;    // [nseq, Hv, 128, 128] or null
+  float* out;            // [T, Hv, 128]
+};
+
+__global__ void __launch_bounds__(THREADS, 1) delta_scan_kernel(ScanArgs a) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int h = blockIdx.x % a.Hv;
+  const int s = blockIdx.x / a.Hv;
+  const int kh = h / (a.Hv / a.Hk);
+  const int64_t start = a.cu ? a.cu[s] : 0;
+  const int64_t len = a.cu ? a.cu[s + 1] - start : a.T;
+  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(sm);
+  float* As = reinterpret_cast<float*>(sm + OFF_A);
+  float* Ts = reinterpret_cast<float*>(sm + OFF_T);
+  float* Ms = reinterpret_cast<float*>(sm + OFF_M);
+  double* Gs = reinterpret_cast<double*>(sm + OFF_G);
+  float* eg = reinterpret_cast<float*>(sm + OFF_EG);
+  float* egd = reinterpret_cast<float*>(sm + OFF_EGD);
+  float* bs = reinterpret_cast<float*>(sm + OFF_BETA);
+  float* ecap = reinterpret_cast<float*>(sm + OFF_ECAP);
+
+  // S^T rows [16w, 16w+16) (value columns) x 128 key columns: 16 n-tiles.
+  const int r0 = lane >> 2, c0 = 2 * (lane & 3);
+  const int dv0 = warp * 16;
+  float S[16][4];
+  {
+    const float* init = a.init ? a.init + (a.init_shared ? 0 : (int64_t)s * a.Hv * DK * DV) +
+                                     (int64_t)h * DK * DV
+                               : nullptr;
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int dv = dv0 + r0 + (e >> 1) * 8;
+        const int dk = nt * 8 + c0 + (e & 1);
+        S[nt][e] = init ? init[(int64_t)dk * DV + dv] : 0.f;
+      }
     }
-    Ss[idx] = v0;
   }
 
-  for (int ci = 0; ci < sq.nchunks; ++ci) {
-    const int64_t gc = sq.chunk0 + ci;
-    const ScanChunk ch = chunks[gc];
-    const int n = ch.n;
-    const float* blk = data + (gc * Hv + h) * kBlock;
-    // (a) stage the chunk.
-    for (int idx = tid; idx < C * (DK / 4); idx += 256) {
-      const int i = idx / (DK / 4), c4 = (idx % (DK / 4)) * 4;
-      const float4 wv = *reinterpret_cast<const float4*>(blk + kW + i * DK + c4);
-      float4 qv = make_float4(0.f, 0.f, 0.f, 0.f), kv = qv;
+  const int64_t nchunks = (len + C - 1) / C;
+  for (int64_t ci = 0; ci < nchunks; ++ci) {
+    const int64_t t0 = start + ci * C;
+    const int n = (int)(len - ci * C < C ? len - ci * C : C);
+    // ---- stage K, Q (hi/lo BF16), gates ----------------------------------
+    for (int idx = tid; idx < C * (DK / 4); idx += THREADS) {
+      const int i = idx >> 5, c4 = (idx & 31) * 4;
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), qv = kv;
       if (i < n) {
-        const int64_t off = ((ch.t0 + i) * Hk + kh) * DK + c4;
-        qv = *reinterpret_cast<const float4*>(q + off);
-        kv = *reinterpret_cast<const float4*>(k + off);
+        const int64_t off = ((t0 + i) * a.Hk + kh) * DK + c4;
+        kv = *reinterpret_cast<const float4*>(a.k + off);
+        qv = *reinterpret_cast<const float4*>(a.q + off);
       }
-      *reinterpret_cast<float4*>(Ws + i * WP + c4) = wv;
-      *reinterpret_cast<float4*>(Qs + i * WP + c4) = qv;
-      *reinterpret_cast<float4*>(Ks + i * WP + c4) = kv;
+      uint32_t kh0, kl0, kh1, kl1, qh0, ql0, qh1, ql1;
+      split2(kv.x, kv.y, kh0, kl0);
+      split2(kv.z, kv.w, kh1, kl1);
+      split2(qv.x, qv.y, qh0, ql0);
+      split2(qv.z, qv.w, qh1, ql1);
+      const uint32_t o = swz(i, c4, 16);
+      *reinterpret_cast<uint2*>(sm + OFF_KHI + o) = make_uint2(kh0, kh1);
+      *reinterpret_cast<uint2*>(sm + OFF_KLO + o) = make_uint2(kl0, kl1);
+      *reinterpret_cast<uint2*>(sm + OFF_QHI + o) = make_uint2(qh0, qh1);
+      *reinterpret_cast<uint2*>(sm + OFF_QLO + o) = make_uint2(ql0, ql1);
     }
-    for (int idx = tid; idx < C * (C / 4); idx += 256) {
-      const int i = idx / (C / 4), c4 = (idx % (C / 4)) * 4;
-      *reinterpret_cast<float4*>(Ps + i * PP + c4) =
-          *reinterpret_cast<const float4*>(blk + kP + i * C + c4);
+    if (warp == 0) {
+      // Chunk-relative inclusive cumsum of g in FP64, two tokens a lane.
+      const int i0 = 2 * lane, i1 = i0 + 1;
+      const double g0 = i0 < n ? (double)a.g[(t0 + i0) * a.Hv + h] : 0.0;
+      const double g1 = i1 < n ? (double)a.g[(t0 + i1) * a.Hv + h] : 0.0;
+      const double pair = g0 + g1;
+      double run = pair;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const double up = __shfl_up_sync(0xffffffffu, run, o);
+        if (lane >= o) run += up;
+      }
+      const double excl = run - pair;
+      Gs[i0] = excl + g0;
+      Gs[i1] = excl + g0 + g1;
+      bs[i0] = i0 < n ? a.beta[(t0 + i0) * a.Hv + h] : 0.f;
+      bs[i1] = i1 < n ? a.beta[(t0 + i1) * a.Hv + h] : 0.f;
     }
-    {
-      const int i = tid >> 2, c4 = (tid & 3) * 4;
-      *reinterpret_cast<float4*>(Us + i * DVS + c4) =
-          *reinterpret_cast<const float4*>(blk + kU + i * DV + c0 + c4);
-    }
+    __syncthreads();
+    const double Glast = Gs[C - 1];  // padded tokens carry g = 0
+    int cap_row = -1;                // row whose post-state is captured
+    if (a.capture_state && a.capture > ci * C && a.capture <= ci * C + n)
+      cap_row = (int)(a.capture - 1 - ci * C);
     if (tid < C) {
-      eg[tid] = blk[kEG + tid];
-      egd[tid] = blk[kEGD + tid];
+      eg[tid] = expf((float)Gs[tid]);
+      egd[tid] = expf((float)(Glast - Gs[tid]));
+      if (cap_row >= 0) ecap[tid] = tid <= cap_row ? expf((float)(Gs[cap_row] - Gs[tid])) : 0.f;
     }
-    if (tid == 0) egl[0] = blk[kEGL];
+    // ---- Gram matrices: K K^T -> A (F32), Q K^T -> P (hi/lo) -----------------
+    {
+      const int m0 = (warp >> 1) * 16, nb = (warp & 1) * 32;
+      float kk[4][4], qk[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) kk[j][e] = qk[j][e] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < DK / 16; ++ks) {
+        uint32_t akh[4], akl[4], aqh[4], aql[4];
+        lda(sbase + OFF_KHI, m0, ks * 16, 16, lane, akh);
+        lda(sbase + OFF_KLO, m0, ks * 16, 16, lane, akl);
+        lda(sbase + OFF_QHI, m0, ks * 16, 16, lane, aqh);
+        lda(sbase + OFF_QLO, m0, ks * 16, 16, lane, aql);
+#pragma unroll
+        for (int np = 0; np < 2; ++np) {
+          uint32_t bh[4], bl[4];
+          ldb_nk(sbase + OFF_KHI, nb + np * 16, ks * 16, 16, lane, bh);
+          ldb_nk(sbase + OFF_KLO, nb + np * 16, ks * 16, 16, lane, bl);
+          mma3(kk[2 * np], akh, akl, bh[0], bh[1], bl[0], bl[1]);
+          mma3(kk[2 * np + 1], akh, akl, bh[2], bh[3], bl[2], bl[3]);
+          mma3(qk[2 * np], aqh, aql, bh[0], bh[1], bl[0], bl[1]);
+          mma3(qk[2 * np + 1], aqh, aql, bh[2], bh[3], bl[2], bl[3]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int e = 0; e < 4; e += 2) {
+          const int i = m0 + r0 + (e >> 1) * 8;
+          float pv[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int col = nb + j * 8 + c0 + u;
+            const bool lower = col <= i && i < n;
+            const float decay = lower ? expf((float)(Gs[i] - Gs[col])) : 0.f;
+            As[i * AP + col] = (lower && col < i) ? bs[i] * (decay * kk[j][e + u]) : 0.f;
+            pv[u] = lower ? decay * qk[j][e + u] : 0.f;
+          }
+          uint32_t ph, pl;
+          split2(pv[0], pv[1], ph, pl);
+          const uint32_t o = swz(i, nb + j * 8 + c0, 8);
+          *reinterpret_cast<uint32_t*>(sm + OFF_PHI + o) = ph;
+          *reinterpret_cast<uint32_t*>(sm + OFF_PLO + o) = pl;
+        }
+      }
+    }
+    __syncthreads();
+    // ---- T = (I + A)^{-1}: diagonal 16 x 16 blocks --------------------------
+    if (warp < 4 && lane < 16) {
+      const int b0 = warp * 16, c = lane;
+      float x[16];
+#pragma unroll
+      for (int r = 0; r < 16; ++r) {
+        float acc = r == c ? 1.f : 0.f;
+#pragma unroll
+        for (int j = 0; j < r; ++j) acc -= As[(b0 + r) * AP + b0 + j] * x[j];
+        x[r] = r < c ? 0.f : acc;
+      }
+#pragma unroll
+      for (int r = 0; r < 16; ++r) Ts[(b0 + r) * AP + b0 + c] = x[r];
+    }
+    // Upper blocks are zero.
+    for (int idx = tid; idx < C * C; idx += THREADS) {
+      const int i = idx >> 6, j = idx & 63;
+      if ((j >> 4) > (i >> 4)) Ts[i * AP + j] = 0.f;
+    }
+    __syncthreads();
+    // Off-diagonal blocks, block row by block row:
+    //   T_bj = -D_b * sum_{k=j}^{b-1} A_bk T_kj.
+    for (int b = 1; b < 4; ++b) {
+      for (int idx = tid; idx < b * 256; idx += THREADS) {
+        const int j = idx >> 8, r = (idx >> 4) & 15, c = idx & 15;
+        float acc = 0.f;
+        for (int kb = j; kb < b; ++kb)
+#pragma unroll
+          for (int q = 0; q < 16; ++q)
+            acc += As[(b * 16 + r) * AP + kb * 16 + q] * Ts[(kb * 16 + q) * AP + j * 16 + c];
+        Ms[(j * 16 + r) * 17 + c] = acc;
+      }
+      __syncthreads();
+      for (int idx = tid; idx < b * 256; idx += THREADS) {
+        const int j = idx >> 8, r = (idx >> 4) & 15, c = idx & 15;
+        float acc = 0.f;
+#pragma unroll
+        for (int q = 0; q <= 15; ++q)
+          acc += Ts[(b * 16 + r) * AP + b * 16 + q] * Ms[(j * 16 + q) * 17 + c];
+        Ts[(b * 16 + r) * AP + j * 16 + c] = -acc;
+      }
+      __syncthreads();
+    }
+    // T diag(beta) -> hi/lo BF16.
+    for (int idx = tid; idx < C * C / 2; idx += THREADS) {
+      const int i = idx >> 5, j = (idx & 31) * 2;
+      uint32_t th, tl;
+      split2(Ts[i * AP + j] * bs[j], Ts[i * AP + j + 1] * bs[j + 1], th, tl);
+      const uint32_t o = swz(i, j, 8);
+      *reinterpret_cast<uint32_t*>(sm + OFF_THI + o) = th;
+      *reinterpret_cast<uint32_t*>(sm + OFF_TLO + o) = tl;
+    }
     __syncthreads();
 
-    // (b) X = W S, Y = Q S; D = U - X.
-    const int r = tid >> 2, cg = (tid & 3) * 4;
-    float4 x = make_float4(0.f, 0.f, 0.f, 0.f), y = x;
-#pragma unroll 8
-    for (int kk = 0; kk < DK; ++kk) {
-      const float4 sv = *reinterpret_cast<const float4*>(Ss + kk * DVS + cg);
-      const float w = Ws[r * WP + kk], qq = Qs[r * WP + kk];
-      x.x = fmaf(w, sv.x, x.x); x.y = fmaf(w, sv.y, x.y);
-      x.z = fmaf(w, sv.z, x.z); x.w = fmaf(w, sv.w, x.w);
-      y.x = fmaf(qq, sv.x, y.x); y.y = fmaf(qq, sv.y, y.y);
-      y.z = fmaf(qq, sv.z, y.z); y.w = fmaf(qq, sv.w, y.w);
-    }
-    {
-      const float4 u = *reinterpret_cast<const float4*>(Us + r * DVS + cg);
-      *reinterpret_cast<float4*>(Ds + r * DVS + cg) =
-          make_float4(u.x - x.x, u.y - x.y, u.z - x.z, u.w - x.w);
-    }
-    __syncthreads();
-
-    // (c) O = e^G o Y + P D  (rows < n).
-    {
-      const float e = eg[r];
-      float4 o = make_float4(e * y.x, e * y.y, e * y.z, e * y.w);
-      const float* prow = Ps + r * PP;
-      for (int j = 0; j <= r; ++j) {
-        const float p = prow[j];
-        const float4 dv = *reinterpret_cast<const float4*>(Ds + j * DVS + cg);
-        o.x = fmaf(p, dv.x, o.x); o.y = fmaf(p, dv.y, o.y);
-        o.z = fmaf(p, dv.z, o.z); o.w = fmaf(p, dv.w, o.w);
-      }
-      if (r < n)
-        *reinterpret_cast<float4*>(out + ((ch.t0 + r) * Hv + h) * DV + c0 + cg) = o;
-    }
-    // (d) S = e^{G_last} S + (e^{G_last-G} o K)^T D.
-    {
-      const int kk = tid >> 1, hc = (tid & 1) * 8;
-      const float el = egl[0];
-      float4 s0 = *reinterpret_cast<const float4*>(Ss + kk * DVS + hc);
-      float4 s1 = *reinterpret_cast<const float4*>(Ss + kk * DVS + hc + 4);
-      float4 a0 = make_float4(el * s0.x, el * s0.y, el * s0.z, el * s0.w);
-      float4 a1 = make_float4(el * s1.x, el * s1.y, el * s1.z, el * s1.w);
-      for (int j = 0; j < n; ++j) {
-        const float kd = egd[j] * Ks[j * WP + kk];
-        const float4 d0 = *reinterpret_cast<const float4*>(Ds + j * DVS + hc);
-        const float4 d1 = *reinterpret_cast<const float4*>(Ds + j * DVS + hc + 4);
-        a0.x = fmaf(kd, d0.x, a0.x); a0.y = fmaf(kd, d0.y, a0.y);
-        a0.z = fmaf(kd, d0.z, a0.z); a0.w = fmaf(kd, d0.w, a0.w);
-        a1.x = fmaf(kd, d1.x, a1.x); a1.y = fmaf(kd, d1.y, a1.y);
-        a1.z = fmaf(kd, d1.z, a1.z); a1.w = fmaf(kd, d1.w, a1.w);
-      }
-      __syncthreads();  // every reader of the old S (step b) is done
-      *reinterpret_cast<float4*>(Ss + kk * DVS + hc) = a0;
-      *reinterpret_cast<float4*>(Ss + kk * DVS + hc + 4) = a1;
-      if (capture_state && ci == sq.capture_chunk) {
-        float* dst = capture_state + ((int64_t)h * DK + kk) * DV + c0 + hc;
-        *reinterpret_cast<float4*>(dst) = a0;
-        *reinterpret_cast<float4*>(dst + 4) = a1;
+    // ---- per-warp state products (value rows dv0..dv0+15) ---------------
+    // R^T = V^T - (S^T K^T) diag(e^G): 16 x 64, eight n-tiles of tokens.
+    float R[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) R[nt][e] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < DK / 16; ++ks) {
+      uint32_t ah[4], al[4];
+      acc_to_a(S[2 * ks], S[2 * ks + 1], ah, al);
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        uint32_t bh[4], bl[4];
+        ldb_nk(sbase + OFF_KHI, np * 16, ks * 16, 16, lane, bh);
+        ldb_nk(sbase + OFF_KLO, np * 16, ks * 16, 16, lane, bl);
+        mma3(R[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
+        mma3(R[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
       }
     }
-    __syncthreads();
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int tok = nt * 8 + c0 + (e & 1);
+        const int dv = dv0 + r0 + (e >> 1) * 8;
+        const float vv = tok < n ? a.v[((t0 + tok) * a.Hv + h) * DV + dv] : 0.f;
+        R[nt][e] = vv - eg[tok] * R[nt][e];
+      }
+    }
+    // D^T = R^T (T diag(beta))^T.
+    float D[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) D[nt][e] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < C / 16; ++ks) {
+      uint32_t ah[4], al[4];
+      acc_to_a(R[2 * ks], R[2 * ks + 1], ah, al);
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        uint32_t bh[4], bl[4];
+        ldb_nk(sbase + OFF_THI, np * 16, ks * 16, 8, lane, bh);
+        ldb_nk(sbase + OFF_TLO, np * 16, ks * 16, 8, lane, bl);
+        mma3(D[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
+        mma3(D[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+      }
+    }
+    // O^T = (S^T Q^T) diag(e^G) + D^T P^T  (R's registers are reused for O).
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) R[nt][e] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < DK / 16; ++ks) {
+      uint32_t ah[4], al[4];
+      acc_to_a(S[2 * ks], S[2 * ks + 1], ah, al);
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        uint32_t bh[4], bl[4];
+        ldb_nk(sbase + OFF_QHI, np * 16, ks * 16, 16, lane, bh);
+        ldb_nk(sbase + OFF_QLO, np * 16, ks * 16, 16, lane, bl);
+        mma3(R[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
+        mma3(R[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) R[nt][e] *= eg[nt * 8 + c0 + (e & 1)];
+#pragma unroll
+    for (int ks = 0; ks < C / 16; ++ks) {
+      uint32_t ah[4], al[4];
+      acc_to_a(D[2 * ks], D[2 * ks + 1], ah, al);
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        uint32_t bh[4], bl[4];
+        ldb_nk(sbase + OFF_PHI, np * 16, ks * 16, 8, lane, bh);
+        ldb_nk(sbase + OFF_PLO, np * 16, ks * 16, 8, lane, bl);
+        mma3(R[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
+        mma3(R[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int tok = nt * 8 + c0 + (e & 1);
+        const int dv = dv0 + r0 + (e >> 1) * 8;
+        if (tok < n) a.out[((t0 + tok) * a.Hv + h) * DV + dv] = R[nt][e];
+      }
+    }
+    // Capture: S_c^T = e^{G_c} S^T + (D^T diag(e^{G_c - G} [j <= c])) K.
+    if (cap_row >= 0) {
+      const float ec = expf((float)Gs[cap_row]);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float X[8][4];
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) X[nt][e] = ec * S[half * 8 + nt][e];
+#pragma unroll
+        for (int ks = 0; ks < C / 16; ++ks) {
+          float d0[4], d1[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            d0[e] = D[2 * ks][e] * ecap[ks * 16 + c0 + (e & 1)];
+            d1[e] = D[2 * ks + 1][e] * ecap[ks * 16 + 8 + c0 + (e & 1)];
+          }
+          uint32_t ah[4], al[4];
+          acc_to_a(d0, d1, ah, al);
+#pragma unroll
+          for (int np = 0; np < 4; ++np) {
+            uint32_t bh[4], bl[4];
+            ldb_kn(sbase + OFF_KHI, half * 64 + np * 16, ks * 16, 16, lane, bh);
+            ldb_kn(sbase + OFF_KLO, half * 64 + np * 16, ks * 16, 16, lane, bl);
+            mma3(X[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
+            mma3(X[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+          }
+        }
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int dv = dv0 + r0 + (e >> 1) * 8;
+            const int dk = (half * 8 + nt) * 8 + c0 + (e & 1);
+            a.capture_state[((int64_t)h * DK + dk) * DV + dv] = X[nt][e];
+          }
+      }
+    }
+    // S^T <- e^{G_last} S^T + (D^T diag(e^{G_last - G})) K.
+    const float el = expf((float)Glast);
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) S[nt][e] *= el;
+#pragma unroll
+    for (int ks = 0; ks < C / 16; ++ks) {
+      float d0[4], d1[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        d0[e] = D[2 * ks][e] * egd[ks * 16 + c0 + (e & 1)];
+        d1[e] = D[2 * ks + 1][e] * egd[ks * 16 + 8 + c0 + (e & 1)];
+      }
+      uint32_t ah[4], al[4];
+      acc_to_a(d0, d1, ah, al);
+#pragma unroll
+      for (int np = 0; np < 8; ++np) {
+        uint32_t bh[4], bl[4];
+        ldb_kn(sbase + OFF_KHI, np * 16, ks * 16, 16, lane, bh);
+        ldb_kn(sbase + OFF_KLO, np * 16, ks * 16, 16, lane, bl);
+        mma3(S[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
+        mma3(S[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+      }
+    }
+    __syncthreads();  // the next chunk overwrites the shared tiles
   }
-  if (final_state) {
-    for (int idx = tid; idx < DK * DVS; idx += 256) {
-      const int kk = idx / DVS, c = idx % DVS;
-      final_state[(((int64_t)s * Hv + h) * DK + kk) * DV + c0 + c] = Ss[idx];
-    }
+  if (a.final_state) {
+    float* dst = a.final_state + ((int64_t)s * a.Hv + h) * DK * DV;
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int dv = dv0 + r0 + (e >> 1) * 8;
+        const int dk = nt * 8 + c0 + (e & 1);
+        dst[(int64_t)dk * DV + dv] = S[nt][e];
+      }
   }
 }
-
-constexpr size_t kPrepSmem = sizeof(float) * (2 * C * KP + C * AP + 2 * C) + sizeof(double) * C;
-constexpr size_t kCarrySmem =
-    sizeof(float) * (3 * C * WP + C * PP + DK * DVS + 2 * C * DVS + 2 * C + 4);
 
 }  // namespace
 
 size_t delta_scan_workspace(int64_t total_tokens, int nseq, int Hv, int dk, int dv) {
+  (void)total_tokens;
+  (void)Hv;
   (void)dk;
   (void)dv;
-  return layout(total_tokens, nseq, Hv).total;
+  // Only the per-sequence token offsets travel to the device.
+  return ((size_t)(nseq + 1) * sizeof(int64_t) + 255) & ~(size_t)255;
+}
+
+// cu_dev: device copy of the offsets (or null for one sequence of cu_host[1]).
+int launch_delta_scan_dev(const float* q, const float* k, const float* v, const float* g,
+                          const float* beta, const int64_t* cu_dev, int64_t total, int nseq, int Hk,
+                          int Hv, const float* init, int init_shared, int64_t capture,
+                          float* capture_state, float* final_state, float* out, cudaStream_t s) {
+  static bool attr[64] = {false};
+  int dev = 0;
+  CLEF_CUDA(cudaGetDevice(&dev));
+  if (dev >= 0 && dev < 64 && !attr[dev]) {
+    CLEF_CUDA(cudaFuncSetAttribute(delta_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+    attr[dev] = true;
+  }
+  ScanArgs a;
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.g = g;
+  a.beta = beta;
+  a.cu = cu_dev;
+  a.T = total;
+  a.Hk = Hk;
+  a.Hv = Hv;
+  a.init = init;
+  a.init_shared = init_shared;
+  a.capture = capture;
+  a.capture_state = capture_state;
+  a.final_state = final_state;
+  a.out = out;
+  delta_scan_kernel<<<(unsigned)(nseq * Hv), THREADS, SMEM, s>>>(a);
+  return launch_status("delta_scan");
 }
 
 int launch_delta_scan(const float* q, const float* k, const float* v, const float* g,
@@ -381,52 +572,15 @@ int launch_delta_scan(const float* q, const float* k, const float* v, const floa
                       size_t ws_bytes, cudaStream_t s) {
   CLEF_CHECK(dk == DK && dv == DV, CLEF_ERR_UNSUPPORTED, "delta_scan: dk and dv must be 128");
   const int64_t total = cu_host[nseq];
-  const Layout l = layout(total, nseq, Hv);
-  CLEF_CHECK(ws_bytes >= l.total, CLEF_ERR_INVALID, "delta_scan: workspace too small");
-  // Chunk plan: 64-token chunks per sequence; a capture point starts a new chunk.
-  std::vector<ScanSeq> seqs(nseq);
-  std::vector<ScanChunk> chunks;
-  chunks.reserve((size_t)l.max_chunks);
-  for (int si = 0; si < nseq; ++si) {
-    const int64_t a = cu_host[si], b = cu_host[si + 1];
-    seqs[si].chunk0 = (int32_t)chunks.size();
-    seqs[si].capture_chunk = -1;
-    seqs[si].pad = 0;
-    const int64_t cut = (capture > 0 && capture < b - a) ? a + capture : b;
-    for (int64_t t = a; t < cut; t += C)
-      chunks.push_back({t, (int32_t)std::min<int64_t>(C, cut - t), si});
-    if (capture > 0) seqs[si].capture_chunk = (int32_t)chunks.size() - 1 - seqs[si].chunk0;
-    for (int64_t t = cut; t < b; t += C)
-      chunks.push_back({t, (int32_t)std::min<int64_t>(C, b - t), si});
-    seqs[si].nchunks = (int32_t)chunks.size() - seqs[si].chunk0;
+  const int64_t* cu_dev = nullptr;
+  if (nseq > 1) {
+    CLEF_CHECK(ws && ws_bytes >= delta_scan_workspace(total, nseq, Hv, dk, dv), CLEF_ERR_INVALID,
+               "delta_scan: workspace too small");
+    CLEF_CUDA(cudaMemcpyAsync(ws, cu_host, sizeof(int64_t) * (nseq + 1), cudaMemcpyHostToDevice, s));
+    cu_dev = reinterpret_cast<const int64_t*>(ws);
   }
-  CLEF_CHECK((int64_t)chunks.size() <= l.max_chunks, CLEF_ERR_INVALID, "delta_scan: chunk plan");
-  char* base = reinterpret_cast<char*>(ws);
-  ScanSeq* seqs_d = reinterpret_cast<ScanSeq*>(base + l.seq_off);
-  ScanChunk* chunks_d = reinterpret_cast<ScanChunk*>(base + l.chunk_off);
-  float* data = reinterpret_cast<float*>(base + l.data_off);
-  CLEF_CUDA(cudaMemcpyAsync(seqs_d, seqs.data(), sizeof(ScanSeq) * seqs.size(),
-                            cudaMemcpyHostToDevice, s));
-  CLEF_CUDA(cudaMemcpyAsync(chunks_d, chunks.data(), sizeof(ScanChunk) * chunks.size(),
-                            cudaMemcpyHostToDevice, s));
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  CLEF_CUDA(cudaGetDevice(&dev));
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    CLEF_CUDA(cudaFuncSetAttribute(delta_chunk_prep, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)kPrepSmem));
-    CLEF_CUDA(cudaFuncSetAttribute(delta_chunk_carry, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)kCarrySmem));
-    attr_set[dev] = true;
-  }
-  const dim3 g1((unsigned)chunks.size(), (unsigned)Hv);
-  delta_chunk_prep<<<g1, 256, kPrepSmem, s>>>(q, k, v, g, beta, chunks_d, Hk, Hv, data);
-  int rc = launch_status("delta_chunk_prep");
-  if (rc) return rc;
-  const unsigned g2 = (unsigned)(nseq * Hv * SLICES);
-  delta_chunk_carry<<<g2, 256, kCarrySmem, s>>>(q, k, seqs_d, chunks_d, data, Hk, Hv, init,
-                                                init_shared, capture_state, final_state, out);
-  return launch_status("delta_chunk_carry");
+  return launch_delta_scan_dev(q, k, v, g, beta, cu_dev, total, nseq, Hk, Hv, init, init_shared,
+                               capture, capture_state, final_state, out, s);
 }
 
 }  // namespace clef
@@ -446,8 +600,7 @@ int clef_delta_scan(const float* q, const float* k, const float* v, const float*
                     const int64_t* cu_seqlens, int32_t nseq, const float* init_state,
                     int32_t init_shared, int64_t capture, float* capture_state, float* final_state,
                     float* out, void* workspace, size_t workspace_bytes, void* stream) {
-  CLEF_CHECK(q && k && v && g && beta && out && workspace, CLEF_ERR_INVALID,
-             "delta_scan: null pointer");
+  CLEF_CHECK(q && k && v && g && beta && out, CLEF_ERR_INVALID, "delta_scan: null pointer");
   CLEF_CHECK(dk == 128 && dv == 128, CLEF_ERR_UNSUPPORTED, "delta_scan: dk and dv must be 128");
   CLEF_CHECK(Hk > 0 && Hv > 0 && Hv % Hk == 0 && Hv <= 4096, CLEF_ERR_INVALID,
              "delta_scan: head counts");
@@ -470,10 +623,14 @@ int clef_delta_scan(const float* q, const float* k, const float* v, const float*
     CLEF_CHECK(capture <= T && capture_state, CLEF_ERR_INVALID,
                "delta_scan: capture boundary or capture_state");
   }
-  CLEF_CHECK(((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) % 16 == 0,
-             CLEF_ERR_INVALID, "delta_scan: q, k, v, out must be 16-byte aligned");
-  CLEF_CHECK(((uintptr_t)workspace & 255) == 0, CLEF_ERR_INVALID,
-             "delta_scan: workspace must be 256-byte aligned");
+  CLEF_CHECK(((uintptr_t)q | (uintptr_t)k) % 16 == 0, CLEF_ERR_INVALID,
+             "delta_scan: q and k must be 16-byte aligned");
+  if (nseq > 1) {
+    CLEF_CHECK(workspace && workspace_bytes >= delta_scan_workspace(T, nseq, Hv, dk, dv),
+               CLEF_ERR_INVALID, "delta_scan: workspace too small");
+    CLEF_CHECK(((uintptr_t)workspace & 255) == 0, CLEF_ERR_INVALID,
+               "delta_scan: workspace must be 256-byte aligned");
+  }
   return launch_delta_scan(q, k, v, g, beta, cu.data(), nseq, Hk, Hv, dk, dv, init_state,
                            init_shared, capture, capture_state, final_state, out, workspace,
                            workspace_bytes, as_stream(stream));

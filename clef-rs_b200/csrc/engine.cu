@@ -479,9 +479,9 @@ int run_pack(clef_engine* e, const int32_t* ids, const int64_t* offsets, int s0,
       }
       {
         STAGE(kStDeltaScan);
-        RC(launch_delta_scan(e->dq, e->dk, e->dv, e->dg, e->db, cu.data(), np, hk, hv, 128, 128,
-                             il ? il->S : nullptr, 1, capture, cap ? cap->layers[li].S : nullptr,
-                             nullptr, e->dout, e->scan_ws, e->scan_ws_bytes, s));
+        RC(launch_delta_scan_dev(e->dq, e->dk, e->dv, e->dg, e->db, e->meta_d, M, np, hk, hv,
+                                 il ? il->S : nullptr, 1, capture,
+                                 cap ? cap->layers[li].S : nullptr, nullptr, e->dout, s));
       }
       if (cap) {
         auto& cl = cap->layers[li];

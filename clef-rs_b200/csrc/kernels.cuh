@@ -57,6 +57,12 @@ int launch_delta_scan(const float* q, const float* k, const float* v, const floa
                       float* capture_state, float* final_state, float* out, void* ws,
                       size_t ws_bytes, cudaStream_t s);
 
+// Same, with the offsets already on the device (null = one sequence of `total`).
+int launch_delta_scan_dev(const float* q, const float* k, const float* v, const float* g,
+                          const float* beta, const int64_t* cu_dev, int64_t total, int nseq, int Hk,
+                          int Hv, const float* init, int init_shared, int64_t capture,
+                          float* capture_state, float* final_state, float* out, cudaStream_t s);
+
 // ---- rng.cu -----------------------------------------------------------------
 // Philox4x32-10 counter-based normal / uniform generator, deterministic in
 // (seed, stream, element index) on host and device.

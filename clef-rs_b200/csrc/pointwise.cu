@@ -120,7 +120,16 @@ __global__ void __launch_bounds__(256) delta_prologue_kernel(
   const int width = 2 * key + Hv * 128;
   const int lane = threadIdx.x & 31;
   for (int base = threadIdx.x * 4; base < width; base += 1024) {
-    // Four causal taps for four channels.
+    // Taps of the four channels: conv_w[c][0..3] for c = base .. base+3.
+    const float4 w0 = *reinterpret_cast<const float4*>(conv_w + (base + 0) * 4);
+    const float4 w1 = *reinterpret_cast<const float4*>(conv_w + (base + 1) * 4);
+    const float4 w2 = *reinterpret_cast<const float4*>(conv_w + (base + 2) * 4);
+    const float4 w3 = *reinterpret_cast<const float4*>(conv_w + (base + 3) * 4);
+    const float tw[4][4] = {{w0.x, w1.x, w2.x, w3.x},
+                            {w0.y, w1.y, w2.y, w3.y},
+                            {w0.z, w1.z, w2.z, w3.z},
+                            {w0.w, w1.w, w2.w, w3.w}};
+    // Four causal taps for four channels, oldest to newest.
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int tap = 0; tap < 4; ++tap) {
@@ -134,18 +143,10 @@ __global__ void __launch_bounds__(256) delta_prologue_kernel(
       } else {
         continue;
       }
-      const float4 wv0 = *reinterpret_cast<const float4*>(conv_w + (base + 0) * 4);
-      const float4 wv1 = *reinterpret_cast<const float4*>(conv_w + (base + 1) * 4);
-      const float4 wv2 = *reinterpret_cast<const float4*>(conv_w + (base + 2) * 4);
-      const float4 wv3 = *reinterpret_cast<const float4*>(conv_w + (base + 3) * 4);
-      const float w0 = tap == 0 ? wv0.x : tap == 1 ? wv0.y : tap == 2 ? wv0.z : wv0.w;
-      const float w1 = tap == 0 ? wv1.x : tap == 1 ? wv1.y : tap == 2 ? wv1.z : wv1.w;
-      const float w2 = tap == 0 ? wv2.x : tap == 1 ? wv2.y : tap == 2 ? wv2.z : wv2.w;
-      const float w3 = tap == 0 ? wv3.x : tap == 1 ? wv3.y : tap == 2 ? wv3.z : wv3.w;
-      acc.x = __fadd_rn(acc.x, __fmul_rn(xv.x, w0));
-      acc.y = __fadd_rn(acc.y, __fmul_rn(xv.y, w1));
-      acc.z = __fadd_rn(acc.z, __fmul_rn(xv.z, w2));
-      acc.w = __fadd_rn(acc.w, __fmul_rn(xv.w, w3));
+      acc.x = __fadd_rn(acc.x, __fmul_rn(xv.x, tw[tap][0]));
+      acc.y = __fadd_rn(acc.y, __fmul_rn(xv.y, tw[tap][1]));
+      acc.z = __fadd_rn(acc.z, __fmul_rn(xv.z, tw[tap][2]));
+      acc.w = __fadd_rn(acc.w, __fmul_rn(xv.w, tw[tap][3]));
     }
     float4 m = make_float4(silu_f(acc.x), silu_f(acc.y), silu_f(acc.z), silu_f(acc.w));
     if (base < 2 * key) {

@@ -71,21 +71,21 @@ def test_delta_scan_rejects_before_launch():
     cu = np.array([0, 40, 30, 64], np.int64)
     assert L.clef_delta_scan(FAKE, FAKE, FAKE, FAKE, FAKE, 64, 16, 32, 128, 128, cu.ctypes.data, 3,
                              None, 0, 0, None, None, FAKE, FAKE, 1 << 30, None) == 1
-    # workspace too small (validated before any upload)
-    assert L.clef_delta_scan(FAKE, FAKE, FAKE, FAKE, FAKE, 64, 16, 32, 128, 128, None, 1, None, 0, 0,
-                             None, None, FAKE, ctypes.c_void_p(0x20000), 16, None) == 1
+    # workspace too small for the offsets of three sequences
+    cu = np.array([0, 10, 30, 64], np.int64)
+    assert L.clef_delta_scan(FAKE, FAKE, FAKE, FAKE, FAKE, 64, 16, 32, 128, 128, cu.ctypes.data, 3,
+                             None, 0, 0, None, None, FAKE, ctypes.c_void_p(0x20000), 16, None) == 1
     assert "workspace" in cb.lib.clef_last_error().decode()
     assert args
 
 
-def test_workspace_size_grows_with_tokens():
-    a = cb.delta_scan_workspace_size(1024, 1, 32)
-    b = cb.delta_scan_workspace_size(4096, 1, 32)
-    assert 0 < a < b
-    # One (chunk, head) block holds W, U (64x128 each), P (64x64) and 3
-    # vectors; the chunk table adds 16 bytes a chunk (256-byte aligned).
-    blocks = (4096 - 1024) // 64 * 32 * (2 * 64 * 128 + 64 * 64 + 3 * 64) * 4
-    assert blocks <= b - a <= blocks + 4096
+def test_workspace_holds_only_the_offsets_table():
+    # The fused scan keeps its state on chip; the workspace carries the
+    # per-sequence token offsets (nseq + 1 int64, 256-byte granules).
+    assert cb.delta_scan_workspace_size(1024, 1, 32) == 256
+    assert cb.delta_scan_workspace_size(1 << 20, 31, 32) == 256
+    assert cb.delta_scan_workspace_size(1 << 20, 32, 32) == 512
+    assert cb.delta_scan_workspace_size(-1, 1, 32) == 0
 
 
 def test_gemm_rejects_before_launch():

@@ -1,0 +1,372 @@
+#!/usr/bin/env python
+"""Prefill throughput of the clef-rs B200 backend.
+
+Workload: the full random-init 32-layer hybrid backbone
+([3 x DeltaNet + 1 x attention] x 8, hidden 2560, intermediate 9216, 16/32
+DeltaNet heads of 128, 16/4 attention heads of 256) plus the linear schema head
+read at each request's last token; a batch of 256 synthetic requests per GPU
+with lengths U[256, 2048] and ids U[0, 248320) (seed 3 + 1000 * rank), BF16
+projections with F32 accumulation and an F32 residual stream and head.
+A step is one prefill of the whole batch. Requests are independent and weights
+are replicated, so each rank serves its own batch with no collective on the
+data path (weak scaling); the max over ranks of the device time is reported.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+`value` is measured with device-resident ids and logits (CUDA events on the
+launching stream); `e2e` runs the public host API (clef_engine_prefill) from
+pinned host ids to host logits. `--impl reference` times the CPU F32
+restatement of the reference path (oracle/) on the host cores instead.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "clef-rs_b200"))
+
+METRIC = "prefill tok/s"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--requests", type=int, default=256)
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample-tokens", type=int, default=256)
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+def workload_config(args, n_gpus):
+    return {"workload": "config4: 32-layer hybrid backbone + linear schema head",
+            "requests_per_gpu": args.requests, "prompt_len": "U[256,2048]", "vocab": 248320,
+            "layers": args.layers, "hidden": 2560, "intermediate": 9216,
+            "deltanet_heads": "16qk/32v x 128", "attention_heads": "16q/4kv x 256",
+            "chunk": 64, "parallelism": f"dp{n_gpus} (request-sharded, weights replicated)",
+            "l2": "not flushed: every step streams 8.4 GB of weights and tens of GB of "
+                  "activations, far above the 126 MB L2"}
+
+
+# ---------------------------------------------------------------------------
+# CPU F32 path (oracle/): the reference's algorithm on the host cores.
+# ---------------------------------------------------------------------------
+def host_weights(cfg, seed=3, std=0.02, threads=8):
+    """Seeded synthetic weights of the benchmark geometry, drawn on the host
+    (same distributions as the engine's device init, not the same values)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from clef_b200.config import weight_shapes
+    shapes = weight_shapes(cfg)
+    names = sorted(shapes)
+
+    def make(i_name):
+        i, name = i_name
+        rng = np.random.default_rng([seed, i])
+        shape = shapes[name]
+        if name.endswith("A_log"):
+            return name, rng.uniform(0, np.log(16), shape).astype(np.float32)
+        if name.endswith("dt_bias"):
+            return name, (0.1 * rng.standard_normal(shape, dtype=np.float32))
+        w = std * rng.standard_normal(shape, dtype=np.float32)
+        if name.endswith("linear_attn.norm.weight"):
+            w += 1
+        return name, w
+
+    with ThreadPoolExecutor(threads) as ex:
+        yield from ex.map(make, enumerate(names))
+
+
+def build_cpu_model(cfg):
+    import oracle
+    m = oracle.Model(cfg)
+    for name, w in host_weights(cfg):
+        m.set_weight(name, w)
+    m.check()
+    return m
+
+
+def cpu_sample_ids(args):
+    from clef_b200 import workloads
+    req = workloads.backbone_requests(n=args.requests, seed=3)[0]
+    return req[: args.cpu_sample_tokens]
+
+
+def time_cpu(model, ids, reps):
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        model.prefill(ids)
+    return (time.perf_counter() - t0) / reps
+
+
+def cpu_baseline(args, cfg):
+    import oracle
+    threads = os.cpu_count() or 1
+    oracle.set_threads(threads)
+    model = build_cpu_model(cfg)
+    ids = cpu_sample_ids(args)
+    time_cpu(model, ids, 1)
+    sec = time_cpu(model, ids, 2)
+    return {"value": round(len(ids) / sec, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"one {len(ids)}-token request of the config-4 batch through the full "
+                      f"{cfg.num_hidden_layers}-layer F32 CPU path (oracle/oracle.cpp, OpenMP "
+                      f"{threads} threads, host-drawn weights of the same distributions), mean of 2 runs"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from clef_b200.config import benchmark_config
+    cfg = benchmark_config(args.layers, 7)
+    import oracle
+    threads = os.cpu_count() or 1
+    oracle.set_threads(threads)
+    model = build_cpu_model(cfg)
+    ids = cpu_sample_ids(args)
+    for _ in range(args.warmup):
+        model.prefill(ids)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        hidden, _ = model.prefill(ids)
+        times.append(time.perf_counter() - t0)
+    ms = 1000 * statistics.mean(times)
+    tok_s = len(ids) / (ms / 1000)
+    sample = (f"one {len(ids)}-token request of the config-4 batch per step through the full "
+              f"{cfg.num_hidden_layers}-layer F32 CPU path (oracle/oracle.cpp: C++ restatement of the "
+              f"reference's Candle CPU path; the Rust reference cannot be built here), "
+              f"{threads} threads")
+    line = {"metric": METRIC, "value": round(tok_s, 3), "unit": "tok/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "decisions_per_s": round(1000.0 / ms, 5),
+            "config": workload_config(args, args.gpus),
+            "cpu_baseline": {"value": round(tok_s, 3), "unit": "tok/s", "cores": threads,
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": round(tok_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "finite": bool(np.isfinite(hidden).all())}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling during the timed region.
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid):
+        self.uuid = uuid
+        self.proc = None
+        self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", self.uuid], stdout=self.out, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.out.flush()
+        rows = [r.split(",") for r in Path(self.out.name).read_text().splitlines() if r.strip()]
+        os.unlink(self.out.name)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [x.strip() for x in r]
+            try:
+                sm.append(float(r[0]))
+                mx = float(r[1])
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, r[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# Our arm.
+# ---------------------------------------------------------------------------
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    import torch
+    import torch.distributed as dist
+
+    import clef_b200 as cb
+    from clef_b200 import workloads
+    from clef_b200.config import benchmark_config, flops_per_request, linear_flops_per_token
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def allmax(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def allsum(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    cfg = benchmark_config(args.layers, 7)
+    eng = cb.Engine(cfg, local)
+    eng.init_random(3, 0.02)
+    eng.finalize()
+    reqs = workloads.backbone_requests(n=args.requests, seed=3 + 1000 * rank)
+    lens = np.array([len(r) for r in reqs], np.int64)
+    offsets = np.zeros(len(reqs) + 1, np.int64)
+    offsets[1:] = np.cumsum(lens)
+    ids = np.concatenate(reqs).astype(np.int32)
+    tokens = int(offsets[-1])
+    ids_dev = torch.from_numpy(ids).cuda()
+    logits_dev = torch.empty((len(reqs), 7), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.Stream()
+
+    for _ in range(args.warmup):
+        eng.prefill_device(ids_dev, offsets, logits_dev, stream=stream)
+    torch.cuda.synchronize()
+
+    # ---- device-resident timed region ---------------------------------------
+    uuid = str(torch.cuda.get_device_properties(local).uuid)
+    sampler = ClockSampler(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+    eng.set_profiling(True)
+    l0 = eng.launches()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler.start()
+    barrier()
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(args.steps):
+        eng.prefill_device(ids_dev, offsets, logits_dev, stream=stream)
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    ms = start.elapsed_time(end) / args.steps
+    launches = eng.launches() - l0
+    stages = eng.stage_times()
+    eng.set_profiling(False)
+    logits = logits_dev.cpu().numpy()
+    ms_max = allmax(ms)
+
+    # ---- end to end through the public host API ------------------------------
+    ids_pin = torch.from_numpy(ids).pin_memory()
+    lg_pin = torch.empty((len(reqs), 7), dtype=torch.float32).pin_memory()
+    ids_np, lg_np = ids_pin.numpy(), lg_pin.numpy()
+    eng.prefill_packed(ids_np, offsets, logits_out=lg_np)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        eng.prefill_packed(ids_np, offsets, logits_out=lg_np)
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    barrier()
+    e2e_max = allmax(e2e_s)
+    assert np.array_equal(lg_np, logits), "host and device-resident prefill disagree"
+    decisions = cb.decide(lg_np)
+
+    total_tokens = allsum(tokens)
+    total_reqs = allsum(len(reqs))
+    value = total_tokens / (ms_max / 1000.0)
+
+    # ---- roofline of the dominant kernel (the projection GEMMs) --------------
+    pk, pk_kind = peaks()
+    lin_flops = tokens * linear_flops_per_token(cfg)
+    gemm_ms = stages["gemm"] / args.steps
+    achieved = lin_flops / (gemm_ms / 1000.0) / 1e12
+    peak = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")))
+    traffic = None
+    tf = ROOT / "profiles" / "gemm_traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("bytes_per_launch")
+    roofline = {"bound": "tensor", "kernel": "gemm_kernel (tcgen05 projection GEMMs, all launches)",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4), "peak_source": f"{pk_kind} bf16_tflops_sustained",
+                "traffic": traffic,
+                "stage_ms_per_step": {k: round(v / args.steps, 3) for k, v in stages.items()}}
+    total_flops = sum(flops_per_request(cfg, int(L)) for L in lens)
+    line = {"metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded ids and random-init weights)",
+            "decisions_per_s": round(total_reqs / (ms_max / 1000.0), 2),
+            "model_tflops": round(allsum(total_flops) / (ms_max / 1000.0) / 1e12, 1),
+            "config": workload_config(args, world),
+            "roofline": roofline,
+            "e2e": {"value": round(total_tokens / e2e_max, 1), "unit": "tok/s",
+                    "decisions_per_s": round(total_reqs / e2e_max, 2),
+                    "h2d_bytes_per_step": int(ids.nbytes + offsets.nbytes),
+                    "d2h_bytes_per_step": int(lg_np.nbytes)},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+            "decisions_finite": bool(all(np.isfinite([d.noul, d.confidence, d.score]).all()
+                                         for d in decisions))}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args, cfg)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -32,7 +32,8 @@ EXPORTS = [
     "clef_delta_prologue", "clef_delta_scan_workspace_size", "clef_delta_scan", "clef_gemm_bf16",
     "clef_gemm_swiglu", "clef_attention_gqa", "clef_compact_copy", "clef_engine_create",
     "clef_engine_set_weight", "clef_engine_init_random", "clef_engine_get_weight",
-    "clef_engine_weight_count", "clef_engine_finalize", "clef_engine_prefill", "clef_engine_cancel",
+    "clef_engine_weight_count", "clef_engine_finalize", "clef_engine_prefill",
+    "clef_engine_prefill_device", "clef_engine_launches", "clef_engine_cancel",
     "clef_engine_stage_times", "clef_engine_set_profiling", "clef_engine_destroy",
     "clef_prefix_tokens", "clef_prefix_bytes", "clef_prefix_destroy", "clef_decide",
 ]
@@ -79,6 +80,8 @@ def _load():
         "clef_engine_finalize": (ctypes.c_int, [_vp]),
         "clef_engine_prefill": (ctypes.c_int, [_vp, _vp, _vp, _i32, _vp, _i64, ctypes.POINTER(_vp),
                                                _vp, _vp]),
+        "clef_engine_prefill_device": (ctypes.c_int, [_vp, _vp, _vp, _i32, _vp, _vp, _vp]),
+        "clef_engine_launches": (_i64, [_vp]),
         "clef_engine_cancel": (ctypes.c_int, [_vp, _i32]),
         "clef_engine_stage_times": (ctypes.c_int, [_vp, _vp, _i32]),
         "clef_engine_set_profiling": (ctypes.c_int, [_vp, _i32]),
@@ -273,12 +276,15 @@ class Prefix:
         return int(lib.clef_prefix_bytes(self.handle))
 
     def close(self):
-        if self.handle:
+        if self.handle and lib is not None:
             lib.clef_prefix_destroy(self.handle)
             self.handle = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class Engine:
@@ -347,10 +353,26 @@ class Engine:
                                        hid.ctypes.data if hid is not None else None))
         return lg, hid, (Prefix(cap.value) if cap.value else None)
 
+    def prefill_device(self, ids_dev, offsets: np.ndarray, logits_dev, initial: Prefix = None,
+                       stream=None) -> None:
+        """Stream-ordered prefill: ids_dev int32 CUDA tensor, logits_dev F32
+        CUDA tensor [nseq, outputs]; returns without synchronising."""
+        offsets = np.ascontiguousarray(offsets, dtype=np.int64)
+        _check(lib.clef_engine_prefill_device(self.handle, _ptr(ids_dev), offsets.ctypes.data,
+                                              offsets.size - 1,
+                                              initial.handle if initial is not None else None,
+                                              _ptr(logits_dev), _stream(stream)))
+
+    def launches(self) -> int:
+        return int(lib.clef_engine_launches(self.handle))
+
     def close(self):
-        if getattr(self, "handle", None):
+        if getattr(self, "handle", None) and lib is not None:
             lib.clef_engine_destroy(self.handle)
             self.handle = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -4,7 +4,6 @@ Mirrors TextConfig of the reference (crates/core/src/models/qwen.rs:42-58):
 the same fields, read from the same Hugging Face `text_config` JSON keys.
 """
 import ctypes
-import math
 
 MAX_LAYERS = 128
 
@@ -127,6 +126,23 @@ def weight_shapes(cfg: ClefConfig) -> dict:
     return s
 
 
+def linear_flops_per_token(cfg: ClefConfig) -> float:
+    """2 x (parameters of every projection): the GEMM FLOPs one token costs."""
+    h = cfg.hidden_size
+    key = cfg.linear_num_key_heads * cfg.linear_key_head_dim
+    value = cfg.linear_num_value_heads * cfg.linear_value_head_dim
+    n = cfg.num_attention_heads * cfg.head_dim
+    kv = cfg.num_key_value_heads * cfg.head_dim
+    lin = 0
+    for i in range(cfg.num_hidden_layers):
+        lin += 3 * cfg.intermediate_size * h
+        if cfg.layer_types[i]:
+            lin += (2 * n + 2 * kv) * h + n * h
+        else:
+            lin += (2 * key + value + value + 2 * cfg.linear_num_value_heads) * h + value * h
+    return 2.0 * lin
+
+
 def flops_per_request(cfg: ClefConfig, tokens: int, prefix: int = 0) -> float:
     """Algorithmic FLOPs of one prefill: 2*params of every linear layer per token
     plus 4*d per (query, key) pair and attention head (QK^T and PV), causal."""
@@ -155,9 +171,3 @@ def scan_flops_per_token(cfg: ClefConfig, chunk: int = 64) -> float:
     per_chunk = 2 * (2 * c * c * dk) + 2 * (2 * c * c * dk) + 2 * (c * dk * dv) * 3 + 2 * c * c * dv
     return per_chunk * hv / c
 
-
-def rope_inv_freq(cfg: ClefConfig):
-    return [cfg.rope_theta ** (-(2 * i) / cfg.rotary_dim) for i in range(cfg.rotary_dim // 2)]
-
-
-_ = math

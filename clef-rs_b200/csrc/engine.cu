@@ -116,6 +116,7 @@ struct clef_engine {
   float stage_ms[kStages] = {0};
   std::vector<cudaEvent_t> ev_pool;
   std::vector<std::pair<int, int>> ev_used;  // (stage, first event index)
+  int64_t launches = 0;  // kernels issued by prefill calls (cumulative)
 };
 
 namespace {
@@ -420,9 +421,13 @@ int alloc_prefix(clef_engine* e, int64_t tokens, clef_prefix** out) {
 }
 
 // One pack of whole sequences [s0, s1).
+// ids_dev: when set, the token ids already sit in device memory (packed like
+// `ids`) and logits_dev receives the logits on the device; nothing is copied
+// to or from the host except the offsets table.
 int run_pack(clef_engine* e, const int32_t* ids, const int64_t* offsets, int s0, int s1,
              const clef_prefix* init, int64_t capture, clef_prefix* cap, float* logits,
-             float* hidden, int64_t hidden_row0) {
+             float* hidden, int64_t hidden_row0, const int32_t* ids_dev = nullptr,
+             float* logits_dev = nullptr) {
   const clef_config& c = e->cfg;
   cudaStream_t s = e->stream;
   const int np = s1 - s0;
@@ -443,7 +448,15 @@ int run_pack(clef_engine* e, const int32_t* ids, const int64_t* offsets, int s0,
   qb[0] = 0;
   for (int i = 0; i < np; ++i) qb[i + 1] = qb[i] + (int32_t)ceil_div(cu[i + 1] - cu[i], 64);
   CLEF_CUDA(cudaMemcpyAsync(e->meta_d, meta.data(), meta.size(), cudaMemcpyHostToDevice, s));
-  CLEF_CUDA(cudaMemcpyAsync(e->ids_d, ids + t0, sizeof(int32_t) * M, cudaMemcpyHostToDevice, s));
+  const int32_t* ids_src = e->ids_d;
+  if (ids_dev) ids_src = ids_dev + t0;
+  else CLEF_CUDA(cudaMemcpyAsync(e->ids_d, ids + t0, sizeof(int32_t) * M, cudaMemcpyHostToDevice, s));
+  {
+    int64_t n = 2;  // embed + head
+    for (int li = 0; li < c.num_hidden_layers; ++li) n += c.layer_types[li] ? 8 : 9;
+    if (hidden || cap) n += 1;
+    e->launches += n;
+  }
   SeqPack pack;
   pack.cu_seqlens = e->meta_d;
   pack.nseq = np;
@@ -452,7 +465,7 @@ int run_pack(clef_engine* e, const int32_t* ids, const int64_t* offsets, int s0,
 
   {
     STAGE(kStEmbed);
-    RC(launch_embed(e->embed, e->ids_d, M, hid, e->h, s));
+    RC(launch_embed(e->embed, ids_src, M, hid, e->h, s));
   }
   for (int li = 0; li < c.num_hidden_layers; ++li) {
     if (e->cancel.load()) {
@@ -562,11 +575,13 @@ int run_pack(clef_engine* e, const int32_t* ids, const int64_t* offsets, int s0,
                      s));
     }
   }
-  if (logits && c.head_outputs) {
+  if ((logits || logits_dev) && c.head_outputs) {
     STAGE(kStHead);
-    RC(launch_head(e->h, e->final_eff, eps, pack, hid, e->head_w, c.head_outputs, e->logits_d, s));
-    CLEF_CUDA(cudaMemcpyAsync(logits + (size_t)s0 * c.head_outputs, e->logits_d,
-                              sizeof(float) * np * c.head_outputs, cudaMemcpyDeviceToHost, s));
+    float* dst = logits_dev ? logits_dev + (size_t)s0 * c.head_outputs : e->logits_d;
+    RC(launch_head(e->h, e->final_eff, eps, pack, hid, e->head_w, c.head_outputs, dst, s));
+    if (logits)
+      CLEF_CUDA(cudaMemcpyAsync(logits + (size_t)s0 * c.head_outputs, dst,
+                                sizeof(float) * np * c.head_outputs, cudaMemcpyDeviceToHost, s));
   }
   if (hidden || cap) {
     float* hn = e->proj;  // [M, hidden] F32 scratch
@@ -806,6 +821,40 @@ int clef_engine_prefill(clef_engine* e, const int32_t* ids, const int64_t* offse
   if (captured) *captured = cap;
   return CLEF_OK;
 }
+
+int clef_engine_prefill_device(clef_engine* e, const int32_t* ids_device, const int64_t* offsets,
+                               int32_t nseq, const clef_prefix* initial, float* logits_device,
+                               void* stream) {
+  CLEF_CHECK(e && ids_device && offsets && logits_device, CLEF_ERR_INVALID,
+             "prefill_device: null argument");
+  CLEF_CHECK(e->finalized, CLEF_ERR_INVALID, "prefill_device: engine not finalized");
+  CLEF_CHECK(nseq >= 1 && offsets[0] == 0, CLEF_ERR_INVALID, "prefill_device: offsets");
+  for (int i = 0; i < nseq; ++i)
+    CLEF_CHECK(offsets[i + 1] > offsets[i], CLEF_ERR_INVALID,
+               "prefill_device: empty or unordered sequence");
+  CLEF_CHECK(e->cfg.head_outputs > 0, CLEF_ERR_INVALID, "prefill_device: model has no head");
+  if (initial)
+    CLEF_CHECK(initial->device == e->device &&
+                   (int)initial->layers.size() == e->cfg.num_hidden_layers,
+               CLEF_ERR_INVALID, "prefill_device: prefix state does not match this engine");
+  DeviceGuard g(e->device);
+  e->ev_used.clear();
+  cudaStream_t user = as_stream(stream);
+  cudaStream_t own = e->stream;
+  e->stream = user ? user : own;
+  int rc = CLEF_OK;
+  for (int s0 = 0; s0 < nseq && rc == CLEF_OK;) {
+    int s1 = s0 + 1;
+    while (s1 < nseq && offsets[s1 + 1] - offsets[s0] <= e->max_pack) ++s1;
+    rc = run_pack(e, nullptr, offsets, s0, s1, initial, 0, nullptr, nullptr, nullptr, 0, ids_device,
+                  logits_device);
+    s0 = s1;
+  }
+  e->stream = own;
+  return rc;
+}
+
+int64_t clef_engine_launches(const clef_engine* e) { return e ? e->launches : 0; }
 
 int clef_engine_cancel(clef_engine* e, int32_t cancel) {
   CLEF_CHECK(e, CLEF_ERR_INVALID, "cancel: null engine");

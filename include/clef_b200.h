@@ -222,6 +222,18 @@ int clef_engine_prefill(clef_engine* e, const int32_t* ids, const int64_t* offse
                         int32_t nseq, const clef_prefix* initial, int64_t capture,
                         clef_prefix** captured, float* logits, float* hidden);
 
+/* Stream-ordered prefill with device-resident ids (int32, packed as in
+ * clef_engine_prefill) and device logits [nseq, head_outputs]; `offsets` is a
+ * host array. Issues the work on `stream` (NULL = the engine's stream) and
+ * returns without synchronising: the caller reads the logits after its own
+ * stream synchronisation. Same computation as clef_engine_prefill. */
+int clef_engine_prefill_device(clef_engine* e, const int32_t* ids_device, const int64_t* offsets,
+                               int32_t nseq, const clef_prefix* initial, float* logits_device,
+                               void* stream);
+
+/* Number of kernels the engine has issued in prefill calls so far. */
+int64_t clef_engine_launches(const clef_engine* e);
+
 /* Requests cooperative cancellation; checked between layers
  * (Control::check, crates/core/src/models/mod.rs:44-59). */
 int clef_engine_cancel(clef_engine* e, int32_t cancel);

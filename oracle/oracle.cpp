@@ -636,11 +636,15 @@ int oracle_model_set_weight(void* mp, const char* name, const float* data, int64
   int64_t n = 1;
   for (auto s : it->second.shape) n *= s;
   if (n != count) return fail(std::string("shape mismatch for ") + name);
-  it->second.data.assign(data, data + count);
   it->second.present = true;
-  if (it->second.projection)
-    pack_weight(it->second.data.data(), it->second.shape[0], it->second.shape[1],
-                it->second.packed);
+  if (it->second.projection) {
+    // Projections are only read through the packed panels; keep no second copy.
+    pack_weight(data, it->second.shape[0], it->second.shape[1], it->second.packed);
+    it->second.data.clear();
+    it->second.data.shrink_to_fit();
+  } else {
+    it->second.data.assign(data, data + count);
+  }
   return 0;
 }
 int64_t oracle_model_weight_count(void* mp, const char* name) {

@@ -177,14 +177,10 @@ int build_layout(clef_engine* e) {
   // One device blob: fused BF16 matrices (with zero padding rows), then F32
   // tensors and the effective offset-norm weights.
   size_t bytes = 0;
-  std::vector<std::pair<std::string, size_t>> place;  // name -> offset
   auto reserve = [&](size_t n) {
     const size_t off = bytes;
     bytes = a256(bytes + n);
     return off;
-  };
-  struct Fused {
-    size_t off;
   };
   std::vector<size_t> in_off(c.num_hidden_layers), att_off(c.num_hidden_layers);
   for (int i = 0; i < c.num_hidden_layers; ++i) {
@@ -204,7 +200,12 @@ int build_layout(clef_engine* e) {
   const size_t inv_off = reserve(sizeof(float) * 128);
   if (cudaMalloc(&e->wblob, bytes) != cudaSuccess)
     return fail(CLEF_ERR_NOMEM, "engine: weight allocation of " + std::to_string(bytes) + " bytes");
-  if (cudaMemset(e->wblob, 0, bytes) != cudaSuccess) return fail(CLEF_ERR_CUDA, "engine: memset");
+  // Zero padding rows. The memset is ordered on the engine's (non-blocking)
+  // stream and completed here: a legacy-stream cudaMemset could still be
+  // running when the first weights are written on the engine's stream.
+  if (cudaMemsetAsync(e->wblob, 0, bytes, e->stream) != cudaSuccess ||
+      cudaStreamSynchronize(e->stream) != cudaSuccess)
+    return fail(CLEF_ERR_CUDA, "engine: memset");
   char* base = reinterpret_cast<char*>(e->wblob);
   for (auto& kv : e->tensors) {
     auto it = off.find(kv.first);
@@ -418,6 +419,17 @@ int alloc_prefix(clef_engine* e, int64_t tokens, clef_prefix** out) {
   p->bytes = logical;
   *out = p;
   return CLEF_OK;
+}
+
+// Adds the elapsed time of every recorded (start, end) event pair to its
+// stage; the events must have completed (the caller synchronised).
+void collect_stage_times(clef_engine* e) {
+  for (auto& x : e->ev_used) {
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, e->ev_pool[x.second], e->ev_pool[x.second + 1]) == cudaSuccess)
+      e->stage_ms[x.first] += ms;
+  }
+  e->ev_used.clear();
 }
 
 // One pack of whole sequences [s0, s1).
@@ -779,7 +791,6 @@ int clef_engine_prefill(clef_engine* e, const int32_t* ids, const int64_t* offse
   }
   if (captured) *captured = nullptr;
   DeviceGuard g(e->device);
-  e->ev_used.clear();
   clef_prefix* cap = nullptr;
   if (capture) RC(alloc_prefix(e, capture, &cap));
   int64_t row0 = 0;
@@ -807,13 +818,7 @@ int clef_engine_prefill(clef_engine* e, const int32_t* ids, const int64_t* offse
     if (derc) rc = derc;
     else if (dev_err) rc = fail(CLEF_ERR_DEVICE_TIMEOUT, "prefill: a device-side wait timed out");
   }
-  if (e->profiling && rc == CLEF_OK) {
-    for (auto& x : e->ev_used) {
-      float ms = 0.f;
-      cudaEventElapsedTime(&ms, e->ev_pool[x.second], e->ev_pool[x.second + 1]);
-      e->stage_ms[x.first] += ms;
-    }
-  }
+  if (rc == CLEF_OK) collect_stage_times(e);
   if (rc != CLEF_OK) {
     if (cap) clef_prefix_destroy(cap);
     return rc;
@@ -838,7 +843,6 @@ int clef_engine_prefill_device(clef_engine* e, const int32_t* ids_device, const 
                    (int)initial->layers.size() == e->cfg.num_hidden_layers,
                CLEF_ERR_INVALID, "prefill_device: prefix state does not match this engine");
   DeviceGuard g(e->device);
-  e->ev_used.clear();
   cudaStream_t user = as_stream(stream);
   cudaStream_t own = e->stream;
   e->stream = user ? user : own;
@@ -864,13 +868,23 @@ int clef_engine_cancel(clef_engine* e, int32_t cancel) {
 
 int clef_engine_set_profiling(clef_engine* e, int32_t enabled) {
   CLEF_CHECK(e, CLEF_ERR_INVALID, "set_profiling: null engine");
+  if (!e->ev_used.empty()) {
+    DeviceGuard g(e->device);
+    CLEF_CUDA(cudaDeviceSynchronize());
+    e->ev_used.clear();
+  }
   e->profiling = enabled != 0;
   for (auto& x : e->stage_ms) x = 0.f;
   return CLEF_OK;
 }
 
-int clef_engine_stage_times(const clef_engine* e, float* ms, int32_t n) {
+int clef_engine_stage_times(clef_engine* e, float* ms, int32_t n) {
   if (!e || !ms) return 0;
+  if (!e->ev_used.empty()) {
+    DeviceGuard g(e->device);
+    cudaDeviceSynchronize();
+    collect_stage_times(e);
+  }
   const int k = std::min<int>(n, kStages);
   for (int i = 0; i < k; ++i) ms[i] = e->stage_ms[i];
   return k;

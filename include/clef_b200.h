@@ -238,10 +238,12 @@ int64_t clef_engine_launches(const clef_engine* e);
  * (Control::check, crates/core/src/models/mod.rs:44-59). */
 int clef_engine_cancel(clef_engine* e, int32_t cancel);
 
-/* Per-stage device milliseconds of the last prefill (CUDA events), written
- * into `ms` [n] in the order: embed, norm, gemm, delta_prologue, delta_scan,
- * delta_epilogue, attention_prologue, attention, head. Returns the count. */
-int clef_engine_stage_times(const clef_engine* e, float* ms, int32_t n);
+/* Per-stage device milliseconds accumulated (CUDA events) since profiling was
+ * last enabled, written into `ms` [n] in the order: embed, norm, gemm,
+ * delta_prologue, delta_scan, delta_epilogue, attention_prologue, attention,
+ * head. Synchronises the device if stream-ordered prefills are pending.
+ * Returns the count written. */
+int clef_engine_stage_times(clef_engine* e, float* ms, int32_t n);
 int clef_engine_set_profiling(clef_engine* e, int32_t enabled);
 
 int clef_engine_destroy(clef_engine* e);

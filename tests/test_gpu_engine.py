@@ -141,3 +141,24 @@ def test_cancel_between_layers(models):
     eng.cancel(False)
     lg, _, _ = eng.prefill([ids(10, 5)])
     assert np.isfinite(lg).all()
+
+
+def test_every_tensor_initialised_on_a_large_model():
+    """A 3 GB weight blob (full vocabulary, two attention layers): every tensor
+    holds its seeded values and the head reads them (regression: the zeroing
+    of the blob must be ordered before the first weight write)."""
+    import clef_b200 as cb
+    from clef_b200.config import weight_shapes
+    cfg = benchmark_config(layers=8, head_outputs=7)
+    eng = cb.Engine(cfg, 0)
+    eng.init_random(3, 0.02)
+    eng.finalize()
+    for name in weight_shapes(cfg):
+        if "embed_tokens" in name:
+            continue
+        assert np.abs(eng.get_weight(name)).max() > 0, name
+    seq = np.random.default_rng(0).integers(0, cfg.vocab_size, 300).astype(np.int32)
+    lg, hid, _ = eng.prefill([seq], hidden=True)
+    w = eng.get_weight("clef.head.weight").reshape(7, cfg.hidden_size)
+    assert np.abs(lg[0] - w @ hid[-1]).max() <= 1e-4
+    eng.close()

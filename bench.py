@@ -49,6 +49,10 @@ def parse():
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-tokens", type=int, default=256)
+    ap.add_argument("--profile-op", default=None,
+                    choices=["gemm", "gemm_swiglu", "scan", "scan1", "attention", "prologue"],
+                    help="run one operator on a profiling-sized case and exit (for ncu)")
+    ap.add_argument("--reps", type=int, default=3)
     return ap.parse_args()
 
 
@@ -227,10 +231,62 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # Our arm.
 # ---------------------------------------------------------------------------
+def profile_op(args):
+    """One operator on a case larger than L2 but a few GB at most: the inputs
+    ncu captures (profiles/*.md give the command lines)."""
+    import torch
+
+    import clef_b200 as cb
+    from clef_b200 import workloads
+    torch.manual_seed(0)
+    dev = "cuda"
+    if args.profile_op in ("gemm", "gemm_swiglu"):
+        M, K, N = 8192, 2560, 9216
+        x = torch.randn(M, K, device=dev).bfloat16()
+        w = (0.02 * torch.randn(N, K, device=dev)).bfloat16()
+        w2 = (0.02 * torch.randn(N, K, device=dev)).bfloat16()
+        out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        for _ in range(args.reps):
+            if args.profile_op == "gemm":
+                cb.gemm(x, w, out=out)
+            else:
+                cb.gemm_swiglu(x, w, w2, out=out)
+    elif args.profile_op in ("scan", "scan1"):
+        T, cu = (65536, np.arange(0, 65537, 1024, dtype=np.int64)) if args.profile_op == "scan" \
+            else (1024, None)
+        inp = workloads.delta_operator_inputs(T=T, seed=1)
+        qs, ks = workloads.scan_operands(inp)
+        t = {k: torch.from_numpy(np.ascontiguousarray(v)).cuda()
+             for k, v in dict(q=qs, k=ks, v=inp["v"], g=inp["g"], b=inp["beta"]).items()}
+        for _ in range(args.reps):
+            cb.delta_scan(t["q"], t["k"], t["v"], t["g"], t["b"], cu_seqlens=cu)
+    elif args.profile_op == "attention":
+        T = 4096
+        q = torch.randn(16, T, 256, device=dev).bfloat16()
+        k = torch.randn(4, T, 256, device=dev).bfloat16()
+        v = torch.randn(4, T, 256, device=dev).bfloat16()
+        for _ in range(args.reps):
+            cb.attention_gqa(q, k, v)
+    elif args.profile_op == "prologue":
+        T, Hk, Hv = 16384, 16, 32
+        width = 2 * Hk * 128 + Hv * 128
+        ldp = width + Hv * 128 + 2 * Hv
+        proj = torch.randn(T, ldp, device=dev)
+        conv = 0.3 * torch.randn(width, 4, device=dev)
+        dt, alog = 0.1 * torch.randn(Hv, device=dev), torch.rand(Hv, device=dev) * 2.7
+        for _ in range(args.reps):
+            cb.delta_prologue(proj, width + Hv * 128, width + Hv * 128 + Hv, conv, dt, alog, Hk, Hv)
+    torch.cuda.synchronize()
+    print(f"profile-op {args.profile_op}: ok", flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.profile_op:
+        return profile_op(args)
     import torch
     import torch.distributed as dist
 

@@ -102,7 +102,8 @@ def test_gemm_config2_sweep(M, shape):
     print(f"M={M} {shape}: rel {err / scale:.2e}")
     assert err <= 2e-5 * scale
     yb = cb.gemm(x, w, epilogue=cb.EPI_BF16).float()
-    assert ((yb - ref).abs() <= ref.abs() * 2 ** -7 + 1e-6 * scale).all()
+    # BF16 rounding of a result that is itself within the F32 bound above.
+    assert ((yb - ref).abs() <= ref.abs() * 2 ** -7 + 2e-5 * scale).all()
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 256, 64), (127, 272, 128), (129, 1040, 2560), (1000, 32, 256),

@@ -389,7 +389,7 @@ def main():
     achieved = lin_flops / (gemm_ms / 1000.0) / 1e12
     peak = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")))
     traffic = None
-    tf = ROOT / "profiles" / "gemm_traffic.json"
+    tf = ROOT / "profiles" / "gemm_traffic.txt"
     if tf.exists():
         traffic = json.loads(tf.read_text()).get("bytes_per_launch")
     roofline = {"bound": "tensor", "kernel": "gemm_kernel (tcgen05 projection GEMMs, all launches)",

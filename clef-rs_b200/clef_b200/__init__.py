@@ -29,7 +29,8 @@ STAGES = ["embed", "norm", "gemm", "delta_prologue", "delta_scan", "delta_epilog
 # Every symbol include/clef_b200.h declares.
 EXPORTS = [
     "clef_last_error", "clef_version", "clef_config_validate", "clef_rmsnorm", "clef_conv4",
-    "clef_delta_prologue", "clef_delta_scan_workspace_size", "clef_delta_scan", "clef_gemm_bf16",
+    "clef_delta_prologue", "clef_delta_scan_workspace_size", "clef_delta_scan",
+    "clef_delta_scan_noalloc", "clef_gemm_bf16",
     "clef_gemm_swiglu", "clef_attention_gqa", "clef_compact_copy", "clef_engine_create",
     "clef_engine_set_weight", "clef_engine_init_random", "clef_engine_get_weight",
     "clef_engine_weight_count", "clef_engine_finalize", "clef_engine_prefill",
@@ -68,6 +69,8 @@ def _load():
         "clef_delta_scan_workspace_size": (_sz, [_i64, _i32, _i32, _i32, _i32]),
         "clef_delta_scan": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _vp,
                                            _i32, _vp, _i32, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
+        "clef_delta_scan_noalloc": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32,
+                                                   _vp, _i32, _vp, _i32, _i64, _vp, _vp, _vp, _vp]),
         "clef_gemm_bf16": (ctypes.c_int, [_vp, _vp, _i64, _i32, _i32, _i32, _vp, _i64, _vp]),
         "clef_gemm_swiglu": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i32, _i32, _vp, _vp]),
         "clef_attention_gqa": (ctypes.c_int, [_vp, _vp, _vp, _i32, _i32, _i64, _i64, _i32, _vp, _vp]),

@@ -583,6 +583,46 @@ int launch_delta_scan(const float* q, const float* k, const float* v, const floa
                                capture, capture_state, final_state, out, s);
 }
 
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of clef_delta_scan.
+//
+// Some callers cannot call cudaMalloc or hand this library a workspace: hosts
+// whose allocator owns every byte of device memory and whose op signature has
+// no room for an extra buffer (a Candle/cudarc custom op gets its inputs and
+// outputs and nothing else), and latency-critical serving loops that must not
+// hit cudaMalloc's implicit device synchronisation. For them the per-sequence
+// offsets table, the only scratch the scan needs, lives in a fixed
+// device-resident array of this library instead of a caller workspace.
+// ---------------------------------------------------------------------------
+constexpr int kNoAllocMaxSeqs = 4096;  // 4097 int64 offsets = 32,776 bytes per device
+
+// Loaded with the library on every device that uses it and kept until the
+// process exits. In host code this name is only a stand-in for the device
+// array: the device address comes from cudaGetSymbolAddress below.
+static __device__ __align__(256) int64_t g_noalloc_offsets[kNoAllocMaxSeqs + 1];
+
+namespace {
+// Device address of g_noalloc_offsets, resolved once per device with that
+// device current (the first call on a device does this set-up).
+int noalloc_offsets_ptr(int64_t** out) {
+  static int64_t* ptrs[64] = {nullptr};
+  int dev = 0;
+  CLEF_CUDA(cudaGetDevice(&dev));
+  CLEF_CHECK(dev >= 0 && dev < 64, CLEF_ERR_UNSUPPORTED, "delta_scan_noalloc: device index >= 64");
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_offsets);
+    if (e != cudaSuccess || !p)
+      return fail(CLEF_ERR_CUDA, std::string("delta_scan_noalloc: cudaGetSymbolAddress: ") +
+                                     cudaGetErrorString(e));
+    ptrs[dev] = reinterpret_cast<int64_t*>(p);
+  }
+  *out = ptrs[dev];
+  return CLEF_OK;
+}
+}  // namespace
+
 }  // namespace clef
 
 using namespace clef;
@@ -634,6 +674,63 @@ int clef_delta_scan(const float* q, const float* k, const float* v, const float*
   return launch_delta_scan(q, k, v, g, beta, cu.data(), nseq, Hk, Hv, dk, dv, init_state,
                            init_shared, capture, capture_state, final_state, out, workspace,
                            workspace_bytes, as_stream(stream));
+}
+
+// Same contract and results as clef_delta_scan, without a workspace: the
+// sequence offsets are copied into the library's fixed device array (at most
+// 4096 sequences). It allocates nothing. The first call on each device looks
+// up the array's device address and should come before any stream capture.
+// Every call shares the one array per device, and each call rewrites the
+// entries [0, nseq] it uses before its kernel reads them (nothing else needs
+// to start at zero); calls whose work overlaps on the GPU (different streams,
+// or host threads issuing concurrently on one device) race on it, so callers
+// serialise them on one stream.
+int clef_delta_scan_noalloc(const float* q, const float* k, const float* v, const float* g,
+                            const float* beta, int64_t T, int32_t Hk, int32_t Hv, int32_t dk,
+                            int32_t dv, const int64_t* cu_seqlens, int32_t nseq,
+                            const float* init_state, int32_t init_shared, int64_t capture,
+                            float* capture_state, float* final_state, float* out, void* stream) {
+  CLEF_CHECK(q && k && v && g && beta && out, CLEF_ERR_INVALID, "delta_scan_noalloc: null pointer");
+  CLEF_CHECK(dk == 128 && dv == 128, CLEF_ERR_UNSUPPORTED,
+             "delta_scan_noalloc: dk and dv must be 128");
+  CLEF_CHECK(Hk > 0 && Hv > 0 && Hv % Hk == 0 && Hv <= 4096, CLEF_ERR_INVALID,
+             "delta_scan_noalloc: head counts");
+  CLEF_CHECK(T > 0, CLEF_ERR_INVALID, "delta_scan_noalloc: T must be positive");
+  if (cu_seqlens) {
+    CLEF_CHECK(nseq > 0, CLEF_ERR_INVALID, "delta_scan_noalloc: nseq");
+    CLEF_CHECK(nseq <= kNoAllocMaxSeqs, CLEF_ERR_UNSUPPORTED,
+               "delta_scan_noalloc: at most 4096 sequences per call (fixed offsets array); "
+               "use clef_delta_scan with a workspace for more");
+    CLEF_CHECK(cu_seqlens[0] == 0 && cu_seqlens[nseq] == T, CLEF_ERR_INVALID,
+               "delta_scan_noalloc: cu_seqlens range");
+    for (int i = 0; i < nseq; ++i)
+      CLEF_CHECK(cu_seqlens[i + 1] > cu_seqlens[i], CLEF_ERR_INVALID,
+                 "delta_scan_noalloc: empty or unordered sequence");
+  } else {
+    CLEF_CHECK(nseq == 1 || nseq == 0, CLEF_ERR_INVALID,
+               "delta_scan_noalloc: nseq without cu_seqlens");
+    nseq = 1;
+  }
+  CLEF_CHECK(capture >= 0, CLEF_ERR_INVALID, "delta_scan_noalloc: capture");
+  if (capture > 0) {
+    CLEF_CHECK(nseq == 1, CLEF_ERR_INVALID, "delta_scan_noalloc: capture needs a single sequence");
+    CLEF_CHECK(capture <= T && capture_state, CLEF_ERR_INVALID,
+               "delta_scan_noalloc: capture boundary or capture_state");
+  }
+  CLEF_CHECK(((uintptr_t)q | (uintptr_t)k) % 16 == 0, CLEF_ERR_INVALID,
+             "delta_scan_noalloc: q and k must be 16-byte aligned");
+  cudaStream_t s = as_stream(stream);
+  const int64_t* cu_dev = nullptr;
+  if (nseq > 1) {
+    int64_t* table = nullptr;
+    int rc = noalloc_offsets_ptr(&table);
+    if (rc) return rc;
+    CLEF_CUDA(cudaMemcpyAsync(table, cu_seqlens, sizeof(int64_t) * (nseq + 1),
+                              cudaMemcpyHostToDevice, s));
+    cu_dev = table;
+  }
+  return launch_delta_scan_dev(q, k, v, g, beta, cu_dev, T, nseq, Hk, Hv, init_state, init_shared,
+                               capture, capture_state, final_state, out, s);
 }
 
 }  // extern "C"

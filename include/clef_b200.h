@@ -143,6 +143,23 @@ int clef_delta_scan(const float* q, const float* k, const float* v, const float*
                     float* capture_state, float* final_state, float* out,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of clef_delta_scan (no counterpart in the
+ * reference). Some callers cannot call cudaMalloc or pass a workspace: hosts
+ * whose allocator owns all device memory behind an op signature with no
+ * room for an extra buffer, and latency-critical loops that must not hit
+ * cudaMalloc's implicit synchronisation. Same arguments and results as
+ * clef_delta_scan minus the workspace; the per-sequence offsets go into a
+ * fixed device array inside this library (at most 4096 sequences per call;
+ * more is rejected with CLEF_ERR_UNSUPPORTED). It allocates nothing. The
+ * first call on each device resolves the array's device address and should
+ * come before any stream capture. All calls on a device share the array:
+ * calls whose work overlaps on the GPU race, so serialise them on one stream. */
+int clef_delta_scan_noalloc(const float* q, const float* k, const float* v, const float* g,
+                            const float* beta, int64_t T, int32_t Hk, int32_t Hv, int32_t dk,
+                            int32_t dv, const int64_t* cu_seqlens, int32_t nseq,
+                            const float* init_state, int32_t init_shared, int64_t capture,
+                            float* capture_state, float* final_state, float* out, void* stream);
+
 /* GEMM epilogues for clef_gemm_bf16. */
 typedef enum clef_epilogue {
   CLEF_EPI_STORE_BF16 = 0,  /* out BF16 [M, ldo] = X W^T                    */

@@ -1,0 +1,80 @@
+"""The allocation-free scan entry point, checked against the workspace one.
+
+clef_delta_scan_noalloc serves callers that cannot allocate device memory or
+pass a workspace (an allocator that owns all device memory behind a fixed op
+signature, or a latency-critical loop that must avoid cudaMalloc's implicit
+synchronisation): the per-sequence offsets live in a fixed device array inside
+the library instead. Both entry points run the same kernel, so the outputs are
+compared bit for bit, on two calls in a row with different packings (the
+second call must not see the first call's offsets).
+
+This file is collected last on purpose; it needs nothing from the others and
+also passes alone in a fresh process.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+from clef_b200 import workloads
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def _p(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def scan_both(inp, cu, final=True):
+    import clef_b200 as cb
+    qs, ks = workloads.scan_operands(inp)
+    t = {k: torch.from_numpy(np.ascontiguousarray(v)).cuda()
+         for k, v in dict(q=qs, k=ks, v=inp["v"], g=inp["g"], b=inp["beta"]).items()}
+    T, Hk, _ = qs.shape
+    Hv = inp["v"].shape[1]
+    nseq = len(cu) - 1
+    cu = np.ascontiguousarray(cu, np.int64)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    outs = []
+    for fn in ("clef_delta_scan", "clef_delta_scan_noalloc"):
+        out = torch.empty((T, Hv, 128), dtype=torch.float32, device="cuda")
+        fin = torch.empty((nseq, Hv, 128, 128), dtype=torch.float32, device="cuda") if final else None
+        args = [_p(t["q"]), _p(t["k"]), _p(t["v"]), _p(t["g"]), _p(t["b"]), T, Hk, Hv, 128, 128,
+                cu.ctypes.data, nseq, None, 0, 0, None, _p(fin), _p(out)]
+        if fn == "clef_delta_scan":
+            size = cb.delta_scan_workspace_size(T, nseq, Hv)
+            ws = torch.empty(size, dtype=torch.uint8, device="cuda")
+            rc = cb.lib.clef_delta_scan(*args, _p(ws), size, stream)
+        else:
+            rc = cb.lib.clef_delta_scan_noalloc(*args, stream)
+        assert rc == 0, cb.lib.clef_last_error().decode()
+        torch.cuda.synchronize()
+        outs.append((out.cpu().numpy(), None if fin is None else fin.cpu().numpy()))
+    return outs
+
+
+def test_noalloc_scan_matches_workspace_scan_on_two_calls_in_a_row():
+    first = workloads.delta_operator_inputs(T=700, seed=21)
+    (o_ws, f_ws), (o_na, f_na) = scan_both(first, [0, 1, 65, 200, 700])
+    assert np.isfinite(o_na).all()
+    assert np.array_equal(o_na, o_ws) and np.array_equal(f_na, f_ws)
+    # Second call, different packing and more sequences: the shared array is
+    # rewritten for every entry the kernel reads.
+    second = workloads.delta_operator_inputs(T=1000, seed=22)
+    (o_ws, f_ws), (o_na, f_na) = scan_both(second, [0, 300, 301, 450, 640, 999, 1000])
+    assert np.array_equal(o_na, o_ws) and np.array_equal(f_na, f_ws)
+
+
+def test_noalloc_scan_single_sequence_and_size_limit():
+    import clef_b200 as cb
+    inp = workloads.delta_operator_inputs(T=257, seed=23)
+    (o_ws, f_ws), (o_na, f_na) = scan_both(inp, [0, 257])
+    assert np.array_equal(o_na, o_ws) and np.array_equal(f_na, f_ws)
+    # More sequences than the fixed array holds: rejected before any launch.
+    cu = np.arange(0, 4098, dtype=np.int64)
+    fake = ctypes.c_void_p(0x10000)
+    rc = cb.lib.clef_delta_scan_noalloc(fake, fake, fake, fake, fake, 4097, 16, 32, 128, 128,
+                                        cu.ctypes.data, 4097, None, 0, 0, None, None, fake, None)
+    assert rc == 3 and "4096" in cb.lib.clef_last_error().decode()

@@ -66,7 +66,7 @@ def _load():
         "clef_conv4": (ctypes.c_int, [_vp, _i64, _vp, _i32, _vp, _i64, _i32, _vp, _vp]),
         "clef_delta_prologue": (ctypes.c_int, [_vp, _i64, _i32, _i32, _vp, _i32, _vp, _vp, _vp, _i64,
                                                _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp]),
-        "clef_delta_scan_workspace_size": (_sz, [_i64, _i32, _i32, _i32, _i32]),
+        "clef_delta_scan_workspace_size": (_sz, [_i64, _i32, _i32, _i32, _i32, _i32]),
         "clef_delta_scan": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _vp,
                                            _i32, _vp, _i32, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
         "clef_delta_scan_noalloc": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32,
@@ -171,8 +171,8 @@ def delta_prologue(proj, a_col, b_col, conv_weight, dt_bias, a_log, Hk, Hv, dk=1
     return q, k, v, g, beta
 
 
-def delta_scan_workspace_size(total_tokens, nseq, Hv, dk=128, dv=128) -> int:
-    return int(lib.clef_delta_scan_workspace_size(total_tokens, nseq, Hv, dk, dv))
+def delta_scan_workspace_size(total_tokens, nseq, Hk, Hv, dk=128, dv=128) -> int:
+    return int(lib.clef_delta_scan_workspace_size(total_tokens, nseq, Hk, Hv, dk, dv))
 
 
 def delta_scan(q, k, v, g, beta, cu_seqlens=None, init_state=None, init_shared=False, capture=0,
@@ -194,7 +194,7 @@ def delta_scan(q, k, v, g, beta, cu_seqlens=None, init_state=None, init_shared=F
     cap = torch.empty((Hv, dk, dv), dtype=torch.float32, device=dev) if capture else None
     fin = torch.empty((nseq, Hv, dk, dv), dtype=torch.float32, device=dev) if final_state else None
     if workspace is None:
-        size = delta_scan_workspace_size(T, nseq, Hv, dk, dv)
+        size = delta_scan_workspace_size(T, nseq, Hk, Hv, dk, dv)
         workspace = torch.empty(size, dtype=torch.uint8, device=dev)
     _check(lib.clef_delta_scan(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), T, Hk, Hv, dk, dv,
                                cu_arr.ctypes.data if cu_arr is not None else None, nseq,

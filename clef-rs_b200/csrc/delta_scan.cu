@@ -31,9 +31,16 @@
 // A capture point inside a chunk does not change the chunking: the state at
 // the capture token is formed from the same chunk quantities, so a prefill with
 // capture is bit-identical to one without.
+#include <algorithm>
 #include <vector>
 
 #include "kernels.cuh"
+
+#define RC_(x)           \
+  do {                   \
+    int rc_ = (x);       \
+    if (rc_) return rc_; \
+  } while (0)
 
 namespace clef {
 
@@ -52,12 +59,13 @@ constexpr int OFF_KHI = 0;
 constexpr int OFF_KLO = OFF_KHI + KQ_BYTES;
 constexpr int OFF_QHI = OFF_KLO + KQ_BYTES;
 constexpr int OFF_QLO = OFF_QHI + KQ_BYTES;
-constexpr int OFF_PHI = OFF_QLO + KQ_BYTES;
-constexpr int OFF_PLO = OFF_PHI + SQ_BYTES;
-constexpr int OFF_THI = OFF_PLO + SQ_BYTES;
+// THI, TLO, PHI, PLO: the order carry_step reads them in (ChunkOps::tp).
+constexpr int OFF_THI = OFF_QLO + KQ_BYTES;
 constexpr int OFF_TLO = OFF_THI + SQ_BYTES;
+constexpr int OFF_PHI = OFF_TLO + SQ_BYTES;
+constexpr int OFF_PLO = OFF_PHI + SQ_BYTES;
 constexpr int AP = 65;                               // F32 pitch of A and T
-constexpr int OFF_A = OFF_TLO + SQ_BYTES;            // F32 [64][65]
+constexpr int OFF_A = OFF_PLO + SQ_BYTES;            // F32 [64][65]
 constexpr int OFF_T = OFF_A + C * AP * 4;            // F32 [64][65]
 constexpr int OFF_M = OFF_T + C * AP * 4;            // F32 [3][16][17] scratch
 constexpr int OFF_G = OFF_M + 3 * 16 * 17 * 4;       // double [64]
@@ -141,6 +149,397 @@ __device__ __forceinline__ void lda(uint32_t base, int m0, int k0, int cpr, int 
   ldsm4(base + swz(m0 + (lane & 15), k0 + (lane >> 4) * 8, cpr), r);
 }
 
+// ---------------------------------------------------------------------------
+// Building blocks shared by the fused kernel and the prep/carry pipeline, so
+// both paths perform the same arithmetic in the same order.
+// ---------------------------------------------------------------------------
+
+// Stores one 32-bit word at byte offset `o` of a tile, in shared or global
+// memory (the global "tile image" has the shared-memory layout byte for byte).
+template <bool GLOBAL>
+__device__ __forceinline__ void put32(uint8_t* base, uint32_t o, uint32_t v) {
+  *reinterpret_cast<uint32_t*>(base + o) = v;
+}
+
+// K, Q rows [t0, t0 + n) of k-head kh, split into hi/lo BF16 tiles (zero rows
+// past n). Writes the four tiles (KHI, KLO, QHI, QLO, 16 KB each) to `sm_kq`
+// and, when `img` is set, the same bytes to a global tile image.
+__device__ __forceinline__ void stage_kq(const float* __restrict__ q, const float* __restrict__ k,
+                                         int64_t t0, int n, int Hk, int kh, uint8_t* sm_kq,
+                                         uint8_t* img, int tid, int nthreads) {
+  for (int idx = tid; idx < C * (DK / 4); idx += nthreads) {
+    const int i = idx >> 5, c4 = (idx & 31) * 4;
+    float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), qv = kv;
+    if (i < n) {
+      const int64_t off = ((t0 + i) * Hk + kh) * DK + c4;
+      kv = *reinterpret_cast<const float4*>(k + off);
+      qv = *reinterpret_cast<const float4*>(q + off);
+    }
+    uint32_t kh0, kl0, kh1, kl1, qh0, ql0, qh1, ql1;
+    split2(kv.x, kv.y, kh0, kl0);
+    split2(kv.z, kv.w, kh1, kl1);
+    split2(qv.x, qv.y, qh0, ql0);
+    split2(qv.z, qv.w, qh1, ql1);
+    const uint32_t o = swz(i, c4, 16);
+    const uint2 w[4] = {make_uint2(kh0, kh1), make_uint2(kl0, kl1), make_uint2(qh0, qh1),
+                        make_uint2(ql0, ql1)};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      *reinterpret_cast<uint2*>(sm_kq + t * KQ_BYTES + o) = w[t];
+      if (img) *reinterpret_cast<uint2*>(img + t * KQ_BYTES + o) = w[t];
+    }
+  }
+}
+
+// Chunk-relative inclusive cumsum of g in FP64 and the betas (one warp).
+__device__ __forceinline__ void cumsum_gates(const float* __restrict__ g,
+                                             const float* __restrict__ beta, int64_t t0, int n,
+                                             int Hv, int h, int lane, double* Gs, float* bs) {
+  const int i0 = 2 * lane, i1 = i0 + 1;
+  const double g0 = i0 < n ? (double)g[(t0 + i0) * Hv + h] : 0.0;
+  const double g1 = i1 < n ? (double)g[(t0 + i1) * Hv + h] : 0.0;
+  const double pair = g0 + g1;
+  double run = pair;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double up = __shfl_up_sync(0xffffffffu, run, o);
+    if (lane >= o) run += up;
+  }
+  const double excl = run - pair;
+  Gs[i0] = excl + g0;
+  Gs[i1] = excl + g0 + g1;
+  bs[i0] = i0 < n ? beta[(t0 + i0) * Hv + h] : 0.f;
+  bs[i1] = i1 < n ? beta[(t0 + i1) * Hv + h] : 0.f;
+}
+
+// Raw Gram fragments of warp w: rows (w/2)*16.., columns (w%2)*32.. of K K^T
+// and Q K^T (8 warps cover 64 x 64).
+__device__ __forceinline__ void gram_mma(uint32_t kq_base, int warp, int lane, float (&kk)[4][4],
+                                         float (&qk)[4][4]) {
+  const int m0 = (warp >> 1) * 16, nb = (warp & 1) * 32;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) kk[j][e] = qk[j][e] = 0.f;
+#pragma unroll
+  for (int ks = 0; ks < DK / 16; ++ks) {
+    uint32_t akh[4], akl[4], aqh[4], aql[4];
+    lda(kq_base + 0 * KQ_BYTES, m0, ks * 16, 16, lane, akh);
+    lda(kq_base + 1 * KQ_BYTES, m0, ks * 16, 16, lane, akl);
+    lda(kq_base + 2 * KQ_BYTES, m0, ks * 16, 16, lane, aqh);
+    lda(kq_base + 3 * KQ_BYTES, m0, ks * 16, 16, lane, aql);
+#pragma unroll
+    for (int np = 0; np < 2; ++np) {
+      uint32_t bh[4], bl[4];
+      ldb_nk(kq_base + 0 * KQ_BYTES, nb + np * 16, ks * 16, 16, lane, bh);
+      ldb_nk(kq_base + 1 * KQ_BYTES, nb + np * 16, ks * 16, 16, lane, bl);
+      mma3(kk[2 * np], akh, akl, bh[0], bh[1], bl[0], bl[1]);
+      mma3(kk[2 * np + 1], akh, akl, bh[2], bh[3], bl[2], bl[3]);
+      mma3(qk[2 * np], aqh, aql, bh[0], bh[1], bl[0], bl[1]);
+      mma3(qk[2 * np + 1], aqh, aql, bh[2], bh[3], bl[2], bl[3]);
+    }
+  }
+}
+
+// A (F32, strictly lower, beta_i e^{G_i-G_j} k_i.k_j) into As and
+// P (lower incl. diagonal, e^{G_i-G_j} q_i.k_j) as hi/lo tiles at p_hi / p_lo.
+template <bool GLOBAL>
+__device__ __forceinline__ void gram_store(const float (&kk)[4][4], const float (&qk)[4][4],
+                                           int warp, int lane, int n, const double* Gs,
+                                           const float* bs, float* As, uint8_t* p_hi,
+                                           uint8_t* p_lo) {
+  const int m0 = (warp >> 1) * 16, nb = (warp & 1) * 32;
+  const int r0 = lane >> 2, c0 = 2 * (lane & 3);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+#pragma unroll
+    for (int e = 0; e < 4; e += 2) {
+      const int i = m0 + r0 + (e >> 1) * 8;
+      float pv[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int col = nb + j * 8 + c0 + u;
+        const bool lower = col <= i && i < n;
+        const float decay = lower ? expf((float)(Gs[i] - Gs[col])) : 0.f;
+        As[i * AP + col] = (lower && col < i) ? bs[i] * (decay * kk[j][e + u]) : 0.f;
+        pv[u] = lower ? decay * qk[j][e + u] : 0.f;
+      }
+      uint32_t ph, pl;
+      split2(pv[0], pv[1], ph, pl);
+      const uint32_t o = swz(i, nb + j * 8 + c0, 8);
+      put32<GLOBAL>(p_hi, o, ph);
+      put32<GLOBAL>(p_lo, o, pl);
+    }
+  }
+}
+
+// T = (I + A)^{-1} by blocked forward substitution in F32, then
+// T diag(beta) split into hi/lo tiles at t_hi / t_lo. Contains block barriers;
+// every thread of the CTA calls it.
+template <bool GLOBAL>
+__device__ __forceinline__ void solve_t(const float* As, float* Ts, float* Ms, const float* bs,
+                                        uint8_t* t_hi, uint8_t* t_lo, int tid, int warp, int lane,
+                                        int nthreads) {
+  // Diagonal 16 x 16 blocks: lane c of warp b solves column c of block b.
+  if (warp < 4 && lane < 16) {
+    const int b0 = warp * 16, c = lane;
+    float x[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      float acc = r == c ? 1.f : 0.f;
+#pragma unroll
+      for (int j = 0; j < r; ++j) acc -= As[(b0 + r) * AP + b0 + j] * x[j];
+      x[r] = r < c ? 0.f : acc;
+    }
+#pragma unroll
+    for (int r = 0; r < 16; ++r) Ts[(b0 + r) * AP + b0 + c] = x[r];
+  }
+  for (int idx = tid; idx < C * C; idx += nthreads) {  // upper blocks are zero
+    const int i = idx >> 6, j = idx & 63;
+    if ((j >> 4) > (i >> 4)) Ts[i * AP + j] = 0.f;
+  }
+  __syncthreads();
+  // Off-diagonal blocks, block row by block row:
+  //   T_bj = -D_b * sum_{k=j}^{b-1} A_bk T_kj.
+  for (int b = 1; b < 4; ++b) {
+    for (int idx = tid; idx < b * 256; idx += nthreads) {
+      const int j = idx >> 8, r = (idx >> 4) & 15, c = idx & 15;
+      float acc = 0.f;
+      for (int kb = j; kb < b; ++kb)
+#pragma unroll
+        for (int q = 0; q < 16; ++q)
+          acc += As[(b * 16 + r) * AP + kb * 16 + q] * Ts[(kb * 16 + q) * AP + j * 16 + c];
+      Ms[(j * 16 + r) * 17 + c] = acc;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < b * 256; idx += nthreads) {
+      const int j = idx >> 8, r = (idx >> 4) & 15, c = idx & 15;
+      float acc = 0.f;
+#pragma unroll
+      for (int q = 0; q <= 15; ++q)
+        acc += Ts[(b * 16 + r) * AP + b * 16 + q] * Ms[(j * 16 + q) * 17 + c];
+      Ts[(b * 16 + r) * AP + j * 16 + c] = -acc;
+    }
+    __syncthreads();
+  }
+  for (int idx = tid; idx < C * C / 2; idx += nthreads) {
+    const int i = idx >> 5, j = (idx & 31) * 2;
+    uint32_t th, tl;
+    split2(Ts[i * AP + j] * bs[j], Ts[i * AP + j + 1] * bs[j + 1], th, tl);
+    const uint32_t o = swz(i, j, 8);
+    put32<GLOBAL>(t_hi, o, th);
+    put32<GLOBAL>(t_lo, o, tl);
+  }
+}
+
+// Shared-memory addresses of one chunk's operands for the state products.
+struct ChunkOps {
+  uint32_t kq;  // KHI, KLO, QHI, QLO tiles (16 KB each)
+  uint32_t tp;  // THI, TLO, PHI, PLO tiles (8 KB each)
+  const float* eg;   // [64] e^{G}
+  const float* egd;  // [64] e^{G_last - G}
+  const double* G;   // [64] chunk-relative cumulative log-decay
+  float el;          // e^{G_last}
+};
+
+// One warp's share of a chunk: value rows [16w, 16w+16) of S^T.
+//   R^T = V^T - (S^T K^T) diag(e^G);  D^T = R^T (T diag(beta))^T
+//   O^T = (S^T Q^T) diag(e^G) + D^T P^T;  S^T <- e^{G_last} S^T + (D^T diag(e^{G_last-G})) K
+// Vr holds this thread's V^T fragment (token-major C layout) for the chunk.
+__device__ __forceinline__ void carry_step(float (&S)[16][4], const float (&Vr)[8][4],
+                                           const ChunkOps& c, int n, int64_t t0, int Hv, int h,
+                                           int warp, int lane, float* __restrict__ out, int cap_row,
+                                           float* __restrict__ capture_state) {
+  const int r0 = lane >> 2, c0 = 2 * (lane & 3);
+  const int dv0 = warp * 16;
+  float R[8][4];
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) R[nt][e] = 0.f;
+#pragma unroll
+  for (int ks = 0; ks < DK / 16; ++ks) {
+    uint32_t ah[4], al[4];
+    acc_to_a(S[2 * ks], S[2 * ks + 1], ah, al);
+#pragma unroll
+    for (int np = 0; np < 4; ++np) {
+      uint32_t bh[4], bl[4];
+      ldb_nk(c.kq + 0 * KQ_BYTES, np * 16, ks * 16, 16, lane, bh);
+      ldb_nk(c.kq + 1 * KQ_BYTES, np * 16, ks * 16, 16, lane, bl);
+      mma3(R[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
+      mma3(R[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+    }
+  }
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) R[nt][e] = Vr[nt][e] - c.eg[nt * 8 + c0 + (e & 1)] * R[nt][e];
+  float D[8][4];
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) D[nt][e] = 0.f;
+#pragma unroll
+  for (int ks = 0; ks < C / 16; ++ks) {
+    uint32_t ah[4], al[4];
+    acc_to_a(R[2 * ks], R[2 * ks + 1], ah, al);
+#pragma unroll
+    for (int np = 0; np < 4; ++np) {
+      uint32_t bh[4], bl[4];
+      ldb_nk(c.tp + 0 * SQ_BYTES, np * 16, ks * 16, 8, lane, bh);
+      ldb_nk(c.tp + 1 * SQ_BYTES, np * 16, ks * 16, 8, lane, bl);
+      mma3(D[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
+      mma3(D[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+    }
+  }
+  // O^T (R's registers are reused).
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) R[nt][e] = 0.f;
+#pragma unroll
+  for (int ks = 0; ks < DK / 16; ++ks) {
+    uint32_t ah[4], al[4];
+    acc_to_a(S[2 * ks], S[2 * ks + 1], ah, al);
+#pragma unroll
+    for (int np = 0; np < 4; ++np) {
+      uint32_t bh[4], bl[4];
+      ldb_nk(c.kq + 2 * KQ_BYTES, np * 16, ks * 16, 16, lane, bh);
+      ldb_nk(c.kq + 3 * KQ_BYTES, np * 16, ks * 16, 16, lane, bl);
+      mma3(R[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
+      mma3(R[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+    }
+  }
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) R[nt][e] *= c.eg[nt * 8 + c0 + (e & 1)];
+#pragma unroll
+  for (int ks = 0; ks < C / 16; ++ks) {
+    uint32_t ah[4], al[4];
+    acc_to_a(D[2 * ks], D[2 * ks + 1], ah, al);
+#pragma unroll
+    for (int np = 0; np < 4; ++np) {
+      uint32_t bh[4], bl[4];
+      ldb_nk(c.tp + 2 * SQ_BYTES, np * 16, ks * 16, 8, lane, bh);
+      ldb_nk(c.tp + 3 * SQ_BYTES, np * 16, ks * 16, 8, lane, bl);
+      mma3(R[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
+      mma3(R[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+    }
+  }
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int tok = nt * 8 + c0 + (e & 1);
+      const int dv = dv0 + r0 + (e >> 1) * 8;
+      if (tok < n) out[((t0 + tok) * Hv + h) * DV + dv] = R[nt][e];
+    }
+  }
+  // Capture: S_c^T = e^{G_c} S^T + (D^T diag(e^{G_c - G} [j <= c])) K.
+  if (cap_row >= 0) {
+    const float ec = expf((float)c.G[cap_row]);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      float X[8][4];
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) X[nt][e] = ec * S[half * 8 + nt][e];
+#pragma unroll
+      for (int ks = 0; ks < C / 16; ++ks) {
+        float d0[4], d1[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int j0 = ks * 16 + c0 + (e & 1), j1 = j0 + 8;
+          d0[e] = D[2 * ks][e] * (j0 <= cap_row ? expf((float)(c.G[cap_row] - c.G[j0])) : 0.f);
+          d1[e] = D[2 * ks + 1][e] * (j1 <= cap_row ? expf((float)(c.G[cap_row] - c.G[j1])) : 0.f);
+        }
+        uint32_t ah[4], al[4];
+        acc_to_a(d0, d1, ah, al);
+#pragma unroll
+        for (int np = 0; np < 4; ++np) {
+          uint32_t bh[4], bl[4];
+          ldb_kn(c.kq + 0 * KQ_BYTES, half * 64 + np * 16, ks * 16, 16, lane, bh);
+          ldb_kn(c.kq + 1 * KQ_BYTES, half * 64 + np * 16, ks * 16, 16, lane, bl);
+          mma3(X[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
+          mma3(X[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int dv = dv0 + r0 + (e >> 1) * 8;
+          const int dk = (half * 8 + nt) * 8 + c0 + (e & 1);
+          capture_state[((int64_t)h * DK + dk) * DV + dv] = X[nt][e];
+        }
+    }
+  }
+  // State update.
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) S[nt][e] *= c.el;
+#pragma unroll
+  for (int ks = 0; ks < C / 16; ++ks) {
+    float d0[4], d1[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      d0[e] = D[2 * ks][e] * c.egd[ks * 16 + c0 + (e & 1)];
+      d1[e] = D[2 * ks + 1][e] * c.egd[ks * 16 + 8 + c0 + (e & 1)];
+    }
+    uint32_t ah[4], al[4];
+    acc_to_a(d0, d1, ah, al);
+#pragma unroll
+    for (int np = 0; np < 8; ++np) {
+      uint32_t bh[4], bl[4];
+      ldb_kn(c.kq + 0 * KQ_BYTES, np * 16, ks * 16, 16, lane, bh);
+      ldb_kn(c.kq + 1 * KQ_BYTES, np * 16, ks * 16, 16, lane, bl);
+      mma3(S[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
+      mma3(S[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+    }
+  }
+}
+
+// This thread's V^T fragment of a chunk (zero past n).
+__device__ __forceinline__ void load_v(const float* __restrict__ v, int64_t t0, int n, int Hv, int h,
+                                       int warp, int lane, float (&Vr)[8][4]) {
+  const int r0 = lane >> 2, c0 = 2 * (lane & 3);
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int tok = nt * 8 + c0 + (e & 1);
+      const int dv = warp * 16 + r0 + (e >> 1) * 8;
+      Vr[nt][e] = tok < n ? v[((t0 + tok) * Hv + h) * DV + dv] : 0.f;
+    }
+}
+
+__device__ __forceinline__ void load_state(float (&S)[16][4], const float* init, int warp, int lane) {
+  const int r0 = lane >> 2, c0 = 2 * (lane & 3);
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int dv = warp * 16 + r0 + (e >> 1) * 8;
+      const int dk = nt * 8 + c0 + (e & 1);
+      S[nt][e] = init ? init[(int64_t)dk * DV + dv] : 0.f;
+    }
+}
+
+__device__ __forceinline__ void store_state(const float (&S)[16][4], float* dst, int warp, int lane) {
+  const int r0 = lane >> 2, c0 = 2 * (lane & 3);
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int dv = warp * 16 + r0 + (e >> 1) * 8;
+      const int dk = nt * 8 + c0 + (e & 1);
+      dst[(int64_t)dk * DV + dv] = S[nt][e];
+    }
+}
+
 struct ScanArgs {
   const float* q;  // [T, Hk, 128] normalised, scaled
   const float* k;  // [T, Hk, 128] normalised
@@ -158,6 +557,15 @@ struct ScanArgs {
   float* out;            // [T, Hv, 128]
 };
 
+__device__ __forceinline__ const float* init_for(const ScanArgs& a, int s, int h) {
+  return a.init ? a.init + (a.init_shared ? 0 : (int64_t)s * a.Hv * DK * DV) + (int64_t)h * DK * DV
+                : nullptr;
+}
+
+// ---------------------------------------------------------------------------
+// Fused single-pass kernel: one CTA per (sequence, v-head) does every stage of
+// every chunk itself. Needs no workspace beyond the sequence offsets.
+// ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(THREADS, 1) delta_scan_kernel(ScanArgs a) {
   extern __shared__ __align__(128) uint8_t sm[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -174,377 +582,301 @@ __global__ void __launch_bounds__(THREADS, 1) delta_scan_kernel(ScanArgs a) {
   float* eg = reinterpret_cast<float*>(sm + OFF_EG);
   float* egd = reinterpret_cast<float*>(sm + OFF_EGD);
   float* bs = reinterpret_cast<float*>(sm + OFF_BETA);
-  float* ecap = reinterpret_cast<float*>(sm + OFF_ECAP);
 
-  // S^T rows [16w, 16w+16) (value columns) x 128 key columns: 16 n-tiles.
-  const int r0 = lane >> 2, c0 = 2 * (lane & 3);
-  const int dv0 = warp * 16;
   float S[16][4];
-  {
-    const float* init = a.init ? a.init + (a.init_shared ? 0 : (int64_t)s * a.Hv * DK * DV) +
-                                     (int64_t)h * DK * DV
-                               : nullptr;
-#pragma unroll
-    for (int nt = 0; nt < 16; ++nt) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int dv = dv0 + r0 + (e >> 1) * 8;
-        const int dk = nt * 8 + c0 + (e & 1);
-        S[nt][e] = init ? init[(int64_t)dk * DV + dv] : 0.f;
-      }
-    }
-  }
-
+  load_state(S, init_for(a, s, h), warp, lane);
   const int64_t nchunks = (len + C - 1) / C;
   for (int64_t ci = 0; ci < nchunks; ++ci) {
     const int64_t t0 = start + ci * C;
     const int n = (int)(len - ci * C < C ? len - ci * C : C);
-    // ---- stage K, Q (hi/lo BF16), gates ----------------------------------
-    for (int idx = tid; idx < C * (DK / 4); idx += THREADS) {
-      const int i = idx >> 5, c4 = (idx & 31) * 4;
-      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), qv = kv;
-      if (i < n) {
-        const int64_t off = ((t0 + i) * a.Hk + kh) * DK + c4;
-        kv = *reinterpret_cast<const float4*>(a.k + off);
-        qv = *reinterpret_cast<const float4*>(a.q + off);
-      }
-      uint32_t kh0, kl0, kh1, kl1, qh0, ql0, qh1, ql1;
-      split2(kv.x, kv.y, kh0, kl0);
-      split2(kv.z, kv.w, kh1, kl1);
-      split2(qv.x, qv.y, qh0, ql0);
-      split2(qv.z, qv.w, qh1, ql1);
-      const uint32_t o = swz(i, c4, 16);
-      *reinterpret_cast<uint2*>(sm + OFF_KHI + o) = make_uint2(kh0, kh1);
-      *reinterpret_cast<uint2*>(sm + OFF_KLO + o) = make_uint2(kl0, kl1);
-      *reinterpret_cast<uint2*>(sm + OFF_QHI + o) = make_uint2(qh0, qh1);
-      *reinterpret_cast<uint2*>(sm + OFF_QLO + o) = make_uint2(ql0, ql1);
-    }
-    if (warp == 0) {
-      // Chunk-relative inclusive cumsum of g in FP64, two tokens a lane.
-      const int i0 = 2 * lane, i1 = i0 + 1;
-      const double g0 = i0 < n ? (double)a.g[(t0 + i0) * a.Hv + h] : 0.0;
-      const double g1 = i1 < n ? (double)a.g[(t0 + i1) * a.Hv + h] : 0.0;
-      const double pair = g0 + g1;
-      double run = pair;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const double up = __shfl_up_sync(0xffffffffu, run, o);
-        if (lane >= o) run += up;
-      }
-      const double excl = run - pair;
-      Gs[i0] = excl + g0;
-      Gs[i1] = excl + g0 + g1;
-      bs[i0] = i0 < n ? a.beta[(t0 + i0) * a.Hv + h] : 0.f;
-      bs[i1] = i1 < n ? a.beta[(t0 + i1) * a.Hv + h] : 0.f;
-    }
+    stage_kq(a.q, a.k, t0, n, a.Hk, kh, sm + OFF_KHI, nullptr, tid, THREADS);
+    if (warp == 0) cumsum_gates(a.g, a.beta, t0, n, a.Hv, h, lane, Gs, bs);
     __syncthreads();
     const double Glast = Gs[C - 1];  // padded tokens carry g = 0
-    int cap_row = -1;                // row whose post-state is captured
-    if (a.capture_state && a.capture > ci * C && a.capture <= ci * C + n)
-      cap_row = (int)(a.capture - 1 - ci * C);
     if (tid < C) {
       eg[tid] = expf((float)Gs[tid]);
       egd[tid] = expf((float)(Glast - Gs[tid]));
-      if (cap_row >= 0) ecap[tid] = tid <= cap_row ? expf((float)(Gs[cap_row] - Gs[tid])) : 0.f;
     }
-    // ---- Gram matrices: K K^T -> A (F32), Q K^T -> P (hi/lo) -----------------
     {
-      const int m0 = (warp >> 1) * 16, nb = (warp & 1) * 32;
       float kk[4][4], qk[4][4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) kk[j][e] = qk[j][e] = 0.f;
-#pragma unroll
-      for (int ks = 0; ks < DK / 16; ++ks) {
-        uint32_t akh[4], akl[4], aqh[4], aql[4];
-        lda(sbase + OFF_KHI, m0, ks * 16, 16, lane, akh);
-        lda(sbase + OFF_KLO, m0, ks * 16, 16, lane, akl);
-        lda(sbase + OFF_QHI, m0, ks * 16, 16, lane, aqh);
-        lda(sbase + OFF_QLO, m0, ks * 16, 16, lane, aql);
-#pragma unroll
-        for (int np = 0; np < 2; ++np) {
-          uint32_t bh[4], bl[4];
-          ldb_nk(sbase + OFF_KHI, nb + np * 16, ks * 16, 16, lane, bh);
-          ldb_nk(sbase + OFF_KLO, nb + np * 16, ks * 16, 16, lane, bl);
-          mma3(kk[2 * np], akh, akl, bh[0], bh[1], bl[0], bl[1]);
-          mma3(kk[2 * np + 1], akh, akl, bh[2], bh[3], bl[2], bl[3]);
-          mma3(qk[2 * np], aqh, aql, bh[0], bh[1], bl[0], bl[1]);
-          mma3(qk[2 * np + 1], aqh, aql, bh[2], bh[3], bl[2], bl[3]);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-#pragma unroll
-        for (int e = 0; e < 4; e += 2) {
-          const int i = m0 + r0 + (e >> 1) * 8;
-          float pv[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int col = nb + j * 8 + c0 + u;
-            const bool lower = col <= i && i < n;
-            const float decay = lower ? expf((float)(Gs[i] - Gs[col])) : 0.f;
-            As[i * AP + col] = (lower && col < i) ? bs[i] * (decay * kk[j][e + u]) : 0.f;
-            pv[u] = lower ? decay * qk[j][e + u] : 0.f;
-          }
-          uint32_t ph, pl;
-          split2(pv[0], pv[1], ph, pl);
-          const uint32_t o = swz(i, nb + j * 8 + c0, 8);
-          *reinterpret_cast<uint32_t*>(sm + OFF_PHI + o) = ph;
-          *reinterpret_cast<uint32_t*>(sm + OFF_PLO + o) = pl;
-        }
-      }
+      gram_mma(sbase + OFF_KHI, warp, lane, kk, qk);
+      gram_store<false>(kk, qk, warp, lane, n, Gs, bs, As, sm + OFF_PHI, sm + OFF_PLO);
     }
     __syncthreads();
-    // ---- T = (I + A)^{-1}: diagonal 16 x 16 blocks --------------------------
-    if (warp < 4 && lane < 16) {
-      const int b0 = warp * 16, c = lane;
-      float x[16];
-#pragma unroll
-      for (int r = 0; r < 16; ++r) {
-        float acc = r == c ? 1.f : 0.f;
-#pragma unroll
-        for (int j = 0; j < r; ++j) acc -= As[(b0 + r) * AP + b0 + j] * x[j];
-        x[r] = r < c ? 0.f : acc;
-      }
-#pragma unroll
-      for (int r = 0; r < 16; ++r) Ts[(b0 + r) * AP + b0 + c] = x[r];
-    }
-    // Upper blocks are zero.
-    for (int idx = tid; idx < C * C; idx += THREADS) {
-      const int i = idx >> 6, j = idx & 63;
-      if ((j >> 4) > (i >> 4)) Ts[i * AP + j] = 0.f;
-    }
+    solve_t<false>(As, Ts, Ms, bs, sm + OFF_THI, sm + OFF_TLO, tid, warp, lane, THREADS);
     __syncthreads();
-    // Off-diagonal blocks, block row by block row:
-    //   T_bj = -D_b * sum_{k=j}^{b-1} A_bk T_kj.
-    for (int b = 1; b < 4; ++b) {
-      for (int idx = tid; idx < b * 256; idx += THREADS) {
-        const int j = idx >> 8, r = (idx >> 4) & 15, c = idx & 15;
-        float acc = 0.f;
-        for (int kb = j; kb < b; ++kb)
-#pragma unroll
-          for (int q = 0; q < 16; ++q)
-            acc += As[(b * 16 + r) * AP + kb * 16 + q] * Ts[(kb * 16 + q) * AP + j * 16 + c];
-        Ms[(j * 16 + r) * 17 + c] = acc;
-      }
-      __syncthreads();
-      for (int idx = tid; idx < b * 256; idx += THREADS) {
-        const int j = idx >> 8, r = (idx >> 4) & 15, c = idx & 15;
-        float acc = 0.f;
-#pragma unroll
-        for (int q = 0; q <= 15; ++q)
-          acc += Ts[(b * 16 + r) * AP + b * 16 + q] * Ms[(j * 16 + q) * 17 + c];
-        Ts[(b * 16 + r) * AP + j * 16 + c] = -acc;
-      }
-      __syncthreads();
-    }
-    // T diag(beta) -> hi/lo BF16.
-    for (int idx = tid; idx < C * C / 2; idx += THREADS) {
-      const int i = idx >> 5, j = (idx & 31) * 2;
-      uint32_t th, tl;
-      split2(Ts[i * AP + j] * bs[j], Ts[i * AP + j + 1] * bs[j + 1], th, tl);
-      const uint32_t o = swz(i, j, 8);
-      *reinterpret_cast<uint32_t*>(sm + OFF_THI + o) = th;
-      *reinterpret_cast<uint32_t*>(sm + OFF_TLO + o) = tl;
-    }
-    __syncthreads();
-
-    // ---- per-warp state products (value rows dv0..dv0+15) ---------------
-    // R^T = V^T - (S^T K^T) diag(e^G): 16 x 64, eight n-tiles of tokens.
-    float R[8][4];
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) R[nt][e] = 0.f;
-#pragma unroll
-    for (int ks = 0; ks < DK / 16; ++ks) {
-      uint32_t ah[4], al[4];
-      acc_to_a(S[2 * ks], S[2 * ks + 1], ah, al);
-#pragma unroll
-      for (int np = 0; np < 4; ++np) {
-        uint32_t bh[4], bl[4];
-        ldb_nk(sbase + OFF_KHI, np * 16, ks * 16, 16, lane, bh);
-        ldb_nk(sbase + OFF_KLO, np * 16, ks * 16, 16, lane, bl);
-        mma3(R[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
-        mma3(R[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
-      }
-    }
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int tok = nt * 8 + c0 + (e & 1);
-        const int dv = dv0 + r0 + (e >> 1) * 8;
-        const float vv = tok < n ? a.v[((t0 + tok) * a.Hv + h) * DV + dv] : 0.f;
-        R[nt][e] = vv - eg[tok] * R[nt][e];
-      }
-    }
-    // D^T = R^T (T diag(beta))^T.
-    float D[8][4];
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) D[nt][e] = 0.f;
-#pragma unroll
-    for (int ks = 0; ks < C / 16; ++ks) {
-      uint32_t ah[4], al[4];
-      acc_to_a(R[2 * ks], R[2 * ks + 1], ah, al);
-#pragma unroll
-      for (int np = 0; np < 4; ++np) {
-        uint32_t bh[4], bl[4];
-        ldb_nk(sbase + OFF_THI, np * 16, ks * 16, 8, lane, bh);
-        ldb_nk(sbase + OFF_TLO, np * 16, ks * 16, 8, lane, bl);
-        mma3(D[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
-        mma3(D[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
-      }
-    }
-    // O^T = (S^T Q^T) diag(e^G) + D^T P^T  (R's registers are reused for O).
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) R[nt][e] = 0.f;
-#pragma unroll
-    for (int ks = 0; ks < DK / 16; ++ks) {
-      uint32_t ah[4], al[4];
-      acc_to_a(S[2 * ks], S[2 * ks + 1], ah, al);
-#pragma unroll
-      for (int np = 0; np < 4; ++np) {
-        uint32_t bh[4], bl[4];
-        ldb_nk(sbase + OFF_QHI, np * 16, ks * 16, 16, lane, bh);
-        ldb_nk(sbase + OFF_QLO, np * 16, ks * 16, 16, lane, bl);
-        mma3(R[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
-        mma3(R[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
-      }
-    }
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) R[nt][e] *= eg[nt * 8 + c0 + (e & 1)];
-#pragma unroll
-    for (int ks = 0; ks < C / 16; ++ks) {
-      uint32_t ah[4], al[4];
-      acc_to_a(D[2 * ks], D[2 * ks + 1], ah, al);
-#pragma unroll
-      for (int np = 0; np < 4; ++np) {
-        uint32_t bh[4], bl[4];
-        ldb_nk(sbase + OFF_PHI, np * 16, ks * 16, 8, lane, bh);
-        ldb_nk(sbase + OFF_PLO, np * 16, ks * 16, 8, lane, bl);
-        mma3(R[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
-        mma3(R[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
-      }
-    }
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int tok = nt * 8 + c0 + (e & 1);
-        const int dv = dv0 + r0 + (e >> 1) * 8;
-        if (tok < n) a.out[((t0 + tok) * a.Hv + h) * DV + dv] = R[nt][e];
-      }
-    }
-    // Capture: S_c^T = e^{G_c} S^T + (D^T diag(e^{G_c - G} [j <= c])) K.
-    if (cap_row >= 0) {
-      const float ec = expf((float)Gs[cap_row]);
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        float X[8][4];
-#pragma unroll
-        for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) X[nt][e] = ec * S[half * 8 + nt][e];
-#pragma unroll
-        for (int ks = 0; ks < C / 16; ++ks) {
-          float d0[4], d1[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            d0[e] = D[2 * ks][e] * ecap[ks * 16 + c0 + (e & 1)];
-            d1[e] = D[2 * ks + 1][e] * ecap[ks * 16 + 8 + c0 + (e & 1)];
-          }
-          uint32_t ah[4], al[4];
-          acc_to_a(d0, d1, ah, al);
-#pragma unroll
-          for (int np = 0; np < 4; ++np) {
-            uint32_t bh[4], bl[4];
-            ldb_kn(sbase + OFF_KHI, half * 64 + np * 16, ks * 16, 16, lane, bh);
-            ldb_kn(sbase + OFF_KLO, half * 64 + np * 16, ks * 16, 16, lane, bl);
-            mma3(X[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
-            mma3(X[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
-          }
-        }
-#pragma unroll
-        for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int dv = dv0 + r0 + (e >> 1) * 8;
-            const int dk = (half * 8 + nt) * 8 + c0 + (e & 1);
-            a.capture_state[((int64_t)h * DK + dk) * DV + dv] = X[nt][e];
-          }
-      }
-    }
-    // S^T <- e^{G_last} S^T + (D^T diag(e^{G_last - G})) K.
-    const float el = expf((float)Glast);
-#pragma unroll
-    for (int nt = 0; nt < 16; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) S[nt][e] *= el;
-#pragma unroll
-    for (int ks = 0; ks < C / 16; ++ks) {
-      float d0[4], d1[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        d0[e] = D[2 * ks][e] * egd[ks * 16 + c0 + (e & 1)];
-        d1[e] = D[2 * ks + 1][e] * egd[ks * 16 + 8 + c0 + (e & 1)];
-      }
-      uint32_t ah[4], al[4];
-      acc_to_a(d0, d1, ah, al);
-#pragma unroll
-      for (int np = 0; np < 8; ++np) {
-        uint32_t bh[4], bl[4];
-        ldb_kn(sbase + OFF_KHI, np * 16, ks * 16, 16, lane, bh);
-        ldb_kn(sbase + OFF_KLO, np * 16, ks * 16, 16, lane, bl);
-        mma3(S[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
-        mma3(S[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
-      }
-    }
+    int cap_row = -1;
+    if (a.capture_state && a.capture > ci * C && a.capture <= ci * C + n)
+      cap_row = (int)(a.capture - 1 - ci * C);
+    ChunkOps ops;
+    ops.kq = sbase + OFF_KHI;
+    ops.tp = sbase + OFF_THI;
+    ops.eg = eg;
+    ops.egd = egd;
+    ops.G = Gs;
+    ops.el = expf((float)Glast);
+    float Vr[8][4];
+    load_v(a.v, t0, n, a.Hv, h, warp, lane, Vr);
+    carry_step(S, Vr, ops, n, t0, a.Hv, h, warp, lane, a.out, cap_row, a.capture_state);
     __syncthreads();  // the next chunk overwrites the shared tiles
   }
-  if (a.final_state) {
-    float* dst = a.final_state + ((int64_t)s * a.Hv + h) * DK * DV;
-#pragma unroll
-    for (int nt = 0; nt < 16; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int dv = dv0 + r0 + (e >> 1) * 8;
-        const int dk = nt * 8 + c0 + (e & 1);
-        dst[(int64_t)dk * DV + dv] = S[nt][e];
-      }
+  if (a.final_state) store_state(S, a.final_state + ((int64_t)s * a.Hv + h) * DK * DV, warp, lane);
+}
+
+// ---------------------------------------------------------------------------
+// Pipelined pair. delta_prep_kernel: one CTA per (chunk, k-head), fully
+// parallel: splits K, Q into hi/lo tiles, forms the Gram products once, and
+// for each v-head of the k-head writes T diag(beta), P and the decay vectors
+// to the workspace as tile images. delta_carry_kernel: one CTA per
+// (sequence, v-head) walks the chunks; every chunk input is independent of the
+// state, so the next chunk's tiles stream in with cp.async while the tensor
+// cores work on the current one.
+// ---------------------------------------------------------------------------
+struct ScanSeq {
+  int32_t chunk0;
+  int32_t nchunks;
+};
+struct ScanChunk {
+  int64_t t0;
+  int32_t n;
+  int32_t seq;
+};
+
+constexpr int TP_TILES = 4 * SQ_BYTES;                   // THI, TLO, PHI, PLO
+constexpr int VEC_BYTES = 64 * 4 + 64 * 4 + 64 * 4 + 64 * 8;  // eg, egd, el, G
+constexpr int TP_IMG = TP_TILES + VEC_BYTES;              // 34048 bytes
+constexpr int KQ_IMG = 4 * KQ_BYTES;                      // 65536 bytes
+constexpr int STAGE = KQ_IMG + TP_IMG;                    // 99584 bytes
+constexpr int CARRY_SMEM = 2 * STAGE;
+
+// prep kernel shared layout
+constexpr int P_OFF_KQ = 0;
+constexpr int P_OFF_A = KQ_IMG;
+constexpr int P_OFF_T = P_OFF_A + C * AP * 4;
+constexpr int P_OFF_M = P_OFF_T + C * AP * 4;
+constexpr int P_OFF_G = P_OFF_M + 3 * 16 * 17 * 4;
+constexpr int P_OFF_B = P_OFF_G + C * 8;
+constexpr int PREP_SMEM = P_OFF_B + C * 4;
+
+struct PipeArgs {
+  ScanArgs a;
+  const ScanSeq* seqs;
+  const ScanChunk* chunks;
+  uint8_t* kq_img;  // [chunks][Hk][KQ_IMG]
+  uint8_t* tp_img;  // [chunks][Hv][TP_IMG]
+};
+
+__global__ void __launch_bounds__(THREADS, 2) delta_prep_kernel(PipeArgs p) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  const ScanArgs& a = p.a;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int kh = blockIdx.y;
+  const int64_t gc = blockIdx.x;
+  const ScanChunk ch = p.chunks[gc];
+  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(sm);
+  float* As = reinterpret_cast<float*>(sm + P_OFF_A);
+  float* Ts = reinterpret_cast<float*>(sm + P_OFF_T);
+  float* Ms = reinterpret_cast<float*>(sm + P_OFF_M);
+  double* Gs = reinterpret_cast<double*>(sm + P_OFF_G);
+  float* bs = reinterpret_cast<float*>(sm + P_OFF_B);
+  uint8_t* kq = p.kq_img + (gc * a.Hk + kh) * (int64_t)KQ_IMG;
+  stage_kq(a.q, a.k, ch.t0, ch.n, a.Hk, kh, sm + P_OFF_KQ, kq, tid, THREADS);
+  __syncthreads();
+  float kk[4][4], qk[4][4];
+  gram_mma(sbase + P_OFF_KQ, warp, lane, kk, qk);
+  const int rep = a.Hv / a.Hk;
+  for (int r = 0; r < rep; ++r) {
+    const int h = kh * rep + r;
+    uint8_t* tp = p.tp_img + (gc * a.Hv + h) * (int64_t)TP_IMG;
+    if (warp == 0) cumsum_gates(a.g, a.beta, ch.t0, ch.n, a.Hv, h, lane, Gs, bs);
+    __syncthreads();
+    const double Glast = Gs[C - 1];
+    if (tid < C) {
+      float* vec = reinterpret_cast<float*>(tp + TP_TILES);
+      vec[tid] = expf((float)Gs[tid]);                   // eg
+      vec[64 + tid] = expf((float)(Glast - Gs[tid]));    // egd
+      vec[128 + tid] = tid == 0 ? expf((float)Glast) : 0.f;  // el
+      reinterpret_cast<double*>(vec + 192)[tid] = Gs[tid];   // G
+    }
+    gram_store<true>(kk, qk, warp, lane, ch.n, Gs, bs, As, tp + 2 * SQ_BYTES, tp + 3 * SQ_BYTES);
+    __syncthreads();
+    solve_t<true>(As, Ts, Ms, bs, tp + 0 * SQ_BYTES, tp + 1 * SQ_BYTES, tid, warp, lane, THREADS);
+    __syncthreads();  // Gs, bs, As, Ts are reused by the next v-head
   }
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src));
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;"); }
+__device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void fetch_stage(uint32_t dst, const uint8_t* kq, const uint8_t* tp,
+                                            int tid) {
+  for (int o = tid * 16; o < KQ_IMG; o += THREADS * 16) cp_async16(dst + o, kq + o);
+  for (int o = tid * 16; o < TP_IMG; o += THREADS * 16) cp_async16(dst + KQ_IMG + o, tp + o);
+}
+
+__global__ void __launch_bounds__(THREADS, 1) delta_carry_kernel(PipeArgs p) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  const ScanArgs& a = p.a;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int h = blockIdx.x % a.Hv;
+  const int s = blockIdx.x / a.Hv;
+  const int kh = h / (a.Hv / a.Hk);
+  const ScanSeq sq = p.seqs[s];
+  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(sm);
+  auto kq_of = [&](int64_t gc) { return p.kq_img + (gc * a.Hk + kh) * (int64_t)KQ_IMG; };
+  auto tp_of = [&](int64_t gc) { return p.tp_img + (gc * a.Hv + h) * (int64_t)TP_IMG; };
+
+  float S[16][4];
+  load_state(S, init_for(a, s, h), warp, lane);
+  fetch_stage(sbase, kq_of(sq.chunk0), tp_of(sq.chunk0), tid);
+  cp_commit();
+  int64_t done = 0;  // tokens of this sequence before the current chunk
+  for (int ci = 0; ci < sq.nchunks; ++ci) {
+    const int64_t gc = sq.chunk0 + ci;
+    const ScanChunk ch = p.chunks[gc];
+    float Vr[8][4];
+    load_v(a.v, ch.t0, ch.n, a.Hv, h, warp, lane, Vr);
+    cp_wait_all();
+    __syncthreads();  // stage ci is in; every warp finished chunk ci - 1
+    if (ci + 1 < sq.nchunks) {
+      const uint32_t nxt = sbase + ((ci + 1) & 1) * STAGE;
+      fetch_stage(nxt, kq_of(gc + 1), tp_of(gc + 1), tid);
+      cp_commit();
+    }
+    const uint32_t cur = sbase + (ci & 1) * STAGE;
+    const uint8_t* cur_ptr = sm + (ci & 1) * STAGE;
+    const float* vec = reinterpret_cast<const float*>(cur_ptr + KQ_IMG + TP_TILES);
+    ChunkOps ops;
+    ops.kq = cur;
+    ops.tp = cur + KQ_IMG;
+    ops.eg = vec;
+    ops.egd = vec + 64;
+    ops.el = vec[128];
+    ops.G = reinterpret_cast<const double*>(vec + 192);
+    int cap_row = -1;
+    if (a.capture_state && a.capture > done && a.capture <= done + ch.n)
+      cap_row = (int)(a.capture - 1 - done);
+    carry_step(S, Vr, ops, ch.n, ch.t0, a.Hv, h, warp, lane, a.out, cap_row, a.capture_state);
+    done += ch.n;
+  }
+  if (a.final_state) store_state(S, a.final_state + ((int64_t)s * a.Hv + h) * DK * DV, warp, lane);
 }
 
 }  // namespace
 
-size_t delta_scan_workspace(int64_t total_tokens, int nseq, int Hv, int dk, int dv) {
-  (void)total_tokens;
-  (void)Hv;
-  (void)dk;
-  (void)dv;
-  // Only the per-sequence token offsets travel to the device.
+// Fused-path workspace: the per-sequence token offsets (nseq + 1 int64).
+size_t delta_scan_fused_workspace(int nseq) {
   return ((size_t)(nseq + 1) * sizeof(int64_t) + 255) & ~(size_t)255;
 }
 
-// cu_dev: device copy of the offsets (or null for one sequence of cu_host[1]).
+namespace {
+size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
+struct PipeLayout {
+  size_t seq_off, chunk_off, kq_off, tp_off, total;
+  int64_t max_chunks;
+};
+PipeLayout pipe_layout(int64_t total_tokens, int nseq, int Hk, int Hv) {
+  PipeLayout l;
+  l.max_chunks = (total_tokens + C - 1) / C + nseq;
+  l.seq_off = 0;
+  l.chunk_off = al256(sizeof(ScanSeq) * (size_t)nseq);
+  l.kq_off = al256(l.chunk_off + sizeof(ScanChunk) * (size_t)l.max_chunks);
+  l.tp_off = al256(l.kq_off + (size_t)KQ_IMG * l.max_chunks * Hk);
+  l.total = al256(l.tp_off + (size_t)TP_IMG * l.max_chunks * Hv);
+  return l;
+}
+bool g_attr_set[64] = {false};
+int set_attrs() {
+  int dev = 0;
+  CLEF_CUDA(cudaGetDevice(&dev));
+  if (dev >= 0 && dev < 64 && !g_attr_set[dev]) {
+    CLEF_CUDA(cudaFuncSetAttribute(delta_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+    CLEF_CUDA(cudaFuncSetAttribute(delta_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   PREP_SMEM));
+    CLEF_CUDA(cudaFuncSetAttribute(delta_carry_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   CARRY_SMEM));
+    g_attr_set[dev] = true;
+  }
+  return CLEF_OK;
+}
+}  // namespace
+
+size_t delta_scan_workspace(int64_t total_tokens, int nseq, int Hk, int Hv) {
+  return pipe_layout(total_tokens, nseq, Hk, Hv).total;
+}
+
+int delta_scan_plan(const int64_t* cu_host, int nseq, int Hk, int Hv, void* ws, size_t ws_bytes,
+                    cudaStream_t s, ScanPlan* plan) {
+  const int64_t total = cu_host[nseq];
+  const PipeLayout l = pipe_layout(total, nseq, Hk, Hv);
+  CLEF_CHECK(ws && ws_bytes >= l.total, CLEF_ERR_INVALID, "delta_scan: workspace too small");
+  CLEF_CHECK(((uintptr_t)ws & 255) == 0, CLEF_ERR_INVALID, "delta_scan: workspace alignment");
+  std::vector<ScanSeq> seqs(nseq);
+  std::vector<ScanChunk> chunks;
+  chunks.reserve((size_t)l.max_chunks);
+  for (int si = 0; si < nseq; ++si) {
+    seqs[si].chunk0 = (int32_t)chunks.size();
+    for (int64_t t = cu_host[si]; t < cu_host[si + 1]; t += C)
+      chunks.push_back({t, (int32_t)std::min<int64_t>(C, cu_host[si + 1] - t), si});
+    seqs[si].nchunks = (int32_t)chunks.size() - seqs[si].chunk0;
+  }
+  char* base = reinterpret_cast<char*>(ws);
+  CLEF_CUDA(cudaMemcpyAsync(base + l.seq_off, seqs.data(), sizeof(ScanSeq) * seqs.size(),
+                            cudaMemcpyHostToDevice, s));
+  CLEF_CUDA(cudaMemcpyAsync(base + l.chunk_off, chunks.data(), sizeof(ScanChunk) * chunks.size(),
+                            cudaMemcpyHostToDevice, s));
+  plan->ws = ws;
+  plan->nseq = nseq;
+  plan->nchunks = (int64_t)chunks.size();
+  plan->total = total;
+  plan->Hk = Hk;
+  plan->Hv = Hv;
+  return CLEF_OK;
+}
+
+int launch_delta_scan_planned(const ScanPlan& plan, const float* q, const float* k, const float* v,
+                              const float* g, const float* beta, const float* init, int init_shared,
+                              int64_t capture, float* capture_state, float* final_state, float* out,
+                              cudaStream_t s) {
+  RC_(set_attrs());
+  const PipeLayout l = pipe_layout(plan.total, plan.nseq, plan.Hk, plan.Hv);
+  char* base = reinterpret_cast<char*>(plan.ws);
+  PipeArgs p;
+  p.a.q = q;
+  p.a.k = k;
+  p.a.v = v;
+  p.a.g = g;
+  p.a.beta = beta;
+  p.a.cu = nullptr;
+  p.a.T = plan.total;
+  p.a.Hk = plan.Hk;
+  p.a.Hv = plan.Hv;
+  p.a.init = init;
+  p.a.init_shared = init_shared;
+  p.a.capture = capture;
+  p.a.capture_state = capture_state;
+  p.a.final_state = final_state;
+  p.a.out = out;
+  p.seqs = reinterpret_cast<const ScanSeq*>(base + l.seq_off);
+  p.chunks = reinterpret_cast<const ScanChunk*>(base + l.chunk_off);
+  p.kq_img = reinterpret_cast<uint8_t*>(base + l.kq_off);
+  p.tp_img = reinterpret_cast<uint8_t*>(base + l.tp_off);
+  delta_prep_kernel<<<dim3((unsigned)plan.nchunks, (unsigned)plan.Hk), THREADS, PREP_SMEM, s>>>(p);
+  RC_(launch_status("delta_prep"));
+  delta_carry_kernel<<<(unsigned)(plan.nseq * plan.Hv), THREADS, CARRY_SMEM, s>>>(p);
+  return launch_status("delta_carry");
+}
+
+// Fused single-pass path with the offsets already on the device (null = one
+// sequence of `total`).
 int launch_delta_scan_dev(const float* q, const float* k, const float* v, const float* g,
                           const float* beta, const int64_t* cu_dev, int64_t total, int nseq, int Hk,
                           int Hv, const float* init, int init_shared, int64_t capture,
                           float* capture_state, float* final_state, float* out, cudaStream_t s) {
-  static bool attr[64] = {false};
-  int dev = 0;
-  CLEF_CUDA(cudaGetDevice(&dev));
-  if (dev >= 0 && dev < 64 && !attr[dev]) {
-    CLEF_CUDA(cudaFuncSetAttribute(delta_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
-    attr[dev] = true;
-  }
+  RC_(set_attrs());
   ScanArgs a;
   a.q = q;
   a.k = k;
@@ -571,18 +903,13 @@ int launch_delta_scan(const float* q, const float* k, const float* v, const floa
                       float* capture_state, float* final_state, float* out, void* ws,
                       size_t ws_bytes, cudaStream_t s) {
   CLEF_CHECK(dk == DK && dv == DV, CLEF_ERR_UNSUPPORTED, "delta_scan: dk and dv must be 128");
-  const int64_t total = cu_host[nseq];
-  const int64_t* cu_dev = nullptr;
-  if (nseq > 1) {
-    CLEF_CHECK(ws && ws_bytes >= delta_scan_workspace(total, nseq, Hv, dk, dv), CLEF_ERR_INVALID,
-               "delta_scan: workspace too small");
-    CLEF_CUDA(cudaMemcpyAsync(ws, cu_host, sizeof(int64_t) * (nseq + 1), cudaMemcpyHostToDevice, s));
-    cu_dev = reinterpret_cast<const int64_t*>(ws);
-  }
-  return launch_delta_scan_dev(q, k, v, g, beta, cu_dev, total, nseq, Hk, Hv, init, init_shared,
-                               capture, capture_state, final_state, out, s);
+  ScanPlan plan;
+  RC_(delta_scan_plan(cu_host, nseq, Hk, Hv, ws, ws_bytes, s, &plan));
+  return launch_delta_scan_planned(plan, q, k, v, g, beta, init, init_shared, capture,
+                                   capture_state, final_state, out, s);
 }
 
+// ---------------------------------------------------------------------------
 
 // ---------------------------------------------------------------------------
 // Allocation-free variant of clef_delta_scan.
@@ -629,10 +956,10 @@ using namespace clef;
 
 extern "C" {
 
-size_t clef_delta_scan_workspace_size(int64_t total_tokens, int32_t nseq, int32_t Hv, int32_t dk,
-                                      int32_t dv) {
-  if (total_tokens < 0 || nseq <= 0 || Hv <= 0) return 0;
-  return delta_scan_workspace(total_tokens, nseq, Hv, dk, dv);
+size_t clef_delta_scan_workspace_size(int64_t total_tokens, int32_t nseq, int32_t Hk, int32_t Hv,
+                                      int32_t dk, int32_t dv) {
+  if (total_tokens < 0 || nseq <= 0 || Hk <= 0 || Hv <= 0 || dk != 128 || dv != 128) return 0;
+  return delta_scan_workspace(total_tokens, nseq, Hk, Hv);
 }
 
 int clef_delta_scan(const float* q, const float* k, const float* v, const float* g,
@@ -665,12 +992,10 @@ int clef_delta_scan(const float* q, const float* k, const float* v, const float*
   }
   CLEF_CHECK(((uintptr_t)q | (uintptr_t)k) % 16 == 0, CLEF_ERR_INVALID,
              "delta_scan: q and k must be 16-byte aligned");
-  if (nseq > 1) {
-    CLEF_CHECK(workspace && workspace_bytes >= delta_scan_workspace(T, nseq, Hv, dk, dv),
-               CLEF_ERR_INVALID, "delta_scan: workspace too small");
-    CLEF_CHECK(((uintptr_t)workspace & 255) == 0, CLEF_ERR_INVALID,
-               "delta_scan: workspace must be 256-byte aligned");
-  }
+  CLEF_CHECK(workspace && workspace_bytes >= delta_scan_workspace(T, nseq, Hk, Hv),
+             CLEF_ERR_INVALID, "delta_scan: workspace too small");
+  CLEF_CHECK(((uintptr_t)workspace & 255) == 0, CLEF_ERR_INVALID,
+             "delta_scan: workspace must be 256-byte aligned");
   return launch_delta_scan(q, k, v, g, beta, cu.data(), nseq, Hk, Hv, dk, dv, init_state,
                            init_shared, capture, capture_state, final_state, out, workspace,
                            workspace_bytes, as_stream(stream));

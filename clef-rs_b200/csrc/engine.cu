@@ -311,7 +311,7 @@ int ensure_capacity(clef_engine* e, int64_t tokens, int64_t seqs) {
   take(sizeof(uint16_t) * M * e->att_kv);                 // 13 katt
   take(sizeof(uint16_t) * M * c.intermediate_size);       // 14 act
   take(sizeof(float) * seqs * std::max(1, c.head_outputs));  // 15 logits
-  const size_t ws = delta_scan_workspace(M, (int)seqs + 1, hv, 128, 128);
+  const size_t ws = delta_scan_workspace(M, (int)seqs, c.linear_num_key_heads, hv);
   take(ws);                                               // 16 scan ws
   if (e->arena) cudaFree(e->arena);
   e->arena = nullptr;
@@ -475,6 +475,11 @@ int run_pack(clef_engine* e, const int32_t* ids, const int64_t* offsets, int s0,
   pack.total = M;
   pack.qblocks = qb[np];
 
+  // Chunk tables of the DeltaNet scan, shared by every DeltaNet layer of the pack.
+  ScanPlan plan;
+  bool any_delta = false;
+  for (int li = 0; li < c.num_hidden_layers; ++li) any_delta |= c.layer_types[li] == 0;
+  if (any_delta) RC(delta_scan_plan(cu.data(), np, hk, hv, e->scan_ws, e->scan_ws_bytes, s, &plan));
   {
     STAGE(kStEmbed);
     RC(launch_embed(e->embed, ids_src, M, hid, e->h, s));
@@ -504,9 +509,9 @@ int run_pack(clef_engine* e, const int32_t* ids, const int64_t* offsets, int s0,
       }
       {
         STAGE(kStDeltaScan);
-        RC(launch_delta_scan_dev(e->dq, e->dk, e->dv, e->dg, e->db, e->meta_d, M, np, hk, hv,
-                                 il ? il->S : nullptr, 1, capture,
-                                 cap ? cap->layers[li].S : nullptr, nullptr, e->dout, s));
+        RC(launch_delta_scan_planned(plan, e->dq, e->dk, e->dv, e->dg, e->db,
+                                     il ? il->S : nullptr, 1, capture,
+                                     cap ? cap->layers[li].S : nullptr, nullptr, e->dout, s));
       }
       if (cap) {
         auto& cl = cap->layers[li];

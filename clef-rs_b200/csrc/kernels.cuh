@@ -49,15 +49,31 @@ int launch_copy_rows(const void* src, int64_t ld, int64_t r0, int64_t count, int
                      int elem, void* dst, int64_t ldd, cudaStream_t s);
 
 // ---- delta_scan.cu ----------------------------------------------------------
-size_t delta_scan_workspace(int64_t total_tokens, int nseq, int Hv, int dk, int dv);
-// cu_host: host int64 [nseq+1].
+// Pipelined scan (prep + carry kernels): workspace = offsets tables + the
+// per-chunk tile images; a plan uploads the tables once and can be reused by
+// every DeltaNet layer of a pack.
+struct ScanPlan {
+  void* ws = nullptr;
+  int nseq = 0;
+  int64_t nchunks = 0, total = 0;
+  int Hk = 0, Hv = 0;
+};
+size_t delta_scan_workspace(int64_t total_tokens, int nseq, int Hk, int Hv);
+int delta_scan_plan(const int64_t* cu_host, int nseq, int Hk, int Hv, void* ws, size_t ws_bytes,
+                    cudaStream_t s, ScanPlan* plan);
+int launch_delta_scan_planned(const ScanPlan& plan, const float* q, const float* k, const float* v,
+                              const float* g, const float* beta, const float* init, int init_shared,
+                              int64_t capture, float* capture_state, float* final_state, float* out,
+                              cudaStream_t s);
+// cu_host: host int64 [nseq+1]; builds a plan in `ws` and launches.
 int launch_delta_scan(const float* q, const float* k, const float* v, const float* g,
                       const float* beta, const int64_t* cu_host, int nseq, int Hk, int Hv, int dk,
                       int dv, const float* init, int init_shared, int64_t capture,
                       float* capture_state, float* final_state, float* out, void* ws,
                       size_t ws_bytes, cudaStream_t s);
-
-// Same, with the offsets already on the device (null = one sequence of `total`).
+// Fused single-pass scan with the offsets already on the device (null = one
+// sequence of `total`); needs no other workspace.
+size_t delta_scan_fused_workspace(int nseq);
 int launch_delta_scan_dev(const float* q, const float* k, const float* v, const float* g,
                           const float* beta, const int64_t* cu_dev, int64_t total, int nseq, int Hk,
                           int Hv, const float* init, int init_shared, int64_t capture,

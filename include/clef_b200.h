@@ -118,8 +118,11 @@ int clef_delta_prologue(const float* proj, int64_t ldp, int32_t a_col, int32_t b
                         float* q, float* k, float* v, float* g, float* beta, void* stream);
 
 /* Workspace bytes needed by clef_delta_scan for `nseq` sequences totalling
- * `total_tokens` tokens (pass nseq = 1 for a single sequence). */
-size_t clef_delta_scan_workspace_size(int64_t total_tokens, int32_t nseq, int32_t Hv,
+ * `total_tokens` tokens with Hk key heads and Hv value heads (0 for
+ * unsupported dimensions). The workspace holds the chunk tables and, per
+ * 64-token chunk, the split K/Q tiles (64 KB per key head) and the solved
+ * T diag(beta), P tiles and decay vectors (33 KB per value head). */
+size_t clef_delta_scan_workspace_size(int64_t total_tokens, int32_t nseq, int32_t Hk, int32_t Hv,
                                       int32_t dk, int32_t dv);
 
 /* Chunked (C = 64) gated-DeltaNet scan over one or more packed sequences.

@@ -79,13 +79,16 @@ def test_delta_scan_rejects_before_launch():
     assert args
 
 
-def test_workspace_holds_only_the_offsets_table():
-    # The fused scan keeps its state on chip; the workspace carries the
-    # per-sequence token offsets (nseq + 1 int64, 256-byte granules).
-    assert cb.delta_scan_workspace_size(1024, 1, 32) == 256
-    assert cb.delta_scan_workspace_size(1 << 20, 31, 32) == 256
-    assert cb.delta_scan_workspace_size(1 << 20, 32, 32) == 512
-    assert cb.delta_scan_workspace_size(-1, 1, 32) == 0
+def test_workspace_size():
+    # Chunk tables plus, per 64-token chunk, 64 KB of split K/Q tiles per key
+    # head and 34048 bytes of solved tiles and decay vectors per value head.
+    a = cb.delta_scan_workspace_size(1024, 1, 16, 32)
+    b = cb.delta_scan_workspace_size(2048, 1, 16, 32)
+    assert 0 < a < b
+    per_chunk = 16 * 65536 + 32 * 34048
+    assert per_chunk * 16 <= b - a <= per_chunk * 16 + 4096
+    assert cb.delta_scan_workspace_size(1024, 1, 16, 32, dk=64) == 0
+    assert cb.delta_scan_workspace_size(-1, 1, 16, 32) == 0
 
 
 def test_gemm_rejects_before_launch():

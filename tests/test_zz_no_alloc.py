@@ -44,7 +44,7 @@ def scan_both(inp, cu, final=True):
         args = [_p(t["q"]), _p(t["k"]), _p(t["v"]), _p(t["g"]), _p(t["b"]), T, Hk, Hv, 128, 128,
                 cu.ctypes.data, nseq, None, 0, 0, None, _p(fin), _p(out)]
         if fn == "clef_delta_scan":
-            size = cb.delta_scan_workspace_size(T, nseq, Hv)
+            size = cb.delta_scan_workspace_size(T, nseq, Hk, Hv)
             ws = torch.empty(size, dtype=torch.uint8, device="cuda")
             rc = cb.lib.clef_delta_scan(*args, _p(ws), size, stream)
         else:

@@ -102,76 +102,118 @@ __global__ void conv4_kernel(const float* __restrict__ x, int64_t ldx, const flo
 }
 
 // ---- DeltaNet prologue -------------------------------------------------------
-// One CTA of 256 threads per token; each thread owns 4 consecutive channels,
-// so one warp covers exactly one 128-wide q/k head and reduces its L2 norm
-// with shuffles (clef_delta_prepare, pointwise.metal:69-114; l2 and scaling,
-// qwen.rs:837-845; gates, qwen.rs:619-627).
-__global__ void __launch_bounds__(256) delta_prologue_kernel(
+// CTA = 256 threads x 4 channels (1024 channels = 8 whole 128-wide heads) over a
+// run of consecutive tokens. Each thread keeps the last four projection rows of
+// its channels in registers and slides the window one token at a time, so each
+// row is read from memory once; a warp covers exactly one q/k head and reduces
+// its L2 norm with shuffles (clef_delta_prepare, pointwise.metal:69-114; l2 and
+// scaling, qwen.rs:837-845). The CTAs of channel block 0 also compute the gates
+// (qwen.rs:619-627).
+constexpr int PRO_RUN = 16;
+
+__device__ __forceinline__ float4 pro_row(const float* __restrict__ proj, int64_t ldp,
+                                          const float* __restrict__ hist, int hist_rows, int width,
+                                          int64_t start, int64_t r, int c) {
+  // Row r (absolute token index) of sequence starting at `start`, channels c..c+3.
+  if (r >= start) return *reinterpret_cast<const float4*>(proj + r * ldp + c);
+  const int64_t hr = hist_rows + (r - start);
+  if (hist && hr >= 0) return *reinterpret_cast<const float4*>(hist + hr * width + c);
+  return make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+__global__ void __launch_bounds__(256, 3) delta_prologue_kernel(
     const float* __restrict__ proj, int64_t ldp, int a_col, int b_col,
     const float* __restrict__ hist, int hist_rows, const float* __restrict__ conv_w,
     const float* __restrict__ dt_bias, const float* __restrict__ a_log,
-    const int64_t* __restrict__ cu, int nseq, int Hk, int Hv, float qscale,
+    const int64_t* __restrict__ cu, int nseq, int64_t T, int Hk, int Hv, float qscale,
     float* __restrict__ q, float* __restrict__ k, float* __restrict__ v, float* __restrict__ g,
     float* __restrict__ beta) {
-  const int64_t t = blockIdx.x;
-  const int64_t start = cu ? cu[seq_of(cu, nseq, t)] : 0;  // cu == NULL: one sequence
-  const int64_t pos = t - start;
   const int key = Hk * 128;
   const int width = 2 * key + Hv * 128;
-  const int lane = threadIdx.x & 31;
-  for (int base = threadIdx.x * 4; base < width; base += 1024) {
-    // Taps of the four channels: conv_w[c][0..3] for c = base .. base+3.
-    const float4 w0 = *reinterpret_cast<const float4*>(conv_w + (base + 0) * 4);
-    const float4 w1 = *reinterpret_cast<const float4*>(conv_w + (base + 1) * 4);
-    const float4 w2 = *reinterpret_cast<const float4*>(conv_w + (base + 2) * 4);
-    const float4 w3 = *reinterpret_cast<const float4*>(conv_w + (base + 3) * 4);
-    const float tw[4][4] = {{w0.x, w1.x, w2.x, w3.x},
-                            {w0.y, w1.y, w2.y, w3.y},
-                            {w0.z, w1.z, w2.z, w3.z},
-                            {w0.w, w1.w, w2.w, w3.w}};
-    // Four causal taps for four channels, oldest to newest.
+  const int c = blockIdx.x * 1024 + threadIdx.x * 4;
+  const int64_t t_begin = (int64_t)blockIdx.y * PRO_RUN;
+  const int64_t t_end = min(T, t_begin + PRO_RUN);
+  // Sequence of the first token.
+  int s = cu ? (int)seq_of(cu, nseq, t_begin) : 0;
+  int64_t start = cu ? cu[s] : 0;
+  int64_t next_start = cu ? cu[s + 1] : T;
+  // Taps of the four channels: conv_w[c][0..3] for c .. c+3.
+  const float4 w0 = *reinterpret_cast<const float4*>(conv_w + (c + 0) * 4);
+  const float4 w1 = *reinterpret_cast<const float4*>(conv_w + (c + 1) * 4);
+  const float4 w2 = *reinterpret_cast<const float4*>(conv_w + (c + 2) * 4);
+  const float4 w3 = *reinterpret_cast<const float4*>(conv_w + (c + 3) * 4);
+  const float tw[4][4] = {{w0.x, w1.x, w2.x, w3.x},
+                          {w0.y, w1.y, w2.y, w3.y},
+                          {w0.z, w1.z, w2.z, w3.z},
+                          {w0.w, w1.w, w2.w, w3.w}};
+  float4 win[4];  // rows t-3, t-2, t-1, t
+  win[0] = pro_row(proj, ldp, hist, hist_rows, width, start, t_begin - 3, c);
+  win[1] = pro_row(proj, ldp, hist, hist_rows, width, start, t_begin - 2, c);
+  win[2] = pro_row(proj, ldp, hist, hist_rows, width, start, t_begin - 1, c);
+  // Rows t .. t+3 are requested before row t is used, so four loads per
+  // thread are in flight while the window slides.
+  float4 ahead[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    ahead[j] = t_begin + j < t_end ? *reinterpret_cast<const float4*>(proj + (t_begin + j) * ldp + c)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+  for (int64_t t = t_begin; t < t_end; ++t) {
+    if (t == next_start) {  // a new sequence starts: its window holds history or zeros
+      ++s;
+      start = t;
+      next_start = cu[s + 1];
+      win[0] = pro_row(proj, ldp, hist, hist_rows, width, start, t - 3, c);
+      win[1] = pro_row(proj, ldp, hist, hist_rows, width, start, t - 2, c);
+      win[2] = pro_row(proj, ldp, hist, hist_rows, width, start, t - 1, c);
+    }
+    win[3] = ahead[0];
+    ahead[0] = ahead[1];
+    ahead[1] = ahead[2];
+    ahead[2] = ahead[3];
+    if (t + 4 < t_end) ahead[3] = *reinterpret_cast<const float4*>(proj + (t + 4) * ldp + c);
+    // taps oldest to newest; rows before the sequence (and history) are zero
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int tap = 0; tap < 4; ++tap) {
-      const int delay = 3 - tap;
-      const int64_t r = pos - delay;
-      float4 xv;
-      if (r >= 0) {
-        xv = *reinterpret_cast<const float4*>(proj + (start + r) * ldp + base);
-      } else if (hist && hist_rows + r >= 0) {
-        xv = *reinterpret_cast<const float4*>(hist + (hist_rows + r) * width + base);
-      } else {
-        continue;
-      }
+      const int64_t r = t - (3 - tap);
+      if (r < start && !(hist && hist_rows + (r - start) >= 0)) continue;
+      const float4 xv = win[tap];
       acc.x = __fadd_rn(acc.x, __fmul_rn(xv.x, tw[tap][0]));
       acc.y = __fadd_rn(acc.y, __fmul_rn(xv.y, tw[tap][1]));
       acc.z = __fadd_rn(acc.z, __fmul_rn(xv.z, tw[tap][2]));
       acc.w = __fadd_rn(acc.w, __fmul_rn(xv.w, tw[tap][3]));
     }
-    float4 m = make_float4(silu_f(acc.x), silu_f(acc.y), silu_f(acc.z), silu_f(acc.w));
-    if (base < 2 * key) {
-      // The whole warp sits in one head (base aligned to 1024, heads of 128).
+    const float4 m = make_float4(silu_f(acc.x), silu_f(acc.y), silu_f(acc.z), silu_f(acc.w));
+    if (c < 2 * key) {
+      // The whole warp sits in one head (channel blocks of 1024, heads of 128).
       float ss = m.x * m.x + m.y * m.y + m.z * m.z + m.w * m.w;
       ss = warp_sum(ss);
-      const float n = sqrtf(ss + 1e-6f);
-      float4 r = make_float4(m.x / n, m.y / n, m.z / n, m.w / n);
-      if (base < key) {
+      const float nrm = sqrtf(ss + 1e-6f);
+      float4 r = make_float4(m.x / nrm, m.y / nrm, m.z / nrm, m.w / nrm);
+      if (c < key) {
         r = make_float4(__fmul_rn(r.x, qscale), __fmul_rn(r.y, qscale), __fmul_rn(r.z, qscale),
                         __fmul_rn(r.w, qscale));
-        *reinterpret_cast<float4*>(q + t * key + base) = r;
+        *reinterpret_cast<float4*>(q + t * key + c) = r;
       } else {
-        *reinterpret_cast<float4*>(k + t * key + (base - key)) = r;
+        *reinterpret_cast<float4*>(k + t * key + (c - key)) = r;
       }
     } else {
-      *reinterpret_cast<float4*>(v + t * (Hv * 128) + (base - 2 * key)) = m;
+      *reinterpret_cast<float4*>(v + t * (int64_t)(Hv * 128) + (c - 2 * key)) = m;
     }
-    (void)lane;
+    win[0] = win[1];
+    win[1] = win[2];
+    win[2] = win[3];
   }
-  for (int h = threadIdx.x; h < Hv; h += blockDim.x) {
-    const float a = __fadd_rn(proj[t * ldp + a_col + h], dt_bias[h]);
-    const float sp = __fadd_rn(fmaxf(a, 0.f), logf(__fadd_rn(expf(-fabsf(a)), 1.f)));
-    g[t * Hv + h] = __fmul_rn(sp, -expf(a_log[h]));
-    beta[t * Hv + h] = sigmoid_f(proj[t * ldp + b_col + h]);
+  if (blockIdx.x == 0) {
+    for (int idx = threadIdx.x; idx < (t_end - t_begin) * Hv; idx += blockDim.x) {
+      const int64_t t = t_begin + idx / Hv;
+      const int h = idx % Hv;
+      const float a = __fadd_rn(proj[t * ldp + a_col + h], dt_bias[h]);
+      const float sp = __fadd_rn(fmaxf(a, 0.f), logf(__fadd_rn(expf(-fabsf(a)), 1.f)));
+      g[t * Hv + h] = __fmul_rn(sp, -expf(a_log[h]));
+      beta[t * Hv + h] = sigmoid_f(proj[t * ldp + b_col + h]);
+    }
   }
 }
 
@@ -376,9 +418,11 @@ int launch_delta_prologue(const float* proj, int64_t ldp, int a_col, int b_col, 
   (void)dk;
   (void)dv;
   const float qscale = (float)(1.0 / std::sqrt(128.0));
-  delta_prologue_kernel<<<(unsigned)pack.total, 256, 0, s>>>(
-      proj, ldp, a_col, b_col, hist, hist_rows, conv_w, dt_bias, a_log, pack.cu_seqlens, pack.nseq,
-      Hk, Hv, qscale, q, k, v, g, beta);
+  const int width = 2 * Hk * 128 + Hv * 128;
+  const dim3 grid((unsigned)(width / 1024), (unsigned)ceil_div(pack.total, PRO_RUN));
+  delta_prologue_kernel<<<grid, 256, 0, s>>>(proj, ldp, a_col, b_col, hist, hist_rows, conv_w,
+                                             dt_bias, a_log, pack.cu_seqlens, pack.nseq,
+                                             pack.total, Hk, Hv, qscale, q, k, v, g, beta);
   return launch_status("delta_prologue");
 }
 

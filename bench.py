@@ -45,6 +45,12 @@ def parse():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="config4", choices=["config4", "config5"],
+                    help="config4: 256 requests U[256,2048] per GPU; config5: one 16384-token "
+                         "prefix computed once per GPU, 64 suffixes U[512,4096] sharded over GPUs")
+    ap.add_argument("--shard", action="store_true",
+                    help="config4 with one fixed batch shared by all ranks (LPT-sharded, "
+                         "strong scaling) instead of a batch per rank")
     ap.add_argument("--requests", type=int, default=256)
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -65,11 +71,19 @@ def peaks():
 
 
 def workload_config(args, n_gpus):
+    if args.workload == "config5":
+        return {"workload": "config5: 32-layer hybrid backbone + linear schema head, prefix reuse",
+                "prefix_tokens": 16384, "suffixes_total": 64, "suffix_len": "U[512,4096]",
+                "vocab": 248320, "layers": args.layers, "hidden": 2560, "intermediate": 9216,
+                "parallelism": f"dp{n_gpus} (suffixes LPT-sharded, prefix computed once per GPU)",
+                "l2": "not flushed: every step streams 8.4 GB of weights, far above the 126 MB L2"}
     return {"workload": "config4: 32-layer hybrid backbone + linear schema head",
             "requests_per_gpu": args.requests, "prompt_len": "U[256,2048]", "vocab": 248320,
             "layers": args.layers, "hidden": 2560, "intermediate": 9216,
             "deltanet_heads": "16qk/32v x 128", "attention_heads": "16q/4kv x 256",
-            "chunk": 64, "parallelism": f"dp{n_gpus} (request-sharded, weights replicated)",
+            "chunk": 64,
+            "parallelism": f"dp{n_gpus} (" + ("one batch LPT-sharded over ranks" if args.shard
+                                             else "one batch per rank") + ", weights replicated)",
             "l2": "not flushed: every step streams 8.4 GB of weights and tens of GB of "
                   "activations, far above the 126 MB L2"}
 
@@ -325,7 +339,20 @@ def main():
     eng = cb.Engine(cfg, local)
     eng.init_random(3, 0.02)
     eng.finalize()
-    reqs = workloads.backbone_requests(n=args.requests, seed=3 + 1000 * rank)
+    from clef_b200.sharding import rank_shard
+    prefix = None
+    prefix_ms = None
+    if args.workload == "config5":
+        pre_ids, suffixes = workloads.prefix_workload()
+        reqs = rank_shard(suffixes, rank, world, lambda r: flops_per_request(cfg, len(r), 16384))
+        t0 = time.perf_counter()
+        _, _, prefix = eng.prefill([pre_ids], capture=len(pre_ids), logits=False)
+        prefix_ms = 1000 * (time.perf_counter() - t0)
+    elif args.shard:
+        batch = workloads.backbone_requests(n=args.requests, seed=3)
+        reqs = rank_shard(batch, rank, world, lambda r: flops_per_request(cfg, len(r)))
+    else:
+        reqs = workloads.backbone_requests(n=args.requests, seed=3 + 1000 * rank)
     lens = np.array([len(r) for r in reqs], np.int64)
     offsets = np.zeros(len(reqs) + 1, np.int64)
     offsets[1:] = np.cumsum(lens)
@@ -336,7 +363,7 @@ def main():
     stream = torch.cuda.Stream()
 
     for _ in range(args.warmup):
-        eng.prefill_device(ids_dev, offsets, logits_dev, stream=stream)
+        eng.prefill_device(ids_dev, offsets, logits_dev, initial=prefix, stream=stream)
     torch.cuda.synchronize()
 
     # ---- device-resident timed region ---------------------------------------
@@ -350,7 +377,7 @@ def main():
     torch.cuda.synchronize()
     start.record(stream)
     for _ in range(args.steps):
-        eng.prefill_device(ids_dev, offsets, logits_dev, stream=stream)
+        eng.prefill_device(ids_dev, offsets, logits_dev, initial=prefix, stream=stream)
     end.record(stream)
     torch.cuda.synchronize()
     barrier()
@@ -366,12 +393,12 @@ def main():
     ids_pin = torch.from_numpy(ids).pin_memory()
     lg_pin = torch.empty((len(reqs), 7), dtype=torch.float32).pin_memory()
     ids_np, lg_np = ids_pin.numpy(), lg_pin.numpy()
-    eng.prefill_packed(ids_np, offsets, logits_out=lg_np)
+    eng.prefill_packed(ids_np, offsets, initial=prefix, logits_out=lg_np)
     barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        eng.prefill_packed(ids_np, offsets, logits_out=lg_np)
+        eng.prefill_packed(ids_np, offsets, initial=prefix, logits_out=lg_np)
     e2e_s = (time.perf_counter() - t0) / args.steps
     barrier()
     e2e_max = allmax(e2e_s)
@@ -397,7 +424,8 @@ def main():
                 "frac": round(achieved / peak, 4), "peak_source": f"{pk_kind} bf16_tflops_sustained",
                 "traffic": traffic,
                 "stage_ms_per_step": {k: round(v / args.steps, 3) for k, v in stages.items()}}
-    total_flops = sum(flops_per_request(cfg, int(L)) for L in lens)
+    pre_len = 16384 if prefix is not None else 0
+    total_flops = sum(flops_per_request(cfg, int(L), pre_len) for L in lens)
     line = {"metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
@@ -411,13 +439,16 @@ def main():
                     "h2d_bytes_per_step": int(ids.nbytes + offsets.nbytes),
                     "d2h_bytes_per_step": int(lg_np.nbytes)},
             "gpu_launches": int(launches),
+            "prefix_ms_once_per_gpu": None if prefix_ms is None else round(allmax(prefix_ms), 1),
             "clocks": clocks,
             "decisions_finite": bool(all(np.isfinite([d.noul, d.confidence, d.score]).all()
                                          for d in decisions))}
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "config4":
         line["cpu_baseline"] = cpu_baseline(args, cfg)
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if prefix is not None:
+        prefix.close()
     eng.close()
     if world > 1:
         dist.destroy_process_group()

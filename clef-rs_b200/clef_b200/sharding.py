@@ -32,3 +32,11 @@ def imbalance(costs: Sequence[float], assignment: List[List[int]]) -> float:
     loads = [sum(costs[i] for i in a) for a in assignment]
     mean = sum(loads) / len(loads)
     return max(loads) / mean if mean else 1.0
+
+
+def rank_shard(requests, rank: int, ranks: int, cost):
+    """The requests rank `rank` of `ranks` serves: LPT over cost(request)."""
+    if not 0 <= rank < ranks:
+        raise ValueError("rank out of range")
+    costs = [float(cost(r)) for r in requests]
+    return [requests[i] for i in lpt_assign(costs, ranks)[rank]]

@@ -428,7 +428,9 @@ def main():
     total_flops = sum(flops_per_request(cfg, int(L), pre_len) for L in lens)
     line = {"metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True,
+            "scaling": "strong" if (args.shard or args.workload == "config5") else "weak",
+            "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded ids and random-init weights)",
             "decisions_per_s": round(total_reqs / (ms_max / 1000.0), 2),
             "model_tflops": round(allsum(total_flops) / (ms_max / 1000.0) / 1e12, 1),

@@ -19,6 +19,7 @@ pinned host ids to host logits. `--impl reference` times the CPU F32
 restatement of the reference path (oracle/) on the host cores instead.
 """
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -56,7 +57,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-tokens", type=int, default=256)
     ap.add_argument("--profile-op", default=None,
-                    choices=["gemm", "gemm_swiglu", "scan", "scan1", "attention", "prologue"],
+                    choices=["gemm", "gemm_swiglu", "scan", "scan1", "attention", "attention_tc",
+                             "prologue"],
                     help="run one operator on a profiling-sized case and exit (for ncu)")
     ap.add_argument("--reps", type=int, default=3)
     return ap.parse_args()
@@ -281,6 +283,27 @@ def profile_op(args):
         v = torch.randn(4, T, 256, device=dev).bfloat16()
         for _ in range(args.reps):
             cb.attention_gqa(q, k, v)
+    elif args.profile_op == "attention_tc":
+        # Token-major q/k and transposed V as the engine keeps them; the C ABI
+        # is called directly so only the attention kernel runs per repetition.
+        T, H, Hkv = 4096, 16, 4
+        q = torch.randn(T, H, 256, device=dev).bfloat16()
+        k = torch.randn(T, Hkv, 256, device=dev).bfloat16()
+        vt = torch.randn(Hkv * 256, T, device=dev).bfloat16()
+        o = torch.empty(T, H, 256, device=dev)
+        st = torch.cuda.current_stream()
+        ptr = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        flops = 2 * 2 * H * 256 * (T * (T + 1) // 2)
+        for i in range(args.reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            rc = cb.lib.clef_attention_gqa_vt(ptr(q), ptr(k), ptr(vt), H, Hkv, T, T, 256, T, ptr(o),
+                                              ctypes.c_void_p(st.cuda_stream))
+            e1.record()
+            assert rc == 0, cb.lib.clef_last_error().decode()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1)
+            print(f"attention_tc T={T}: {ms:.3f} ms, {flops / ms / 1e9:.1f} TFLOP/s", flush=True)
     elif args.profile_op == "prologue":
         T, Hk, Hv = 16384, 16, 32
         width = 2 * Hk * 128 + Hv * 128

@@ -31,7 +31,8 @@ EXPORTS = [
     "clef_last_error", "clef_version", "clef_config_validate", "clef_rmsnorm", "clef_conv4",
     "clef_delta_prologue", "clef_delta_scan_workspace_size", "clef_delta_scan",
     "clef_delta_scan_noalloc", "clef_gemm_bf16",
-    "clef_gemm_swiglu", "clef_attention_gqa", "clef_compact_copy", "clef_engine_create",
+    "clef_gemm_swiglu", "clef_attention_gqa", "clef_attention_gqa_vt", "clef_compact_copy",
+    "clef_engine_create",
     "clef_engine_set_weight", "clef_engine_init_random", "clef_engine_get_weight",
     "clef_engine_weight_count", "clef_engine_finalize", "clef_engine_prefill",
     "clef_engine_prefill_device", "clef_engine_launches", "clef_engine_cancel",
@@ -74,6 +75,8 @@ def _load():
         "clef_gemm_bf16": (ctypes.c_int, [_vp, _vp, _i64, _i32, _i32, _i32, _vp, _i64, _vp]),
         "clef_gemm_swiglu": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i32, _i32, _vp, _vp]),
         "clef_attention_gqa": (ctypes.c_int, [_vp, _vp, _vp, _i32, _i32, _i64, _i64, _i32, _vp, _vp]),
+        "clef_attention_gqa_vt": (ctypes.c_int, [_vp, _vp, _vp, _i32, _i32, _i64, _i64, _i32, _i64, _vp,
+                                                 _vp]),
         "clef_compact_copy": (ctypes.c_int, [_vp, _i32, _vp, _vp, _i32, _vp, _vp]),
         "clef_engine_create": (ctypes.c_int, [_vp, _i32, ctypes.POINTER(_vp)]),
         "clef_engine_set_weight": (ctypes.c_int, [_vp, ctypes.c_char_p, _vp, _sz]),
@@ -239,6 +242,28 @@ def attention_gqa(q, k, v, out=None, stream=None):
     _check(lib.clef_attention_gqa(_ptr(q), _ptr(k), _ptr(v), Hq, Hkv, Tq, Tk, d, _ptr(out),
                                   _stream(stream)))
     return out
+
+
+def attention_gqa_tc(q, k, v, out=None, stream=None):
+    """tcgen05 attention: q BF16 [Hq, Tq, 256], k, v BF16 [Hkv, Tk, 256]
+    (head-major like attention_gqa; converted to the kernel's token-major
+    q/k and transposed V here); returns F32 [Hq, Tq, 256]."""
+    import torch
+    Hq, Tq, d = q.shape
+    Hkv, Tk = k.shape[0], k.shape[1]
+    qt = q.transpose(0, 1).contiguous()
+    kt = k.transpose(0, 1).contiguous()
+    pitch = (Tk + 63) // 64 * 64
+    vt = torch.zeros((Hkv * d, pitch), dtype=torch.bfloat16, device=q.device)
+    vt[:, :Tk] = v.permute(0, 2, 1).reshape(Hkv * d, Tk)
+    o = torch.empty((Tq, Hq, d), dtype=torch.float32, device=q.device)
+    _check(lib.clef_attention_gqa_vt(_ptr(qt), _ptr(kt), _ptr(vt), Hq, Hkv, Tq, Tk, d, pitch, _ptr(o),
+                                     _stream(stream)))
+    res = o.transpose(0, 1).contiguous()
+    if out is not None:
+        out.copy_(res)
+        return out
+    return res
 
 
 def compact_copy(src, out=None, stream=None):

@@ -1,0 +1,569 @@
+// attention_tc.cu — causal grouped-query flash attention on the tcgen05
+// tensor cores (head dim 256, BF16 operands, F32 accumulation in TMEM).
+//
+// Same result as ops::attention (crates/core/src/models/ops.rs:62-143):
+// softmax(q k^T / 16 + lower-right causal mask) v per query head, kv head
+// h / (H / Hkv), keys = [shared prefix keys] ++ [the sequence's own keys].
+//
+// CTA = 128 query rows of one (sequence, query head); 6 warps:
+//   warp 0      TMA producer: the Q tile once, then K and V^T tiles of 64 keys
+//               into a two-stage ring (no multicast);
+//   warp 1      allocates 512 TMEM columns; one thread issues
+//               S_j = Q K_j^T (128 x 64, double-buffered in TMEM) and
+//               O += P_j V_j (128 x 256 accumulator in TMEM), with S_{j+2}
+//               issued while the softmax of block j runs;
+//   warps 2..5  one query row per thread: tcgen05.ld of the S row, mask,
+//               online softmax in the log2 domain, P row (BF16) into a
+//               swizzled shared tile for the PV product. The running maximum is
+//               only raised (and O rescaled in TMEM) when a row's maximum grows
+//               by more than 8 in log2 units, so O is rarely touched; the
+//               epilogue normalises O by the row sum and applies the output
+//               gate o * sigmoid(gate) (qwen.rs:519-524).
+// V is consumed transposed (V^T rows = head dimension, keys contiguous) so both
+// products use K-major shared-memory operands with the 128-byte swizzle.
+#include <cudaTypedefs.h>
+
+#include "kernels.cuh"
+#include "sm100.cuh"
+
+namespace clef {
+
+namespace {
+
+using namespace sm100;
+
+constexpr int D = 256;
+constexpr int BQ = 128;
+constexpr int BK = 64;
+constexpr int Q_BYTES = BQ * D * 2;        // 64 KB: 4 atoms of [128 rows x 128 B]
+constexpr int K_BYTES = BK * D * 2;        // 32 KB: 4 atoms of [64 rows x 128 B]
+constexpr int VT_BYTES = D * BK * 2;       // 32 KB: [256 rows x 128 B]
+constexpr int P_BYTES = BQ * BK * 2;       // 16 KB: [128 rows x 128 B]
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = OFF_Q + Q_BYTES;                 // 2 stages
+constexpr int OFF_VT = OFF_K + 2 * K_BYTES;            // 2 stages
+constexpr int OFF_P = OFF_VT + 2 * VT_BYTES;           // 2 buffers
+constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
+constexpr int SMEM = 1024 + OFF_BAR + 256;
+constexpr int THREADS = 192;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t COL_O = 0, COL_S = 256;             // S buffers at 256 and 320
+constexpr float RESCALE_THRESHOLD = 8.f;               // log2 units
+
+struct TcParams {
+  int H, Hkv;
+  int64_t prefix_len;
+  float sl2;                 // scale * log2(e)
+  const int64_t* cu;         // [nseq + 1] token offsets, or null (one sequence of `total`)
+  const int64_t* cu_vt;      // [nseq + 1] padded key offsets of V^T, or null (= 0)
+  const int32_t* cu_qb;      // [nseq + 1] query-block (128-row) offsets, or null
+  int nseq;
+  int64_t total;
+  // output: F32 [t * o_ts + h * o_hs + e] if gate == null, else BF16 gated
+  void* out;
+  int64_t o_ts, o_hs;
+  const uint16_t* gate;
+  int64_t g_ts, g_hs;
+};
+
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+      "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+      "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]));
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void fence_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 2^x by the MUFU instruction (ex2.approx.ftz: relative error ~2^-22, far
+// below the BF16 rounding applied to its result; -inf gives +0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ int find_seq(const int32_t* cu_qb, int nseq, int b) {
+  int lo = 0, hi = nseq - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (cu_qb[mid] <= b) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                        const __grid_constant__ CUtensorMap map_vt, const __grid_constant__ CUtensorMap map_pk,
+                        const __grid_constant__ CUtensorMap map_pvt, TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
+  uint64_t* q_full = bar + 0;
+  uint64_t* kv_full = bar + 1;   // [2]
+  uint64_t* kv_empty = bar + 3;  // [2]
+  uint64_t* s_full = bar + 5;    // [2]
+  uint64_t* p_full = bar + 7;    // [2]
+  uint64_t* pv_done = bar + 9;   // [2]
+  uint64_t* o_final = bar + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 12);
+  uint64_t* drain = bar + 13;    // error path: completion of this CTA's own MMAs
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y;
+  const int kvh = h / (p.H / p.Hkv);
+  int s = 0;
+  int64_t start = 0, len = p.total, vt0 = 0;
+  int qb;
+  if (p.cu) {
+    s = find_seq(p.cu_qb, p.nseq, blockIdx.x);
+    start = p.cu[s];
+    len = p.cu[s + 1] - start;
+    vt0 = p.cu_vt ? p.cu_vt[s] : start;
+    const int nqb = p.cu_qb[s + 1] - p.cu_qb[s];
+    qb = nqb - 1 - (blockIdx.x - p.cu_qb[s]);
+  } else {
+    qb = (int)((len + BQ - 1) / BQ) - 1 - blockIdx.x;
+  }
+  const int64_t q0 = (int64_t)qb * BQ;
+  const int64_t P = p.prefix_len;
+  const int nbp = (int)((P + BK - 1) / BK);                         // prefix key blocks
+  const int nbo = (int)((min(len, q0 + BQ) + BK - 1) / BK);          // own key blocks
+  const int nblk = nbp + nbo;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&pv_done[i], 1);
+    }
+    mbar_init(o_final, 1);
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sbase = smem_u32(sm);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      bool ok = true;
+      int last[2] = {-1, -1};  // last block issued into each stage
+      mbar_expect_tx(q_full, Q_BYTES);
+      for (int a = 0; a < 4; ++a)
+        tma_load_2d(&map_q, q_full, sm + OFF_Q + a * (BQ * 128), h * D + a * 64, (int)(start + q0));
+      for (int j = 0; j < nblk && ok; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1)) {
+          ok = false;
+          break;
+        }
+        mbar_expect_tx(&kv_full[st], K_BYTES + VT_BYTES);
+        last[st] = j;
+        uint8_t* kd = sm + OFF_K + st * K_BYTES;
+        uint8_t* vd = sm + OFF_VT + st * VT_BYTES;
+        if (j < nbp) {
+          for (int a = 0; a < 4; ++a)
+            tma_load_2d(&map_pk, &kv_full[st], kd + a * (BK * 128), kvh * D + a * 64, j * BK);
+          tma_load_2d(&map_pvt, &kv_full[st], vd, j * BK, kvh * D);
+        } else {
+          const int jo = j - nbp;
+          for (int a = 0; a < 4; ++a)
+            tma_load_2d(&map_k, &kv_full[st], kd + a * (BK * 128), kvh * D + a * 64,
+                        (int)(start + (int64_t)jo * BK));
+          tma_load_2d(&map_vt, &kv_full[st], vd, (int)(vt0 + (int64_t)jo * BK), kvh * D);
+        }
+      }
+      if (!ok) {
+        // Let the copies already issued land before the CTA exits (bounded).
+        raise_device_error(kDevAttentionTimeout);
+        mbar_wait(q_full, 0);
+        for (int st = 0; st < 2; ++st)
+          if (last[st] >= 0) mbar_wait(&kv_full[st], (last[st] >> 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_bf16_f32(BQ, BK);
+      constexpr uint32_t idesc_o = idesc_bf16_f32(BQ, D);
+      bool ok = mbar_wait(q_full, 0);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_full[st], (j >> 1) & 1)) return false;
+        tc_fence_after();
+        const uint32_t qa = sbase + OFF_Q, kb = sbase + OFF_K + st * K_BYTES;
+        const uint32_t d = tmem + COL_S + st * BK;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2), in = (kk & 3) * 32;
+          umma_f16(d, desc_k_sw128(qa + off * (BQ * 128) + in), desc_k_sw128(kb + off * (BK * 128) + in),
+                   idesc_s, kk != 0);
+        }
+        umma_commit(&s_full[st]);
+        return true;
+      };
+      if (ok && nblk > 0) ok = issue_s(0);
+      if (ok && nblk > 1) ok = issue_s(1);
+      for (int j = 0; j < nblk && ok; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&p_full[st], (j >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t pa = sbase + OFF_P + st * P_BYTES, vb = sbase + OFF_VT + st * VT_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk)
+          umma_f16(tmem + COL_O, desc_k_sw128(pa + kk * 32), desc_k_sw128(vb + kk * 32), idesc_o,
+                   (j | kk) != 0);
+        umma_commit(&pv_done[st]);
+        umma_commit(&kv_empty[st]);
+        if (j + 2 < nblk) ok = issue_s(j + 2);
+      }
+      if (ok) {
+        umma_commit(o_final);
+      } else {
+        // Wait (bounded) for the MMAs already issued before TMEM is released.
+        raise_device_error(kDevAttentionTimeout);
+        umma_commit(drain);
+        mbar_wait(drain, 0);
+      }
+    }
+  } else {
+    // Softmax warps: row r of the query tile; TMEM lane quarter = warp % 4.
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int64_t qi = q0 + r;  // query index within the sequence
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nblk; ++j) {
+      const int st = j & 1;
+      // Waits end warp-uniformly so the .sync.aligned TMEM accesses below
+      // always run with the full warp.
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[st], (j >> 1) & 1));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t sr[64];
+      tmem_ld_32x32b_x32(tmem + lane_off + COL_S + st * BK, *reinterpret_cast<uint32_t(*)[32]>(sr));
+      tmem_ld_32x32b_x32(tmem + lane_off + COL_S + st * BK + 32,
+                         *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+      tmem_ld_wait();
+      // Visible keys of this row in block j: columns c <= lim. A block every
+      // row of the tile sees in full skips the mask (CTA-uniform branch).
+      const bool pre = j < nbp;
+      const int64_t kbase = pre ? (int64_t)j * BK : (int64_t)(j - nbp) * BK;
+      const bool full = pre ? kbase + BK <= P : kbase + BK - 1 <= q0;
+      if (!full) {
+        const int64_t l64 = pre ? P - 1 - kbase : qi - kbase;
+        const int lim = l64 < -1 ? -1 : (l64 > 63 ? 63 : (int)l64);
+#pragma unroll
+        for (int c = 0; c < 64; ++c)
+          if (c > lim) sr[c] = 0xff800000u;  // -inf
+      }
+      // Row maximum of the raw scores (the scale is positive), four chains.
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < 64; c += 4) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) mx[u] = fmaxf(mx[u], __uint_as_float(sr[c + u]));
+      }
+      const float bmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * p.sl2;
+      // Lazy maximum: raise it (and rescale O) only when it grows by > 8.
+      const bool need = bmax > m_run + RESCALE_THRESHOLD;
+      float alpha = 1.f;
+      if (need) {
+        alpha = exp2f(m_run - bmax);
+        m_run = bmax;
+        l_run *= alpha;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // O holds PV_0 .. PV_{j-1}: wait for the last one, rescale this row.
+        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1));
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(tmem + lane_off + COL_O + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st_32x32b_x32(tmem + lane_off + COL_O + c * 32, o);
+        }
+        tmem_st_wait();
+      }
+      // P buffer st was last read by PV_{j-2}.
+      if (j >= 2) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[st], ((j - 2) >> 1) & 1));
+        if (!ok) break;
+      }
+      // p = 2^(s * scale * log2 e - m), rounded to BF16 as the PV product
+      // consumes it; the row sum adds the rounded values.
+      uint8_t* prow = sm + OFF_P + st * P_BYTES + r * 128;
+      const float neg_m = -m_run;
+      float ps[2] = {0.f, 0.f};
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[ch * 8 + 2 * e]), p.sl2, neg_m));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[ch * 8 + 2 * e + 1]), p.sl2, neg_m));
+          w[e] = pack_bf16x2(p0, p1);
+          ps[0] += __uint_as_float(w[e] << 16);
+          ps[1] += __uint_as_float(w[e] & 0xffff0000u);
+        }
+        *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      l_run += ps[0] + ps[1];
+      fence_async_shared();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[st]);
+    }
+    if (ok && nblk > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_final, 0));
+    if (!ok) {
+      raise_device_error(kDevAttentionTimeout);
+    } else {
+      tc_fence_after();
+      const float inv = 1.f / l_run;
+      const bool valid = qi < len;
+      const int64_t row = start + qi;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(tmem + lane_off + COL_O + c * 32, o);
+        tmem_ld_wait();
+        if (!valid) continue;
+        if (p.gate) {
+          const uint16_t* gp = p.gate + row * p.g_ts + (int64_t)h * p.g_hs + c * 32;
+          uint16_t* op = reinterpret_cast<uint16_t*>(p.out) + row * p.o_ts + (int64_t)h * p.o_hs + c * 32;
+#pragma unroll
+          for (int e4 = 0; e4 < 4; ++e4) {
+            const uint4 graw = *reinterpret_cast<const uint4*>(gp + e4 * 8);
+            const uint32_t gw[4] = {graw.x, graw.y, graw.z, graw.w};
+            uint32_t ow[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float g0 = bf16_round(sigmoid_f(__uint_as_float(gw[e] << 16)));
+              const float g1 = bf16_round(sigmoid_f(__uint_as_float(gw[e] & 0xffff0000u)));
+              const float v0 = bf16_round(__uint_as_float(o[e4 * 8 + 2 * e]) * inv);
+              const float v1 = bf16_round(__uint_as_float(o[e4 * 8 + 2 * e + 1]) * inv);
+              ow[e] = pack_bf16x2(v0 * g0, v1 * g1);
+            }
+            *reinterpret_cast<uint4*>(op + e4 * 8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+          }
+        } else {
+          float* op = reinterpret_cast<float*>(p.out) + row * p.o_ts + (int64_t)h * p.o_hs + c * 32;
+#pragma unroll
+          for (int e4 = 0; e4 < 8; ++e4)
+            *reinterpret_cast<float4*>(op + e4 * 4) =
+                make_float4(__uint_as_float(o[e4 * 4]) * inv, __uint_as_float(o[e4 * 4 + 1]) * inv,
+                            __uint_as_float(o[e4 * 4 + 2]) * inv, __uint_as_float(o[e4 * 4 + 3]) * inv);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// V^T: vt[kvh * 256 + e][vt_off(s) + j] = v[(cu[s] + j) * v_ts + kvh * v_hs + e], one
+// 64-key x 256-feature tile per CTA through shared memory.
+__global__ void transpose_v_kernel(const uint16_t* __restrict__ v, int64_t v_ts, int64_t v_hs,
+                                   const int64_t* __restrict__ cu, const int64_t* __restrict__ cu_vt,
+                                   const int32_t* __restrict__ cu_kb, int nseq, int64_t total,
+                                   uint16_t* __restrict__ vt, int64_t vt_pitch) {
+  __shared__ uint16_t tile[64][D + 8];
+  const int kvh = blockIdx.y;
+  int s = 0;
+  int64_t start = 0, len = total, off = 0;
+  int kb = blockIdx.x;
+  if (cu) {
+    s = find_seq(cu_kb, nseq, blockIdx.x);
+    start = cu[s];
+    len = cu[s + 1] - start;
+    off = cu_vt[s];
+    kb = blockIdx.x - cu_kb[s];
+  }
+  const int64_t j0 = (int64_t)kb * 64;
+  for (int idx = threadIdx.x; idx < 64 * (D / 8); idx += blockDim.x) {
+    const int j = idx / (D / 8), e8 = (idx % (D / 8)) * 8;
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (j0 + j < len) val = *reinterpret_cast<const uint4*>(v + (start + j0 + j) * v_ts + kvh * v_hs + e8);
+    const uint32_t w[4] = {val.x, val.y, val.z, val.w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      tile[j][e8 + 2 * t] = (uint16_t)(w[t] & 0xffff);
+      tile[j][e8 + 2 * t + 1] = (uint16_t)(w[t] >> 16);
+    }
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < D * 8; idx += blockDim.x) {
+    const int e = idx / 8, j8 = (idx % 8) * 8;
+    uint32_t w[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t)
+      w[t] = (uint32_t)tile[j8 + 2 * t][e] | ((uint32_t)tile[j8 + 2 * t + 1][e] << 16);
+    *reinterpret_cast<uint4*>(vt + (int64_t)(kvh * D + e) * vt_pitch + off + j0 + j8) =
+        make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// BF16 matrix [rows, cols] with row pitch `pitch` elements; box = box_rows x 64.
+int map2d(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t cols, uint64_t pitch,
+          uint32_t box_rows) {
+  auto fn = encode();
+  if (!fn) return fail(CLEF_ERR_CUDA, "attention: cuTensorMapEncodeTiled unavailable");
+  CLEF_CHECK(((uintptr_t)ptr & 15) == 0 && (pitch * 2) % 16 == 0, CLEF_ERR_INVALID,
+             "attention: tensor base and row pitch must be 16-byte aligned");
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {pitch * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(CLEF_ERR_CUDA, "attention: cuTensorMapEncodeTiled failed");
+  return CLEF_OK;
+}
+
+}  // namespace
+
+int launch_transpose_v(const uint16_t* v, int64_t v_ts, int64_t v_hs, const SeqPackVT& pk, int Hkv,
+                       uint16_t* vt, int64_t vt_pitch, cudaStream_t s) {
+  if (pk.total == 0) return CLEF_OK;
+  const unsigned blocks = pk.cu ? (unsigned)pk.kblocks : (unsigned)ceil_div(pk.total, 64);
+  transpose_v_kernel<<<dim3(blocks, (unsigned)Hkv), 256, 0, s>>>(v, v_ts, v_hs, pk.cu, pk.cu_vt, pk.cu_kb,
+                                                              pk.nseq, pk.total, vt, vt_pitch);
+  return launch_status("transpose_v");
+}
+
+int launch_attention_tc(const AttnTcArgs& a, const SeqPackVT& pk, cudaStream_t s) {
+  CLEF_CHECK(a.H > 0 && a.Hkv > 0 && a.H % a.Hkv == 0, CLEF_ERR_INVALID, "attention_tc: heads");
+  if (pk.total == 0) return CLEF_OK;
+  CLEF_CHECK(a.rows_q < (1LL << 31) && a.vt_cols < (1LL << 31), CLEF_ERR_UNSUPPORTED,
+             "attention_tc: tensors too large for 32-bit TMA coordinates");
+  CUtensorMap mq, mk, mvt, mpk, mpvt;
+  int rc = map2d(&mq, a.q, (uint64_t)a.rows_q, (uint64_t)a.H * D, (uint64_t)a.H * D, BQ);
+  if (!rc) rc = map2d(&mk, a.k, (uint64_t)a.rows_k, (uint64_t)a.Hkv * D, (uint64_t)a.Hkv * D, BK);
+  if (!rc) rc = map2d(&mvt, a.vt, (uint64_t)a.Hkv * D, (uint64_t)a.vt_cols, (uint64_t)a.vt_pitch, D);
+  if (rc) return rc;
+  if (a.prefix_len > 0) {
+    rc = map2d(&mpk, a.pk, (uint64_t)a.prefix_len, (uint64_t)a.Hkv * D, (uint64_t)a.Hkv * D, BK);
+    if (!rc)
+      rc = map2d(&mpvt, a.pvt, (uint64_t)a.Hkv * D, (uint64_t)a.prefix_len, (uint64_t)a.pvt_pitch, D);
+    if (rc) return rc;
+  } else {
+    mpk = mk;
+    mpvt = mvt;
+  }
+  TcParams p;
+  p.H = a.H;
+  p.Hkv = a.Hkv;
+  p.prefix_len = a.prefix_len;
+  p.sl2 = a.scale * 1.4426950408889634f;
+  p.cu = pk.cu;
+  p.cu_vt = pk.cu_vt;
+  p.cu_qb = pk.cu_qb;
+  p.nseq = pk.nseq;
+  p.total = pk.total;
+  p.out = a.out;
+  p.o_ts = a.o_ts;
+  p.o_hs = a.o_hs;
+  p.gate = a.gate;
+  p.g_ts = a.g_ts;
+  p.g_hs = a.g_hs;
+  static bool attr[64] = {false};
+  int dev = 0;
+  CLEF_CUDA(cudaGetDevice(&dev));
+  if (dev >= 0 && dev < 64 && !attr[dev]) {
+    CLEF_CUDA(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+    attr[dev] = true;
+  }
+  const unsigned blocks = pk.cu ? (unsigned)pk.qblocks : (unsigned)ceil_div(pk.total, BQ);
+  attention_tc_kernel<<<dim3(blocks, (unsigned)a.H), THREADS, SMEM, s>>>(mq, mk, mvt, mpk, mpvt, p);
+  return launch_status("attention_tc");
+}
+
+int attention_tc_device_error(int* code) { return read_device_error(code); }
+
+}  // namespace clef
+
+using namespace clef;
+
+extern "C" {
+
+int clef_attention_gqa_vt(const uint16_t* q, const uint16_t* k, const uint16_t* vt, int32_t Hq,
+                          int32_t Hkv, int64_t Tq, int64_t Tk, int32_t d, int64_t vt_pitch,
+                          float* out, void* stream) {
+  CLEF_CHECK(q && k && vt && out, CLEF_ERR_INVALID, "attention_gqa_vt: null pointer");
+  CLEF_CHECK(d == 256, CLEF_ERR_UNSUPPORTED, "attention_gqa_vt: d must be 256");
+  CLEF_CHECK(Hq > 0 && Hkv > 0 && Hq % Hkv == 0, CLEF_ERR_INVALID, "attention_gqa_vt: head counts");
+  CLEF_CHECK(Tq > 0 && Tk >= Tq, CLEF_ERR_INVALID, "attention_gqa_vt: need 0 < Tq <= Tk");
+  const int64_t pre = Tk - Tq;
+  CLEF_CHECK(pre % 8 == 0, CLEF_ERR_UNSUPPORTED,
+             "attention_gqa_vt: Tk - Tq must be a multiple of 8 (16-byte aligned V^T columns)");
+  CLEF_CHECK(vt_pitch >= Tk && vt_pitch % 8 == 0, CLEF_ERR_INVALID, "attention_gqa_vt: vt_pitch");
+  CLEF_CHECK((((uintptr_t)q | (uintptr_t)k | (uintptr_t)vt | (uintptr_t)out) & 15) == 0,
+             CLEF_ERR_INVALID, "attention_gqa_vt: pointers must be 16-byte aligned");
+  AttnTcArgs a;
+  a.H = Hq;
+  a.Hkv = Hkv;
+  a.scale = 1.f / 16.f;
+  a.q = q;
+  a.rows_q = Tq;
+  a.k = k + pre * Hkv * 256;
+  a.rows_k = Tq;
+  a.vt = vt + pre;
+  a.vt_cols = Tq;
+  a.vt_pitch = vt_pitch;
+  a.prefix_len = pre;
+  a.pk = k;
+  a.pvt = vt;
+  a.pvt_pitch = vt_pitch;
+  a.out = out;
+  a.o_ts = (int64_t)Hq * 256;
+  a.o_hs = 256;
+  SeqPackVT pk;
+  pk.nseq = 1;
+  pk.total = Tq;
+  return launch_attention_tc(a, pk, as_stream(stream));
+}
+
+}  // extern "C"

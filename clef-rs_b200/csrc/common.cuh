@@ -69,6 +69,7 @@ static inline int read_device_error(int* code) {
 // Synchronises the current device and collects every kernel family's flag.
 int device_errors(int* code);
 int gemm_device_error(int* code);
+int attention_tc_device_error(int* code);
 
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
@@ -89,8 +90,12 @@ __device__ __forceinline__ uint16_t f2bf(float x) {
 __device__ __forceinline__ float bf2f(uint16_t u) {
   return __uint_as_float(((uint32_t)u) << 16);
 }
+// Two round-to-nearest-even BF16 conversions in one instruction; `lo` lands
+// in the low half (lower address).
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  return (uint32_t)f2bf(lo) | ((uint32_t)f2bf(hi) << 16);
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
 }
 
 // Candle's CPU definitions: sigmoid = 1 / (1 + exp(-x)), silu = x / (1 + exp(-x)).

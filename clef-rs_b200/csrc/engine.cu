@@ -70,13 +70,14 @@ struct clef_prefix {
   int device = 0;
   int64_t tokens = 0;
   int hidden = 0;
+  int64_t vt_pitch = 0;
   void* blob = nullptr;
   uint64_t bytes = 0;
   float* hidden_rows = nullptr;  // [tokens, hidden]
   struct Layer {
     bool full = false;
-    uint16_t* k = nullptr;  // [tokens, Hkv, d]
-    uint16_t* v = nullptr;
+    uint16_t* k = nullptr;   // [tokens, Hkv, d] (post-RoPE keys)
+    uint16_t* vt = nullptr;  // [Hkv * d, vt_pitch] values, transposed (keys contiguous)
     float* S = nullptr;     // [Hv, 128, 128]
     float* hist = nullptr;  // [hist_rows, qkv width]
     int hist_rows = 0;
@@ -109,6 +110,8 @@ struct clef_engine {
   float *h = nullptr, *proj = nullptr, *dq = nullptr, *dk = nullptr, *dv = nullptr, *dg = nullptr,
         *db = nullptr, *dout = nullptr, *logits_d = nullptr;
   uint16_t *u = nullptr, *y = nullptr, *qatt = nullptr, *katt = nullptr, *act = nullptr;
+  uint16_t* vt = nullptr;  // [Hkv * d, vt_pitch] transposed values of the pack
+  int64_t vt_pitch = 0;
   void* scan_ws = nullptr;
   size_t scan_ws_bytes = 0;
   // profiling
@@ -281,6 +284,14 @@ struct DeviceGuard {
   }
 };
 
+// Per-pack device offsets for n1 = sequences + 1 entries: int64 cu | int32
+// 64-row q-blocks | (8-byte aligned) int64 padded V^T offsets | int32 128-row
+// q-blocks | int32 64-key blocks.
+size_t meta_vt_offset(size_t n1) { return (n1 * (sizeof(int64_t) + sizeof(int32_t)) + 7) / 8 * 8; }
+size_t meta_bytes(size_t n1) {
+  return meta_vt_offset(n1) + n1 * (sizeof(int64_t) + 2 * sizeof(int32_t)) + 64;
+}
+
 int ensure_capacity(clef_engine* e, int64_t tokens, int64_t seqs) {
   if (tokens <= e->cap_tokens && seqs <= e->cap_seqs && e->arena) return CLEF_OK;
   const clef_config& c = e->cfg;
@@ -296,7 +307,7 @@ int ensure_capacity(clef_engine* e, int64_t tokens, int64_t seqs) {
     b = a256(b + n);
   };
   take(sizeof(int32_t) * M);                              // 0 ids
-  take((sizeof(int64_t) + sizeof(int32_t)) * (seqs + 1) + 16);  // 1 meta
+  take(meta_bytes((size_t)seqs + 1));                     // 1 meta
   take(sizeof(float) * M * hid);                          // 2 h
   take(std::max(sizeof(float) * M * e->n_in, sizeof(uint16_t) * M * e->n_att));  // 3 proj
   take(sizeof(float) * M * e->key);                       // 4 dq
@@ -313,6 +324,8 @@ int ensure_capacity(clef_engine* e, int64_t tokens, int64_t seqs) {
   take(sizeof(float) * seqs * std::max(1, c.head_outputs));  // 15 logits
   const size_t ws = delta_scan_workspace(M, (int)seqs, c.linear_num_key_heads, hv);
   take(ws);                                               // 16 scan ws
+  const int64_t vt_pitch = (M + 64 * seqs + 63) / 64 * 64;
+  take(sizeof(uint16_t) * (size_t)vt_pitch * e->att_kv);  // 17 V^T
   if (e->arena) cudaFree(e->arena);
   e->arena = nullptr;
   if (cudaMalloc(&e->arena, b) != cudaSuccess)
@@ -335,6 +348,8 @@ int ensure_capacity(clef_engine* e, int64_t tokens, int64_t seqs) {
   e->act = (uint16_t*)(p + o[14]);
   e->logits_d = (float*)(p + o[15]);
   e->scan_ws = p + o[16];
+  e->vt = (uint16_t*)(p + o[17]);
+  e->vt_pitch = vt_pitch;
   e->scan_ws_bytes = ws;
   e->arena_bytes = b;
   e->cap_tokens = tokens;
@@ -384,11 +399,12 @@ int alloc_prefix(clef_engine* e, int64_t tokens, clef_prefix** out) {
   };
   take(sizeof(float) * tokens * c.hidden_size);
   uint64_t logical = sizeof(float) * tokens * c.hidden_size;
+  p->vt_pitch = (tokens + 63) / 64 * 64;
   p->layers.resize(c.num_hidden_layers);
   for (int i = 0; i < c.num_hidden_layers; ++i) {
     if (c.layer_types[i]) {
       take(sizeof(uint16_t) * tokens * e->att_kv);
-      take(sizeof(uint16_t) * tokens * e->att_kv);
+      take(sizeof(uint16_t) * p->vt_pitch * e->att_kv);
       logical += 2 * sizeof(uint16_t) * tokens * e->att_kv;
     } else {
       const int64_t rows = std::min<int64_t>(tokens, 3);
@@ -409,7 +425,7 @@ int alloc_prefix(clef_engine* e, int64_t tokens, clef_prefix** out) {
     L.full = c.layer_types[i] != 0;
     if (L.full) {
       L.k = (uint16_t*)(base + o[k++]);
-      L.v = (uint16_t*)(base + o[k++]);
+      L.vt = (uint16_t*)(base + o[k++]);
     } else {
       L.S = (float*)(base + o[k++]);
       L.hist = (float*)(base + o[k++]);
@@ -454,18 +470,43 @@ int run_pack(clef_engine* e, const int32_t* ids, const int64_t* offsets, int s0,
   // Offsets: int64 cu (rebased) then int32 q-block offsets.
   std::vector<int64_t> cu(np + 1);
   for (int i = 0; i <= np; ++i) cu[i] = offsets[s0 + i] - t0;
-  std::vector<char> meta((np + 1) * (sizeof(int64_t) + sizeof(int32_t)));
-  memcpy(meta.data(), cu.data(), sizeof(int64_t) * (np + 1));
-  int32_t* qb = reinterpret_cast<int32_t*>(meta.data() + sizeof(int64_t) * (np + 1));
-  qb[0] = 0;
-  for (int i = 0; i < np; ++i) qb[i + 1] = qb[i] + (int32_t)ceil_div(cu[i + 1] - cu[i], 64);
+  // Device offsets: int64 cu | int32 64-row q-blocks | int64 padded V^T
+  // offsets | int32 128-row q-blocks | int32 64-key blocks.
+  const size_t n1 = (size_t)np + 1;
+  std::vector<char> meta(meta_bytes(n1));
+  int64_t* m_cu = reinterpret_cast<int64_t*>(meta.data());
+  int32_t* qb = reinterpret_cast<int32_t*>(m_cu + n1);
+  const size_t vt_off_bytes = meta_vt_offset(n1);
+  int64_t* m_vt = reinterpret_cast<int64_t*>(meta.data() + vt_off_bytes);
+  int32_t* qb128 = reinterpret_cast<int32_t*>(m_vt + n1);
+  int32_t* kb64 = qb128 + n1;
+  memcpy(m_cu, cu.data(), sizeof(int64_t) * n1);
+  qb[0] = qb128[0] = kb64[0] = 0;
+  m_vt[0] = 0;
+  for (int i = 0; i < np; ++i) {
+    const int64_t L = cu[i + 1] - cu[i];
+    qb[i + 1] = qb[i] + (int32_t)ceil_div(L, 64);
+    qb128[i + 1] = qb128[i] + (int32_t)ceil_div(L, 128);
+    kb64[i + 1] = kb64[i] + (int32_t)ceil_div(L, 64);
+    m_vt[i + 1] = m_vt[i] + ceil_div(L, 64) * 64;
+  }
+  CLEF_CHECK(m_vt[np] <= e->vt_pitch, CLEF_ERR_INVALID, "prefill: V^T buffer too small");
   CLEF_CUDA(cudaMemcpyAsync(e->meta_d, meta.data(), meta.size(), cudaMemcpyHostToDevice, s));
+  SeqPackVT vpack;
+  vpack.cu = e->meta_d;
+  vpack.cu_vt = reinterpret_cast<const int64_t*>(reinterpret_cast<const char*>(e->meta_d) + vt_off_bytes);
+  vpack.cu_qb = reinterpret_cast<const int32_t*>(vpack.cu_vt + n1);
+  vpack.cu_kb = vpack.cu_qb + n1;
+  vpack.nseq = np;
+  vpack.total = M;
+  vpack.qblocks = qb128[np];
+  vpack.kblocks = kb64[np];
   const int32_t* ids_src = e->ids_d;
   if (ids_dev) ids_src = ids_dev + t0;
   else CLEF_CUDA(cudaMemcpyAsync(e->ids_d, ids + t0, sizeof(int32_t) * M, cudaMemcpyHostToDevice, s));
   {
     int64_t n = 2;  // embed + head
-    for (int li = 0; li < c.num_hidden_layers; ++li) n += c.layer_types[li] ? 8 : 9;
+    for (int li = 0; li < c.num_hidden_layers; ++li) n += 9;  // 2 norms, 4 GEMMs, 3 mixer kernels
     if (hidden || cap) n += 1;
     e->launches += n;
   }
@@ -539,31 +580,34 @@ int run_pack(clef_engine* e, const int32_t* ids, const int64_t* offsets, int s0,
                                      e->inv_freq, e->qatt, e->katt, s));
       }
       const int v_col = 2 * e->att_n + e->att_kv;
+      {
+        STAGE(kStAttnPro);
+        RC(launch_transpose_v(pb + v_col, L.n_att, d, vpack, Hkv, e->vt, e->vt_pitch, s));
+      }
       if (cap) {
         auto& cl = cap->layers[li];
         RC(launch_copy_rows(e->katt, e->att_kv, 0, capture, e->att_kv, 2, cl.k, e->att_kv, s));
-        RC(launch_copy_rows(pb + v_col, L.n_att, 0, capture, e->att_kv, 2, cl.v, e->att_kv, s));
+        // V^T columns [0, capture) of the single captured sequence.
+        CLEF_CUDA(cudaMemcpy2DAsync(cl.vt, sizeof(uint16_t) * cap->vt_pitch, e->vt,
+                                    sizeof(uint16_t) * e->vt_pitch, sizeof(uint16_t) * capture,
+                                    (size_t)e->att_kv, cudaMemcpyDeviceToDevice, s));
       }
-      AttnArgs a;
+      AttnTcArgs a;
       a.H = H;
       a.Hkv = Hkv;
-      a.d = d;
       a.scale = (float)(1.0 / std::sqrt((double)d));
       a.q = e->qatt;
-      a.q_ts = (int64_t)H * d;
-      a.q_hs = d;
+      a.rows_q = M;
       a.k = e->katt;
-      a.k_ts = e->att_kv;
-      a.k_hs = d;
-      a.v = pb + v_col;
-      a.v_ts = L.n_att;
-      a.v_hs = d;
+      a.rows_k = M;
+      a.vt = e->vt;
+      a.vt_cols = e->vt_pitch;
+      a.vt_pitch = e->vt_pitch;
       if (init) {
-        a.pk = init->layers[li].k;
-        a.pv = init->layers[li].v;
-        a.p_ts = e->att_kv;
-        a.p_hs = d;
         a.prefix_len = P;
+        a.pk = init->layers[li].k;
+        a.pvt = init->layers[li].vt;
+        a.pvt_pitch = init->vt_pitch;
       }
       a.gate = pb + d;
       a.g_ts = L.n_att;
@@ -573,7 +617,7 @@ int run_pack(clef_engine* e, const int32_t* ids, const int64_t* offsets, int s0,
       a.o_hs = d;
       {
         STAGE(kStAttn);
-        RC(launch_attention(a, pack, s));
+        RC(launch_attention_tc(a, vpack, s));
       }
       {
         STAGE(kStGemm);

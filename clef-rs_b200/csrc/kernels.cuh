@@ -117,4 +117,41 @@ struct AttnArgs {
 };
 int launch_attention(const AttnArgs& a, const SeqPack& pack, cudaStream_t s);
 
+// ---- attention_tc.cu --------------------------------------------------------
+// Packed sequences for the tcgen05 attention: token offsets, padded V^T column
+// offsets (each sequence starts at a multiple of 64 keys so every TMA
+// coordinate is 16-byte aligned), 128-row query-block offsets and 64-key
+// block offsets. All device arrays; cu == null means one sequence of `total`.
+struct SeqPackVT {
+  const int64_t* cu = nullptr;
+  const int64_t* cu_vt = nullptr;
+  const int32_t* cu_qb = nullptr;
+  const int32_t* cu_kb = nullptr;
+  int nseq = 1;
+  int64_t total = 0, qblocks = 0, kblocks = 0;
+};
+struct AttnTcArgs {
+  int H = 0, Hkv = 0;
+  float scale = 0.0625f;
+  const uint16_t* q = nullptr;   // [rows_q, H, 256]
+  int64_t rows_q = 0;
+  const uint16_t* k = nullptr;   // [rows_k, Hkv, 256] own keys
+  int64_t rows_k = 0;
+  const uint16_t* vt = nullptr;  // [Hkv * 256, vt_pitch] own values, transposed
+  int64_t vt_cols = 0, vt_pitch = 0;
+  int64_t prefix_len = 0;        // shared prefix keys every sequence sees first
+  const uint16_t* pk = nullptr;  // [prefix_len, Hkv, 256]
+  const uint16_t* pvt = nullptr; // [Hkv * 256, pvt_pitch]
+  int64_t pvt_pitch = 0;
+  void* out = nullptr;           // F32 (gate null) or BF16 o * sigmoid(gate)
+  int64_t o_ts = 0, o_hs = 0;
+  const uint16_t* gate = nullptr;
+  int64_t g_ts = 0, g_hs = 0;
+};
+int launch_attention_tc(const AttnTcArgs& a, const SeqPackVT& pk, cudaStream_t s);
+// vt[kvh * 256 + e][cu_vt[s] + j] = v[(cu[s] + j) * v_ts + kvh * v_hs + e].
+int launch_transpose_v(const uint16_t* v, int64_t v_ts, int64_t v_hs, const SeqPackVT& pk, int Hkv,
+                       uint16_t* vt, int64_t vt_pitch, cudaStream_t s);
+int attention_tc_device_error(int* code);
+
 }  // namespace clef

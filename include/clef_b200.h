@@ -193,6 +193,15 @@ int clef_attention_gqa(const uint16_t* q, const uint16_t* k, const uint16_t* v, 
                        int32_t Hkv, int64_t Tq, int64_t Tk, int32_t d, float* out,
                        void* stream);
 
+/* The same attention on the tcgen05 tensor cores, in the engine's layouts:
+ * q BF16 [Tq, Hq, 256] and k BF16 [Tk, Hkv, 256] token-major; V given
+ * transposed, vt BF16 [Hkv * 256, vt_pitch] (row = kv head * 256 + feature,
+ * column = key); out F32 [Tq, Hq, 256]. Keys [0, Tk - Tq) act as a shared
+ * prefix; Tk - Tq and vt_pitch must be multiples of 8. */
+int clef_attention_gqa_vt(const uint16_t* q, const uint16_t* k, const uint16_t* vt, int32_t Hq,
+                          int32_t Hkv, int64_t Tq, int64_t Tk, int32_t d, int64_t vt_pitch,
+                          float* out, void* stream);
+
 /* Contiguous copy of a strided view (up to 4 dims, element size 2 or 4).
  * Replaces CompactCopy (metal.rs:26-77). */
 int clef_compact_copy(const void* src, int32_t ndim, const int64_t* dims,

@@ -156,6 +156,25 @@ def test_attention_gqa(Hq, Hkv, Tq, prefix):
     assert err <= 5e-3
 
 
+@pytest.mark.parametrize("Hq,Hkv,Tq,prefix", [(2, 1, 1, 0), (2, 1, 17, 0), (16, 4, 64, 0),
+                                              (16, 4, 257, 0), (2, 1, 1, 256), (2, 1, 17, 256),
+                                              (16, 4, 257, 256), (4, 1, 1000, 40), (16, 4, 129, 64)])
+def test_attention_tcgen05(Hq, Hkv, Tq, prefix):
+    """tcgen05 path (clef_attention_gqa_vt): same tolerance as the mma.sync path."""
+    import clef_b200 as cb
+    d = 256
+    Tk = Tq + prefix
+    q = bf16_round(np.sin(np.arange(Hq * Tq * d, dtype=np.float32) * np.float32(0.017)).reshape(Hq, Tq, d))
+    k = bf16_round(np.cos(np.arange(Hkv * Tk * d, dtype=np.float32) * np.float32(0.031)).reshape(Hkv, Tk, d))
+    rng = np.random.default_rng(Tq + 7)
+    v = bf16_round(rng.standard_normal((Hkv, Tk, d)).astype(np.float32))
+    ref = oracle.attention(q, k, v, causal=True)
+    out = cb.attention_gqa_tc(dev(q).bfloat16(), dev(k).bfloat16(), dev(v).bfloat16()).cpu().numpy()
+    err = np.abs(out - ref).max()
+    print(f"attention tcgen05 {Hq}/{Hkv} Tq={Tq} prefix={prefix}: {err:.3e}")
+    assert np.isfinite(out).all() and err <= 5e-3
+
+
 def test_compact_copy_of_strided_view():
     import clef_b200 as cb
     src = torch.arange(4 * 8 * 128, dtype=torch.float32, device="cuda").reshape(4, 8, 128)

@@ -39,10 +39,12 @@ constexpr int Q_BYTES = BQ * D * 2;        // 64 KB: 4 atoms of [128 rows x 128 
 constexpr int K_BYTES = BK * D * 2;        // 32 KB: 4 atoms of [64 rows x 128 B]
 constexpr int VT_BYTES = D * BK * 2;       // 32 KB: [256 rows x 128 B]
 constexpr int P_BYTES = BQ * BK * 2;       // 16 KB: [128 rows x 128 B]
+constexpr int TILE_BYTES = 32 * 1024;      // one ring slot: a K tile or a V^T tile
+static_assert(K_BYTES == TILE_BYTES && VT_BYTES == TILE_BYTES, "ring slots hold K or V^T tiles");
+constexpr int NSLOT = 4;
 constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + Q_BYTES;                 // 2 stages
-constexpr int OFF_VT = OFF_K + 2 * K_BYTES;            // 2 stages
-constexpr int OFF_P = OFF_VT + 2 * VT_BYTES;           // 2 buffers
+constexpr int OFF_RING = OFF_Q + Q_BYTES;               // NSLOT slots
+constexpr int OFF_P = OFF_RING + NSLOT * TILE_BYTES;    // 2 buffers
 constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
 constexpr int SMEM = 1024 + OFF_BAR + 256;
 constexpr int THREADS = 192;
@@ -104,19 +106,22 @@ __device__ __forceinline__ int find_seq(const int32_t* cu_qb, int nseq, int b) {
 __global__ void __launch_bounds__(THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                         const __grid_constant__ CUtensorMap map_vt, const __grid_constant__ CUtensorMap map_pk,
-                        const __grid_constant__ CUtensorMap map_pvt, TcParams p) {
+                        const __grid_constant__ CUtensorMap map_pvt, const __grid_constant__ CUtensorMap map_g,
+                        TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
   uint64_t* q_full = bar + 0;
-  uint64_t* kv_full = bar + 1;   // [2]
-  uint64_t* kv_empty = bar + 3;  // [2]
-  uint64_t* s_full = bar + 5;    // [2]
-  uint64_t* p_full = bar + 7;    // [2]
-  uint64_t* pv_done = bar + 9;   // [2]
-  uint64_t* o_final = bar + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 12);
-  uint64_t* drain = bar + 13;    // error path: completion of this CTA's own MMAs
+  uint64_t* s_full = bar + 1;    // [2]
+  uint64_t* p_full = bar + 3;    // [2]
+  uint64_t* pv_done = bar + 5;   // [2]
+  uint64_t* o_final = bar + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 8);
+  uint64_t* drain = bar + 9;     // error path: completion of this CTA's own MMAs
+  uint64_t* q_free = bar + 10;   // the last S product has read Q
+  uint64_t* g_full = bar + 11;   // gate tile landed in the Q buffer
+  uint64_t* full = bar + 12;     // [NSLOT] ring slot loaded
+  uint64_t* empty = bar + 12 + NSLOT;  // [NSLOT] ring slot consumed
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y;
@@ -142,15 +147,19 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    for (int i = 0; i < NSLOT; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);
       mbar_init(&pv_done[i], 1);
     }
     mbar_init(o_final, 1);
     mbar_init(drain, 1);
+    mbar_init(q_free, 1);
+    mbar_init(g_full, 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -166,38 +175,57 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       bool ok = true;
-      int last[2] = {-1, -1};  // last block issued into each stage
+      // The K and V^T tiles go through one ring in the order the MMA issuer
+      // consumes them: K_0, K_1, then V_j, K_{j+2} for j = 0, 1, ...
+      int t = 0;
+      int last[NSLOT];
+      for (int i = 0; i < NSLOT; ++i) last[i] = -1;
       mbar_expect_tx(q_full, Q_BYTES);
       for (int a = 0; a < 4; ++a)
         tma_load_2d(&map_q, q_full, sm + OFF_Q + a * (BQ * 128), h * D + a * 64, (int)(start + q0));
-      for (int j = 0; j < nblk && ok; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1)) {
-          ok = false;
-          break;
-        }
-        mbar_expect_tx(&kv_full[st], K_BYTES + VT_BYTES);
-        last[st] = j;
-        uint8_t* kd = sm + OFF_K + st * K_BYTES;
-        uint8_t* vd = sm + OFF_VT + st * VT_BYTES;
-        if (j < nbp) {
-          for (int a = 0; a < 4; ++a)
-            tma_load_2d(&map_pk, &kv_full[st], kd + a * (BK * 128), kvh * D + a * 64, j * BK);
-          tma_load_2d(&map_pvt, &kv_full[st], vd, j * BK, kvh * D);
+      auto load_tile = [&](bool is_k, int j) -> bool {
+        const int slot = t % NSLOT;
+        if (!mbar_wait(&empty[slot], ((t / NSLOT) & 1) ^ 1)) return false;
+        mbar_expect_tx(&full[slot], TILE_BYTES);
+        last[slot] = t++;
+        uint8_t* dst = sm + OFF_RING + slot * TILE_BYTES;
+        const bool pre = j < nbp;
+        if (is_k) {
+          const CUtensorMap* m = pre ? &map_pk : &map_k;
+          const int row = pre ? j * BK : (int)(start + (int64_t)(j - nbp) * BK);
+          for (int a = 0; a < 4; ++a) tma_load_2d(m, &full[slot], dst + a * (BK * 128), kvh * D + a * 64, row);
+        } else if (pre) {
+          tma_load_2d(&map_pvt, &full[slot], dst, j * BK, kvh * D);
         } else {
-          const int jo = j - nbp;
+          tma_load_2d(&map_vt, &full[slot], dst, (int)(vt0 + (int64_t)(j - nbp) * BK), kvh * D);
+        }
+        return true;
+      };
+      for (int j = 0; j < 2 && j < nblk && ok; ++j) ok = load_tile(true, j);
+      for (int j = 0; j < nblk && ok; ++j) {
+        ok = load_tile(false, j);
+        if (ok && j + 2 < nblk) ok = load_tile(true, j + 2);
+      }
+      // The gate tile of the output epilogue goes into the Q buffer once the
+      // last S product has consumed Q: it is in shared memory before O is final.
+      bool gate_issued = false;
+      if (ok && p.gate) {
+        ok = mbar_wait(q_free, 0);
+        if (ok) {
+          mbar_expect_tx(g_full, Q_BYTES);
           for (int a = 0; a < 4; ++a)
-            tma_load_2d(&map_k, &kv_full[st], kd + a * (BK * 128), kvh * D + a * 64,
-                        (int)(start + (int64_t)jo * BK));
-          tma_load_2d(&map_vt, &kv_full[st], vd, (int)(vt0 + (int64_t)jo * BK), kvh * D);
+            tma_load_2d(&map_g, g_full, sm + OFF_Q + a * (BQ * 128), h * (int)p.g_hs + a * 64,
+                        (int)(start + q0));
+          gate_issued = true;
         }
       }
       if (!ok) {
         // Let the copies already issued land before the CTA exits (bounded).
         raise_device_error(kDevAttentionTimeout);
         mbar_wait(q_full, 0);
-        for (int st = 0; st < 2; ++st)
-          if (last[st] >= 0) mbar_wait(&kv_full[st], (last[st] >> 1) & 1);
+        for (int i = 0; i < NSLOT; ++i)
+          if (last[i] >= 0) mbar_wait(&full[i], (last[i] / NSLOT) & 1);
+        if (gate_issued) mbar_wait(g_full, 0);
       }
     }
   } else if (warp == 1) {
@@ -205,11 +233,19 @@ __global__ void __launch_bounds__(THREADS, 1)
       constexpr uint32_t idesc_s = idesc_bf16_f32(BQ, BK);
       constexpr uint32_t idesc_o = idesc_bf16_f32(BQ, D);
       bool ok = mbar_wait(q_full, 0);
+      int t = 0;  // ring position, same order as the producer
+      auto take = [&]() -> int {
+        const int slot = t % NSLOT;
+        if (!mbar_wait(&full[slot], (t / NSLOT) & 1)) return -1;
+        ++t;
+        tc_fence_after();
+        return slot;
+      };
       auto issue_s = [&](int j) -> bool {
         const int st = j & 1;
-        if (!mbar_wait(&kv_full[st], (j >> 1) & 1)) return false;
-        tc_fence_after();
-        const uint32_t qa = sbase + OFF_Q, kb = sbase + OFF_K + st * K_BYTES;
+        const int slot = take();
+        if (slot < 0) return false;
+        const uint32_t qa = sbase + OFF_Q, kb = sbase + OFF_RING + slot * TILE_BYTES;
         const uint32_t d = tmem + COL_S + st * BK;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -217,7 +253,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           umma_f16(d, desc_k_sw128(qa + off * (BQ * 128) + in), desc_k_sw128(kb + off * (BK * 128) + in),
                    idesc_s, kk != 0);
         }
+        umma_commit(&empty[slot]);
         umma_commit(&s_full[st]);
+        if (j == nblk - 1) umma_commit(q_free);
         return true;
       };
       if (ok && nblk > 0) ok = issue_s(0);
@@ -228,14 +266,18 @@ __global__ void __launch_bounds__(THREADS, 1)
           ok = false;
           break;
         }
-        tc_fence_after();
-        const uint32_t pa = sbase + OFF_P + st * P_BYTES, vb = sbase + OFF_VT + st * VT_BYTES;
+        const int slot = take();
+        if (slot < 0) {
+          ok = false;
+          break;
+        }
+        const uint32_t pa = sbase + OFF_P + st * P_BYTES, vb = sbase + OFF_RING + slot * TILE_BYTES;
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk)
           umma_f16(tmem + COL_O, desc_k_sw128(pa + kk * 32), desc_k_sw128(vb + kk * 32), idesc_o,
                    (j | kk) != 0);
+        umma_commit(&empty[slot]);
         umma_commit(&pv_done[st]);
-        umma_commit(&kv_empty[st]);
         if (j + 2 < nblk) ok = issue_s(j + 2);
       }
       if (ok) {
@@ -341,6 +383,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (lane == 0) mbar_arrive(&p_full[st]);
     }
     if (ok && nblk > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_final, 0));
+    if (ok && p.gate) ok = __all_sync(0xffffffffu, mbar_wait(g_full, 0));
     if (!ok) {
       raise_device_error(kDevAttentionTimeout);
     } else {
@@ -355,11 +398,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_ld_wait();
         if (!valid) continue;
         if (p.gate) {
-          const uint16_t* gp = p.gate + row * p.g_ts + (int64_t)h * p.g_hs + c * 32;
+          // Gate columns c*32 .. c*32+31 of row r: atom c/2, 16-byte chunks
+          // (c%2)*4 + e4, stored at chunk ^ (r % 8) by the 128-byte swizzle.
+          const uint8_t* grow = sm + OFF_Q + (c >> 1) * (BQ * 128) + r * 128;
           uint16_t* op = reinterpret_cast<uint16_t*>(p.out) + row * p.o_ts + (int64_t)h * p.o_hs + c * 32;
 #pragma unroll
           for (int e4 = 0; e4 < 4; ++e4) {
-            const uint4 graw = *reinterpret_cast<const uint4*>(gp + e4 * 8);
+            const uint4 graw =
+                *reinterpret_cast<const uint4*>(grow + (((((c & 1) << 2) + e4) ^ (r & 7)) << 4));
             const uint32_t gw[4] = {graw.x, graw.y, graw.z, graw.w};
             uint32_t ow[4];
 #pragma unroll
@@ -479,7 +525,7 @@ int launch_attention_tc(const AttnTcArgs& a, const SeqPackVT& pk, cudaStream_t s
   if (pk.total == 0) return CLEF_OK;
   CLEF_CHECK(a.rows_q < (1LL << 31) && a.vt_cols < (1LL << 31), CLEF_ERR_UNSUPPORTED,
              "attention_tc: tensors too large for 32-bit TMA coordinates");
-  CUtensorMap mq, mk, mvt, mpk, mpvt;
+  CUtensorMap mq, mk, mvt, mpk, mpvt, mg;
   int rc = map2d(&mq, a.q, (uint64_t)a.rows_q, (uint64_t)a.H * D, (uint64_t)a.H * D, BQ);
   if (!rc) rc = map2d(&mk, a.k, (uint64_t)a.rows_k, (uint64_t)a.Hkv * D, (uint64_t)a.Hkv * D, BK);
   if (!rc) rc = map2d(&mvt, a.vt, (uint64_t)a.Hkv * D, (uint64_t)a.vt_cols, (uint64_t)a.vt_pitch, D);
@@ -492,6 +538,13 @@ int launch_attention_tc(const AttnTcArgs& a, const SeqPackVT& pk, cudaStream_t s
   } else {
     mpk = mk;
     mpvt = mvt;
+  }
+  if (a.gate) {
+    CLEF_CHECK(a.g_hs % 8 == 0, CLEF_ERR_INVALID, "attention_tc: gate head stride");
+    rc = map2d(&mg, a.gate, (uint64_t)a.rows_q, (uint64_t)(a.H - 1) * a.g_hs + D, (uint64_t)a.g_ts, BQ);
+    if (rc) return rc;
+  } else {
+    mg = mq;
   }
   TcParams p;
   p.H = a.H;
@@ -517,7 +570,7 @@ int launch_attention_tc(const AttnTcArgs& a, const SeqPackVT& pk, cudaStream_t s
     attr[dev] = true;
   }
   const unsigned blocks = pk.cu ? (unsigned)pk.qblocks : (unsigned)ceil_div(pk.total, BQ);
-  attention_tc_kernel<<<dim3(blocks, (unsigned)a.H), THREADS, SMEM, s>>>(mq, mk, mvt, mpk, mpvt, p);
+  attention_tc_kernel<<<dim3(blocks, (unsigned)a.H), THREADS, SMEM, s>>>(mq, mk, mvt, mpk, mpvt, mg, p);
   return launch_status("attention_tc");
 }
 

@@ -226,7 +226,7 @@ class ClockSampler:
         self.out.flush()
         rows = [r.split(",") for r in Path(self.out.name).read_text().splitlines() if r.strip()]
         os.unlink(self.out.name)
-        sm, mx, reasons = [], None, set()
+        sm, mx, reasons, watts, capped = [], None, set(), [], 0
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
             r = [x.strip() for x in r]
@@ -235,13 +235,21 @@ class ClockSampler:
                 mx = float(r[1])
             except (ValueError, IndexError):
                 continue
+            try:
+                watts.append(float(r[2]))
+            except (ValueError, IndexError):
+                pass
             for n, v in zip(names, r[4:8]):
                 if v.lower() == "active":
                     reasons.add(n)
+            if len(r) > 7 and r[7].lower() == "active":
+                capped += 1
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "sm_mhz_range": [min(sm), max(sm)],
+                "power_w": statistics.median(watts) if watts else None,
+                "power_cap_frac": round(capped / len(sm), 3)}
 
 
 # ---------------------------------------------------------------------------

@@ -103,36 +103,123 @@ __global__ void conv4_kernel(const float* __restrict__ x, int64_t ldx, const flo
 
 // ---- DeltaNet prologue -------------------------------------------------------
 // CTA = 256 threads x 4 channels (1024 channels = 8 whole 128-wide heads) over a
-// run of consecutive tokens. Each thread keeps the last four projection rows of
-// its channels in registers and slides the window one token at a time, so each
-// row is read from memory once; a warp covers exactly one q/k head and reduces
-// its L2 norm with shuffles (clef_delta_prepare, pointwise.metal:69-114; l2 and
-// scaling, qwen.rs:837-845). The CTAs of channel block 0 also compute the gates
-// (qwen.rs:619-627).
+// run of PRO_RUN consecutive tokens. Every thread issues the asynchronous
+// copies of all PRO_RUN + 3 projection rows of its channels (3 rows of conv
+// history) into shared memory up front, one copy group per row, and consumes
+// the rows in order as their groups complete: the whole run is in flight at
+// once without holding it in registers. A warp covers exactly one q/k head and
+// reduces its L2 norm with shuffles (clef_delta_prepare, pointwise.metal:69-114;
+// l2 and scaling, qwen.rs:837-845). The CTAs of channel block 0 also compute
+// the gates (qwen.rs:619-627).
 constexpr int PRO_RUN = 16;
+constexpr int PRO_ROWS = PRO_RUN + 3;
+constexpr int PRO_SMEM = PRO_ROWS * 256 * 16;
 
-__device__ __forceinline__ float4 pro_row(const float* __restrict__ proj, int64_t ldp,
-                                          const float* __restrict__ hist, int hist_rows, int width,
-                                          int64_t start, int64_t r, int c) {
-  // Row r (absolute token index) of sequence starting at `start`, channels c..c+3.
-  if (r >= start) return *reinterpret_cast<const float4*>(proj + r * ldp + c);
-  const int64_t hr = hist_rows + (r - start);
-  if (hist && hr >= 0) return *reinterpret_cast<const float4*>(hist + hr * width + c);
-  return make_float4(0.f, 0.f, 0.f, 0.f);
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-__global__ void __launch_bounds__(256, 3) delta_prologue_kernel(
+// silu(x) = x / (1 + e^-x) with the MUFU exponential and divide (a few ulp of
+// the correctly rounded quotient; e^-x overflowing gives -0 for very negative x).
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.f + __expf(-x)); }
+
+template <int I>
+__device__ __forceinline__ void pro_step(const float4* __restrict__ rows, const float* __restrict__ hist,
+                                         int hist_rows, int width, const float (&tw)[4][4], int64_t t,
+                                         int64_t start, int c, int key, int Hv, float qscale,
+                                         float* __restrict__ q, float* __restrict__ k,
+                                         float* __restrict__ v) {
+  // rows[(I + i) * 256] is token t - 3 + i of this thread's channels (i = 0..3).
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int tap = 0; tap < 4; ++tap) {
+    const int64_t r = t - (3 - tap);
+    float4 xv;
+    if (r >= start) {
+      xv = rows[(I + tap) * 256];
+    } else {
+      const int64_t hr = hist_rows + (r - start);
+      if (!hist || hr < 0) continue;  // rows before the sequence are zero
+      xv = *reinterpret_cast<const float4*>(hist + hr * width + c);
+    }
+    acc.x = __fadd_rn(acc.x, __fmul_rn(xv.x, tw[tap][0]));
+    acc.y = __fadd_rn(acc.y, __fmul_rn(xv.y, tw[tap][1]));
+    acc.z = __fadd_rn(acc.z, __fmul_rn(xv.z, tw[tap][2]));
+    acc.w = __fadd_rn(acc.w, __fmul_rn(xv.w, tw[tap][3]));
+  }
+  const float4 m = make_float4(silu_fast(acc.x), silu_fast(acc.y), silu_fast(acc.z), silu_fast(acc.w));
+  if (c < 2 * key) {
+    // The whole warp sits in one head (channel blocks of 1024, heads of 128).
+    float ss = m.x * m.x + m.y * m.y + m.z * m.z + m.w * m.w;
+    ss = warp_sum(ss);
+    float inv = 1.f / sqrtf(ss + 1e-6f);
+    if (c < key) {
+      inv = __fmul_rn(inv, qscale);
+      *reinterpret_cast<float4*>(q + t * key + c) = make_float4(m.x * inv, m.y * inv, m.z * inv, m.w * inv);
+    } else {
+      *reinterpret_cast<float4*>(k + t * key + (c - key)) =
+          make_float4(m.x * inv, m.y * inv, m.z * inv, m.w * inv);
+    }
+  } else {
+    *reinterpret_cast<float4*>(v + t * (int64_t)(Hv * 128) + (c - 2 * key)) = m;
+  }
+}
+
+template <int I>
+struct ProRun {
+  // Token t_begin + I, once copy group I + 3 has landed.
+  __device__ __forceinline__ static void run(const float4* rows, const float* hist, int hist_rows,
+                                             int width, const float (&tw)[4][4], int64_t t_begin,
+                                             int64_t t_end, int64_t& start, int64_t& next_start,
+                                             int& s, const int64_t* cu, int c, int key, int Hv,
+                                             float qscale, float* q, float* k, float* v) {
+    const int64_t t = t_begin + I;
+    if (t >= t_end) return;
+    cp_async_wait<PRO_RUN - 1 - I>();
+    if (t == next_start) {  // a new sequence starts: its window holds history or zeros
+      ++s;
+      start = t;
+      next_start = cu[s + 1];
+    }
+    pro_step<I>(rows, hist, hist_rows, width, tw, t, start, c, key, Hv, qscale, q, k, v);
+    ProRun<I + 1>::run(rows, hist, hist_rows, width, tw, t_begin, t_end, start, next_start, s, cu, c,
+                       key, Hv, qscale, q, k, v);
+  }
+};
+template <>
+struct ProRun<PRO_RUN> {
+  __device__ __forceinline__ static void run(const float4*, const float*, int, int, const float (&)[4][4],
+                                             int64_t, int64_t, int64_t&, int64_t&, int&, const int64_t*,
+                                             int, int, int, float, float*, float*, float*) {}
+};
+
+__global__ void __launch_bounds__(256, 2) delta_prologue_kernel(
     const float* __restrict__ proj, int64_t ldp, int a_col, int b_col,
     const float* __restrict__ hist, int hist_rows, const float* __restrict__ conv_w,
     const float* __restrict__ dt_bias, const float* __restrict__ a_log,
     const int64_t* __restrict__ cu, int nseq, int64_t T, int Hk, int Hv, float qscale,
     float* __restrict__ q, float* __restrict__ k, float* __restrict__ v, float* __restrict__ g,
     float* __restrict__ beta) {
+  extern __shared__ float4 pro_sm[];  // [PRO_ROWS][256]
   const int key = Hk * 128;
   const int width = 2 * key + Hv * 128;
   const int c = blockIdx.x * 1024 + threadIdx.x * 4;
   const int64_t t_begin = (int64_t)blockIdx.y * PRO_RUN;
   const int64_t t_end = min(T, t_begin + PRO_RUN);
+  float4* rows = pro_sm + threadIdx.x;
+#pragma unroll
+  for (int i = 0; i < PRO_ROWS; ++i) {
+    const int64_t r = t_begin - 3 + i;
+    if (r >= 0 && r < t_end) cp_async16(rows + i * 256, proj + r * ldp + c);
+    cp_async_commit();
+  }
   // Sequence of the first token.
   int s = cu ? (int)seq_of(cu, nseq, t_begin) : 0;
   int64_t start = cu ? cu[s] : 0;
@@ -146,65 +233,9 @@ __global__ void __launch_bounds__(256, 3) delta_prologue_kernel(
                           {w0.y, w1.y, w2.y, w3.y},
                           {w0.z, w1.z, w2.z, w3.z},
                           {w0.w, w1.w, w2.w, w3.w}};
-  float4 win[4];  // rows t-3, t-2, t-1, t
-  win[0] = pro_row(proj, ldp, hist, hist_rows, width, start, t_begin - 3, c);
-  win[1] = pro_row(proj, ldp, hist, hist_rows, width, start, t_begin - 2, c);
-  win[2] = pro_row(proj, ldp, hist, hist_rows, width, start, t_begin - 1, c);
-  // Rows t .. t+3 are requested before row t is used, so four loads per
-  // thread are in flight while the window slides.
-  float4 ahead[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j)
-    ahead[j] = t_begin + j < t_end ? *reinterpret_cast<const float4*>(proj + (t_begin + j) * ldp + c)
-                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 1
-  for (int64_t t = t_begin; t < t_end; ++t) {
-    if (t == next_start) {  // a new sequence starts: its window holds history or zeros
-      ++s;
-      start = t;
-      next_start = cu[s + 1];
-      win[0] = pro_row(proj, ldp, hist, hist_rows, width, start, t - 3, c);
-      win[1] = pro_row(proj, ldp, hist, hist_rows, width, start, t - 2, c);
-      win[2] = pro_row(proj, ldp, hist, hist_rows, width, start, t - 1, c);
-    }
-    win[3] = ahead[0];
-    ahead[0] = ahead[1];
-    ahead[1] = ahead[2];
-    ahead[2] = ahead[3];
-    if (t + 4 < t_end) ahead[3] = *reinterpret_cast<const float4*>(proj + (t + 4) * ldp + c);
-    // taps oldest to newest; rows before the sequence (and history) are zero
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int tap = 0; tap < 4; ++tap) {
-      const int64_t r = t - (3 - tap);
-      if (r < start && !(hist && hist_rows + (r - start) >= 0)) continue;
-      const float4 xv = win[tap];
-      acc.x = __fadd_rn(acc.x, __fmul_rn(xv.x, tw[tap][0]));
-      acc.y = __fadd_rn(acc.y, __fmul_rn(xv.y, tw[tap][1]));
-      acc.z = __fadd_rn(acc.z, __fmul_rn(xv.z, tw[tap][2]));
-      acc.w = __fadd_rn(acc.w, __fmul_rn(xv.w, tw[tap][3]));
-    }
-    const float4 m = make_float4(silu_f(acc.x), silu_f(acc.y), silu_f(acc.z), silu_f(acc.w));
-    if (c < 2 * key) {
-      // The whole warp sits in one head (channel blocks of 1024, heads of 128).
-      float ss = m.x * m.x + m.y * m.y + m.z * m.z + m.w * m.w;
-      ss = warp_sum(ss);
-      const float nrm = sqrtf(ss + 1e-6f);
-      float4 r = make_float4(m.x / nrm, m.y / nrm, m.z / nrm, m.w / nrm);
-      if (c < key) {
-        r = make_float4(__fmul_rn(r.x, qscale), __fmul_rn(r.y, qscale), __fmul_rn(r.z, qscale),
-                        __fmul_rn(r.w, qscale));
-        *reinterpret_cast<float4*>(q + t * key + c) = r;
-      } else {
-        *reinterpret_cast<float4*>(k + t * key + (c - key)) = r;
-      }
-    } else {
-      *reinterpret_cast<float4*>(v + t * (int64_t)(Hv * 128) + (c - 2 * key)) = m;
-    }
-    win[0] = win[1];
-    win[1] = win[2];
-    win[2] = win[3];
-  }
+  ProRun<0>::run(rows, hist, hist_rows, width, tw, t_begin, t_end, start, next_start, s, cu, c, key, Hv,
+                 qscale, q, k, v);
+  cp_async_wait<0>();
   if (blockIdx.x == 0) {
     for (int idx = threadIdx.x; idx < (t_end - t_begin) * Hv; idx += blockDim.x) {
       const int64_t t = t_begin + idx / Hv;
@@ -420,7 +451,14 @@ int launch_delta_prologue(const float* proj, int64_t ldp, int a_col, int b_col, 
   const float qscale = (float)(1.0 / std::sqrt(128.0));
   const int width = 2 * Hk * 128 + Hv * 128;
   const dim3 grid((unsigned)(width / 1024), (unsigned)ceil_div(pack.total, PRO_RUN));
-  delta_prologue_kernel<<<grid, 256, 0, s>>>(proj, ldp, a_col, b_col, hist, hist_rows, conv_w,
+  static bool attr[64] = {false};
+  int dev = 0;
+  CLEF_CUDA(cudaGetDevice(&dev));
+  if (dev >= 0 && dev < 64 && !attr[dev]) {
+    CLEF_CUDA(cudaFuncSetAttribute(delta_prologue_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PRO_SMEM));
+    attr[dev] = true;
+  }
+  delta_prologue_kernel<<<grid, 256, PRO_SMEM, s>>>(proj, ldp, a_col, b_col, hist, hist_rows, conv_w,
                                              dt_bias, a_log, pack.cu_seqlens, pack.nseq,
                                              pack.total, Hk, Hv, qscale, q, k, v, g, beta);
   return launch_status("delta_prologue");
@@ -511,6 +549,10 @@ int clef_delta_prologue(const float* proj, int64_t ldp, int32_t a_col, int32_t b
              "delta_prologue: q|k|v width must be a multiple of 1024");
   CLEF_CHECK(T > 0 && T <= (1LL << 31), CLEF_ERR_INVALID, "delta_prologue: T");
   CLEF_CHECK(ldp >= width && ldp % 4 == 0, CLEF_ERR_INVALID, "delta_prologue: ldp");
+  CLEF_CHECK(((uintptr_t)proj & 15) == 0 && ((uintptr_t)q & 15) == 0 && ((uintptr_t)k & 15) == 0 &&
+                 ((uintptr_t)v & 15) == 0 && ((uintptr_t)conv_weight & 15) == 0 &&
+                 ((uintptr_t)history & 15) == 0,
+             CLEF_ERR_INVALID, "delta_prologue: tensors must be 16-byte aligned");
   CLEF_CHECK(a_col >= width && a_col + Hv <= ldp && b_col >= width && b_col + Hv <= ldp,
              CLEF_ERR_INVALID, "delta_prologue: gate columns");
   CLEF_CHECK(history_rows >= 0 && history_rows <= 3 && (history_rows == 0 || history),

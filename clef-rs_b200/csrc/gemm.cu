@@ -59,6 +59,95 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
 
 __device__ __forceinline__ float u2f(uint32_t x) { return __uint_as_float(x); }
 
+// Epilogue of one accumulator row: TMEM row `tbase` (lane quarter and
+// accumulator already applied) of output row m, output column tile tn.
+__device__ __forceinline__ void store_tile(const GemmParams& p, uint32_t tbase, int64_t m, int tn,
+                                           bool swiglu) {
+  if (swiglu) {
+    uint16_t* out = reinterpret_cast<uint16_t*>(p.out);
+#pragma unroll 1
+    for (int c = 0; c < 128 / 32; ++c) {
+      uint32_t gr[32], ur[32];
+      tmem_ld_32x32b_x32(tbase + c * 32, gr);
+      tmem_ld_32x32b_x32(tbase + 128 + c * 32, ur);
+      tmem_ld_wait();
+      const int n0 = tn * 128 + c * 32;
+      if (m < p.M) {
+        uint32_t packed[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float g0 = u2f(gr[2 * j]), g1 = u2f(gr[2 * j + 1]);
+          const float y0 = silu_f(g0) * u2f(ur[2 * j]);
+          const float y1 = silu_f(g1) * u2f(ur[2 * j + 1]);
+          packed[j] = pack_bf16x2(y0, y1);
+        }
+        uint16_t* dst = out + m * p.ldo + n0;
+        if (n0 + 32 <= p.N) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            reinterpret_cast<uint4*>(dst)[j] =
+                make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < p.N) dst[j] = (uint16_t)((packed[j >> 1] >> ((j & 1) * 16)) & 0xffff);
+        }
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      const int n0 = tn * BN + c * 32;
+      if (n0 >= p.N) break;  // warp-uniform
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tbase + c * 32, r);
+      tmem_ld_wait();
+      if (m >= p.M) continue;
+      const bool full_chunk = n0 + 32 <= p.N;
+      if (p.epi == kEpiBF16) {
+        uint16_t* dst = reinterpret_cast<uint16_t*>(p.out) + m * p.ldo + n0;
+        if (full_chunk) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            reinterpret_cast<uint4*>(dst)[j] = make_uint4(
+                pack_bf16x2(u2f(r[8 * j]), u2f(r[8 * j + 1])),
+                pack_bf16x2(u2f(r[8 * j + 2]), u2f(r[8 * j + 3])),
+                pack_bf16x2(u2f(r[8 * j + 4]), u2f(r[8 * j + 5])),
+                pack_bf16x2(u2f(r[8 * j + 6]), u2f(r[8 * j + 7])));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < p.N) dst[j] = f2bf(u2f(r[j]));
+        }
+      } else {
+        float* dst = reinterpret_cast<float*>(p.out) + m * p.ldo + n0;
+        if (full_chunk) {
+          if (p.epi == kEpiAddF32) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float4 o = reinterpret_cast<float4*>(dst)[j];
+              o.x += u2f(r[4 * j]);
+              o.y += u2f(r[4 * j + 1]);
+              o.z += u2f(r[4 * j + 2]);
+              o.w += u2f(r[4 * j + 3]);
+              reinterpret_cast<float4*>(dst)[j] = o;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              reinterpret_cast<float4*>(dst)[j] = make_float4(
+                  u2f(r[4 * j]), u2f(r[4 * j + 1]), u2f(r[4 * j + 2]), u2f(r[4 * j + 3]));
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < p.N) dst[j] = p.epi == kEpiAddF32 ? dst[j] + u2f(r[j]) : u2f(r[j]);
+        }
+      }
+    }
+  }
+}
+
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 const __grid_constant__ CUtensorMap map_b2, GemmParams p) {
@@ -186,85 +275,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const int64_t m = (int64_t)tm * BM + row_in_tile;
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
-      if (swiglu) {
-        uint16_t* out = reinterpret_cast<uint16_t*>(p.out);
-#pragma unroll 1
-        for (int c = 0; c < 128 / 32; ++c) {
-          uint32_t gr[32], ur[32];
-          tmem_ld_32x32b_x32(tbase + c * 32, gr);
-          tmem_ld_32x32b_x32(tbase + 128 + c * 32, ur);
-          tmem_ld_wait();
-          const int n0 = tn * 128 + c * 32;
-          if (m < p.M) {
-            uint32_t packed[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const float g0 = u2f(gr[2 * j]), g1 = u2f(gr[2 * j + 1]);
-              const float y0 = silu_f(g0) * u2f(ur[2 * j]);
-              const float y1 = silu_f(g1) * u2f(ur[2 * j + 1]);
-              packed[j] = pack_bf16x2(y0, y1);
-            }
-            uint16_t* dst = out + m * p.ldo + n0;
-            if (n0 + 32 <= p.N) {
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                reinterpret_cast<uint4*>(dst)[j] =
-                    make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
-            } else {
-              for (int j = 0; j < 32 && n0 + j < p.N; ++j)
-                dst[j] = (uint16_t)((packed[j >> 1] >> ((j & 1) * 16)) & 0xffff);
-            }
-          }
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          const int n0 = tn * BN + c * 32;
-          if (n0 >= p.N) break;  // warp-uniform
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tbase + c * 32, r);
-          tmem_ld_wait();
-          if (m >= p.M) continue;
-          const bool full_chunk = n0 + 32 <= p.N;
-          if (p.epi == kEpiBF16) {
-            uint16_t* dst = reinterpret_cast<uint16_t*>(p.out) + m * p.ldo + n0;
-            if (full_chunk) {
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                reinterpret_cast<uint4*>(dst)[j] = make_uint4(
-                    pack_bf16x2(u2f(r[8 * j]), u2f(r[8 * j + 1])),
-                    pack_bf16x2(u2f(r[8 * j + 2]), u2f(r[8 * j + 3])),
-                    pack_bf16x2(u2f(r[8 * j + 4]), u2f(r[8 * j + 5])),
-                    pack_bf16x2(u2f(r[8 * j + 6]), u2f(r[8 * j + 7])));
-            } else {
-              for (int j = 0; j < 32 && n0 + j < p.N; ++j) dst[j] = f2bf(u2f(r[j]));
-            }
-          } else {
-            float* dst = reinterpret_cast<float*>(p.out) + m * p.ldo + n0;
-            if (full_chunk) {
-              if (p.epi == kEpiAddF32) {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                  float4 o = reinterpret_cast<float4*>(dst)[j];
-                  o.x += u2f(r[4 * j]);
-                  o.y += u2f(r[4 * j + 1]);
-                  o.z += u2f(r[4 * j + 2]);
-                  o.w += u2f(r[4 * j + 3]);
-                  reinterpret_cast<float4*>(dst)[j] = o;
-                }
-              } else {
-#pragma unroll
-                for (int j = 0; j < 8; ++j)
-                  reinterpret_cast<float4*>(dst)[j] = make_float4(
-                      u2f(r[4 * j]), u2f(r[4 * j + 1]), u2f(r[4 * j + 2]), u2f(r[4 * j + 3]));
-              }
-            } else {
-              for (int j = 0; j < 32 && n0 + j < p.N; ++j)
-                dst[j] = p.epi == kEpiAddF32 ? dst[j] + u2f(r[j]) : u2f(r[j]);
-            }
-          }
-        }
-      }
+      store_tile(p, tbase, m, tn, swiglu);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -279,6 +290,183 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---- CTA-pair variant ---------------------------------------------------------
+// A cluster of two CTAs on neighbouring SMs computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2: CTA r holds A rows [128 r, 128 r + 128) and B rows
+// [128 r, 128 r + 128) of the tile (for SwiGLU: CTA 0 the gate rows, CTA 1 the
+// up rows), the even CTA issues the MMAs, and each CTA's TMEM receives its own
+// 128 rows x 256 columns. Every CTA streams 32 KB per 64-wide K slab instead of
+// 48 KB for the same tensor work, so L2 and shared-memory traffic per FLOP drop
+// by a third. Both CTAs load their halves with plain (non-multicast) TMA whose
+// byte counts land on the even CTA's stage barrier; the MMA completion is
+// signalled to both CTAs' barriers by one multicast commit.
+constexpr int P_STAGES = 6;
+constexpr int P_A_BYTES = 128 * BK * 2;  // 16 KB
+constexpr int P_B_BYTES = 128 * BK * 2;  // 16 KB
+constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
+constexpr size_t P_SMEM_BYTES = 1024 + (size_t)P_STAGES * P_STAGE_BYTES + 256;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                     const __grid_constant__ CUtensorMap map_b2, GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)P_STAGES * P_STAGE_BYTES);
+  uint64_t* empty = full + P_STAGES;
+  uint64_t* tfull = empty + P_STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+  const bool swiglu = p.epi == kEpiSwiGLU;
+  const int num_tiles = p.tiles_m * p.tiles_n;
+  const int nk = p.K / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * EPI_WARPS);  // the epilogue warps of both CTAs
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+    tma_prefetch(&map_a);
+    tma_prefetch(&map_b);
+    if (swiglu) tma_prefetch(&map_b2);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before any remote arrival
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  bool ok = true;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t full0 = mapa_shared(&full[0], 0);  // the even CTA's stage barriers
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = cluster; t < num_tiles && ok; t += nclusters) {
+        int tm, tn;
+        tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + (size_t)stage * P_STAGE_BYTES;
+          uint8_t* sb = sa + P_A_BYTES;
+          if (leader) mbar_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
+          const uint32_t bar = full0 + (uint32_t)(stage * sizeof(uint64_t));
+          tma_load_2d_pair(&map_a, bar, sa, kb * BK, tm * 256 + (int)rank * 128);
+          if (swiglu)
+            tma_load_2d_pair(leader ? &map_b : &map_b2, bar, sb, kb * BK, tn * 128);
+          else
+            tma_load_2d_pair(&map_b, bar, sb, kb * BK, tn * BN + (int)rank * 128);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) raise_device_error(kDevGemmTimeout);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = idesc_bf16_f32(256, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool issued = false;
+      for (int t = cluster; t < num_tiles && ok; t += nclusters) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&full[stage], phase)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + (size_t)stage * P_STAGE_BYTES);
+          const uint32_t sb = sa + P_A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_f16_pair(d, desc_k_sw128(sa + k * 32), desc_k_sw128(sb + k * 32), idesc, (kb | k) != 0);
+          issued = true;
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[acc], 0x3);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      if (!ok) {
+        // The MMAs already issued write both CTAs' TMEM: let them finish
+        // (bounded) before the allocation is released.
+        raise_device_error(kDevGemmTimeout);
+        if (issued) {
+          umma_commit_pair(drain, 0x1);
+          mbar_wait(drain, 0);
+        }
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    const uint32_t tempty0 = mapa_shared(&tempty[0], 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = cluster; t < num_tiles; t += nclusters) {
+      int tm, tn;
+      tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase))) {
+        raise_device_error(kDevGemmTimeout);
+        break;
+      }
+      tc_fence_after();
+      const int64_t m = (int64_t)tm * 256 + rank * 128 + row_in_tile;
+      const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+      store_tile(p, tbase, m, tn, swiglu);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty0 + (uint32_t)(acc * sizeof(uint64_t)));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA releases TMEM or exits while its pair still uses it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
 }
 
@@ -325,6 +513,7 @@ int launch_gemm(const uint16_t* X, const uint16_t* W, const uint16_t* W2, int64_
   CLEF_CHECK(ldo >= N && (ldo * elem) % 16 == 0, CLEF_ERR_INVALID,
              "gemm: ldo must cover N and keep rows 16-byte aligned");
   CUtensorMap ma, mb, mb2;
+  const bool pair_maps = M > BM;  // the CTA-pair kernel loads 128-row halves of B
   int rc = make_map(&ma, X, (uint64_t)M, (uint64_t)K, BM);
   if (rc) return rc;
   if (swiglu) {
@@ -332,10 +521,11 @@ int launch_gemm(const uint16_t* X, const uint16_t* W, const uint16_t* W2, int64_
     rc = make_map(&mb, W, (uint64_t)N, (uint64_t)K, 128);
     if (!rc) rc = make_map(&mb2, W2, (uint64_t)N, (uint64_t)K, 128);
   } else {
-    rc = make_map(&mb, W, (uint64_t)N, (uint64_t)K, BN);
+    rc = make_map(&mb, W, (uint64_t)N, (uint64_t)K, pair_maps ? 128 : BN);
     mb2 = mb;
   }
   if (rc) return rc;
+  const bool pair = M > BM;
   GemmParams p;
   p.M = M;
   p.N = N;
@@ -343,7 +533,7 @@ int launch_gemm(const uint16_t* X, const uint16_t* W, const uint16_t* W2, int64_
   p.epi = epi;
   p.out = out;
   p.ldo = ldo;
-  p.tiles_m = (int)ceil_div(M, BM);
+  p.tiles_m = (int)ceil_div(M, pair ? 256 : BM);
   p.tiles_n = (int)ceil_div(N, swiglu ? 128 : BN);
   int dev = 0;
   CLEF_CUDA(cudaGetDevice(&dev));
@@ -351,9 +541,16 @@ int launch_gemm(const uint16_t* X, const uint16_t* W, const uint16_t* W2, int64_
   if (dev >= 0 && dev < 64 && !attr[dev]) {
     CLEF_CUDA(cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)SMEM_BYTES));
+    CLEF_CUDA(cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)P_SMEM_BYTES));
     attr[dev] = true;
   }
   const int tiles = p.tiles_m * p.tiles_n;
+  if (pair) {
+    const int clusters = std::min(tiles, num_sms(dev) / 2);
+    gemm_pair_kernel<<<2 * clusters, THREADS, P_SMEM_BYTES, s>>>(ma, mb, mb2, p);
+    return launch_status("gemm_pair");
+  }
   const int grid = std::min(tiles, num_sms(dev));
   gemm_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, mb2, p);
   return launch_status("gemm");

@@ -264,17 +264,27 @@ def profile_op(args):
     from clef_b200 import workloads
     torch.manual_seed(0)
     dev = "cuda"
+
+    def timed(label, fn):
+        # CUDA events on the launching (current) stream around each repetition.
+        for _ in range(args.reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            print(f"{label}: {e0.elapsed_time(e1):.3f} ms", flush=True)
+
     if args.profile_op in ("gemm", "gemm_swiglu"):
         M, K, N = 8192, 2560, 9216
         x = torch.randn(M, K, device=dev).bfloat16()
         w = (0.02 * torch.randn(N, K, device=dev)).bfloat16()
         w2 = (0.02 * torch.randn(N, K, device=dev)).bfloat16()
         out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
-        for _ in range(args.reps):
-            if args.profile_op == "gemm":
-                cb.gemm(x, w, out=out)
-            else:
-                cb.gemm_swiglu(x, w, w2, out=out)
+        if args.profile_op == "gemm":
+            timed(f"gemm {M}x{N}x{K}", lambda: cb.gemm(x, w, out=out))
+        else:
+            timed(f"gemm_swiglu {M}x{N}x{K}", lambda: cb.gemm_swiglu(x, w, w2, out=out))
     elif args.profile_op in ("scan", "scan1"):
         T, cu = (65536, np.arange(0, 65537, 1024, dtype=np.int64)) if args.profile_op == "scan" \
             else (1024, None)
@@ -282,8 +292,7 @@ def profile_op(args):
         qs, ks = workloads.scan_operands(inp)
         t = {k: torch.from_numpy(np.ascontiguousarray(v)).cuda()
              for k, v in dict(q=qs, k=ks, v=inp["v"], g=inp["g"], b=inp["beta"]).items()}
-        for _ in range(args.reps):
-            cb.delta_scan(t["q"], t["k"], t["v"], t["g"], t["b"], cu_seqlens=cu)
+        timed(f"delta_scan T={T}", lambda: cb.delta_scan(t["q"], t["k"], t["v"], t["g"], t["b"], cu_seqlens=cu))
     elif args.profile_op == "attention":
         T = 4096
         q = torch.randn(16, T, 256, device=dev).bfloat16()
@@ -319,8 +328,8 @@ def profile_op(args):
         proj = torch.randn(T, ldp, device=dev)
         conv = 0.3 * torch.randn(width, 4, device=dev)
         dt, alog = 0.1 * torch.randn(Hv, device=dev), torch.rand(Hv, device=dev) * 2.7
-        for _ in range(args.reps):
-            cb.delta_prologue(proj, width + Hv * 128, width + Hv * 128 + Hv, conv, dt, alog, Hk, Hv)
+        timed(f"delta_prologue T={T}",
+              lambda: cb.delta_prologue(proj, width + Hv * 128, width + Hv * 128 + Hv, conv, dt, alog, Hk, Hv))
     torch.cuda.synchronize()
     print(f"profile-op {args.profile_op}: ok", flush=True)
     return 0

@@ -64,7 +64,7 @@ constexpr int OFF_THI = OFF_QLO + KQ_BYTES;
 constexpr int OFF_TLO = OFF_THI + SQ_BYTES;
 constexpr int OFF_PHI = OFF_TLO + SQ_BYTES;
 constexpr int OFF_PLO = OFF_PHI + SQ_BYTES;
-constexpr int AP = 65;                               // F32 pitch of A and T
+constexpr int AP = 72;                               // F32 pitch of A and T (8-byte pairs spread over all banks)
 constexpr int OFF_A = OFF_PLO + SQ_BYTES;            // F32 [64][65]
 constexpr int OFF_T = OFF_A + C * AP * 4;            // F32 [64][65]
 constexpr int OFF_M = OFF_T + C * AP * 4;            // F32 [3][16][17] scratch
@@ -255,15 +255,16 @@ __device__ __forceinline__ void gram_store(const float (&kk)[4][4], const float 
 #pragma unroll
     for (int e = 0; e < 4; e += 2) {
       const int i = m0 + r0 + (e >> 1) * 8;
-      float pv[2];
+      float pv[2], av[2];
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         const int col = nb + j * 8 + c0 + u;
         const bool lower = col <= i && i < n;
         const float decay = lower ? expf((float)(Gs[i] - Gs[col])) : 0.f;
-        As[i * AP + col] = (lower && col < i) ? bs[i] * (decay * kk[j][e + u]) : 0.f;
+        av[u] = (lower && col < i) ? bs[i] * (decay * kk[j][e + u]) : 0.f;
         pv[u] = lower ? decay * qk[j][e + u] : 0.f;
       }
+      *reinterpret_cast<float2*>(As + i * AP + nb + j * 8 + c0) = make_float2(av[0], av[1]);
       uint32_t ph, pl;
       split2(pv[0], pv[1], ph, pl);
       const uint32_t o = swz(i, nb + j * 8 + c0, 8);
@@ -325,7 +326,8 @@ __device__ __forceinline__ void solve_t(const float* As, float* Ts, float* Ms, c
   for (int idx = tid; idx < C * C / 2; idx += nthreads) {
     const int i = idx >> 5, j = (idx & 31) * 2;
     uint32_t th, tl;
-    split2(Ts[i * AP + j] * bs[j], Ts[i * AP + j + 1] * bs[j + 1], th, tl);
+    const float2 tv = *reinterpret_cast<const float2*>(Ts + i * AP + j);
+    split2(tv.x * bs[j], tv.y * bs[j + 1], th, tl);
     const uint32_t o = swz(i, j, 8);
     put32<GLOBAL>(t_hi, o, th);
     put32<GLOBAL>(t_lo, o, tl);

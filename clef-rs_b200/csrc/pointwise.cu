@@ -111,7 +111,7 @@ __global__ void conv4_kernel(const float* __restrict__ x, int64_t ldx, const flo
 // reduces its L2 norm with shuffles (clef_delta_prepare, pointwise.metal:69-114;
 // l2 and scaling, qwen.rs:837-845). The CTAs of channel block 0 also compute
 // the gates (qwen.rs:619-627).
-constexpr int PRO_RUN = 16;
+constexpr int PRO_RUN = 12;
 constexpr int PRO_ROWS = PRO_RUN + 3;
 constexpr int PRO_SMEM = PRO_ROWS * 256 * 16;
 
@@ -200,7 +200,7 @@ struct ProRun<PRO_RUN> {
                                              int, int, int, float, float*, float*, float*) {}
 };
 
-__global__ void __launch_bounds__(256, 2) delta_prologue_kernel(
+__global__ void __launch_bounds__(256, 3) delta_prologue_kernel(
     const float* __restrict__ proj, int64_t ldp, int a_col, int b_col,
     const float* __restrict__ hist, int hist_rows, const float* __restrict__ conv_w,
     const float* __restrict__ dt_bias, const float* __restrict__ a_log,

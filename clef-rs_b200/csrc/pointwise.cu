@@ -251,98 +251,133 @@ __global__ void __launch_bounds__(256, 3) delta_prologue_kernel(
 // ---- DeltaNet epilogue (qwen.rs:671-676) -------------------------------------
 // Rounding points follow the reference run in the BF16 projection dtype:
 // o -> P, norm output -> P, z in P, product -> P.
-__global__ void delta_epilogue_kernel(const float* __restrict__ o, const float* __restrict__ z,
-                                      int64_t ldz, const float* __restrict__ w, float eps,
-                                      int64_t rows, int Hv, uint16_t* __restrict__ y) {
+__global__ void __launch_bounds__(256) delta_epilogue_kernel(const float* __restrict__ o,
+                                                             const float* __restrict__ z, int64_t ldz,
+                                                             const float* __restrict__ w, float eps,
+                                                             int64_t T, int Hv, uint16_t* __restrict__ y) {
+  // One warp per token; its Hv rows of 128 go four at a time with all eight
+  // 16-byte loads of a batch issued before any is used.
   const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);  // t*Hv + h
-  if (row >= rows) return;
-  const int64_t t = row / Hv;
-  const int h = (int)(row % Hv);
-  float4 a = *reinterpret_cast<const float4*>(o + row * 128 + lane * 4);
-  a = make_float4(bf16_round(a.x), bf16_round(a.y), bf16_round(a.z), bf16_round(a.w));
-  float ss = a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
-  ss = warp_sum(ss);
-  const float inv = 1.f / sqrtf(ss / 128.f + eps);
+  const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= T) return;
   const float4 wv = *reinterpret_cast<const float4*>(w + lane * 4);
-  const float4 zv = *reinterpret_cast<const float4*>(z + t * ldz + h * 128 + lane * 4);
-  float n0 = bf16_round(__fmul_rn(__fmul_rn(a.x, inv), wv.x));
-  float n1 = bf16_round(__fmul_rn(__fmul_rn(a.y, inv), wv.y));
-  float n2 = bf16_round(__fmul_rn(__fmul_rn(a.z, inv), wv.z));
-  float n3 = bf16_round(__fmul_rn(__fmul_rn(a.w, inv), wv.w));
-  float y0 = __fmul_rn(n0, silu_f(bf16_round(zv.x)));
-  float y1 = __fmul_rn(n1, silu_f(bf16_round(zv.y)));
-  float y2 = __fmul_rn(n2, silu_f(bf16_round(zv.z)));
-  float y3 = __fmul_rn(n3, silu_f(bf16_round(zv.w)));
-  *reinterpret_cast<uint2*>(y + t * (int64_t)Hv * 128 + h * 128 + lane * 4) =
-      make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y2, y3));
+  for (int h0 = 0; h0 < Hv; h0 += 4) {
+    float4 a[4], zv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (h0 + u < Hv) {
+        a[u] = *reinterpret_cast<const float4*>(o + (t * Hv + h0 + u) * 128 + lane * 4);
+        zv[u] = *reinterpret_cast<const float4*>(z + t * ldz + (h0 + u) * 128 + lane * 4);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (h0 + u >= Hv) break;
+      const float4 b = make_float4(bf16_round(a[u].x), bf16_round(a[u].y), bf16_round(a[u].z),
+                                   bf16_round(a[u].w));
+      float ss = b.x * b.x + b.y * b.y + b.z * b.z + b.w * b.w;
+      ss = warp_sum(ss);
+      const float inv = 1.f / sqrtf(ss / 128.f + eps);
+      const float n0 = bf16_round(__fmul_rn(__fmul_rn(b.x, inv), wv.x));
+      const float n1 = bf16_round(__fmul_rn(__fmul_rn(b.y, inv), wv.y));
+      const float n2 = bf16_round(__fmul_rn(__fmul_rn(b.z, inv), wv.z));
+      const float n3 = bf16_round(__fmul_rn(__fmul_rn(b.w, inv), wv.w));
+      const float y0 = __fmul_rn(n0, silu_f(bf16_round(zv[u].x)));
+      const float y1 = __fmul_rn(n1, silu_f(bf16_round(zv[u].y)));
+      const float y2 = __fmul_rn(n2, silu_f(bf16_round(zv[u].z)));
+      const float y3 = __fmul_rn(n3, silu_f(bf16_round(zv[u].w)));
+      *reinterpret_cast<uint2*>(y + (t * Hv + h0 + u) * 128 + lane * 4) =
+          make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y2, y3));
+    }
+  }
 }
 
 // ---- attention prologue (qwen.rs:463-490; rotary, ops.rs:144-188) ------------
-// One warp per (token, head) row of 256 features, 8 per lane. Rows [0, H) are
-// query heads (projection columns h*2d .. h*2d+d), rows [H, H+Hkv) key heads
-// (columns 2*H*d + j*d). The norm output is rounded to BF16 (the projection
-// dtype) before the rotation, and the rotated features again after it.
-__global__ void attention_prologue_kernel(const uint16_t* __restrict__ proj, int64_t ldp,
-                                          const float* __restrict__ qw, const float* __restrict__ kw,
-                                          float eps, const int64_t* __restrict__ cu, int nseq,
-                                          int64_t pos_offset, int H, int Hkv, int rot,
-                                          const float* __restrict__ inv_freq,
-                                          uint16_t* __restrict__ q_out, uint16_t* __restrict__ k_out,
-                                          int64_t T) {
-  const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int per = H + Hkv;
-  if (row >= T * per) return;
-  const int64_t t = row / per;
-  const int hh = (int)(row % per);
-  const bool isq = hh < H;
+// One warp per token: the token's position and its rotary cos/sin table
+// (half = rot/2 frequencies, in shared memory) are computed once and used for
+// all H + Hkv rows of 256 features, which go four at a time (8 features per
+// lane, loads issued up front). Rows [0, H) are query heads (projection
+// columns h*2d .. h*2d+d), rows [H, H+Hkv) key heads (columns 2*H*d + j*d).
+// The norm output is rounded to BF16 (the projection dtype) before the
+// rotation, and the rotated features again after it.
+constexpr int AP_WARPS = 8;
+
+__global__ void __launch_bounds__(AP_WARPS * 32) attention_prologue_kernel(
+    const uint16_t* __restrict__ proj, int64_t ldp, const float* __restrict__ qw,
+    const float* __restrict__ kw, float eps, const int64_t* __restrict__ cu, int nseq, int64_t pos_offset,
+    int H, int Hkv, int rot, const float* __restrict__ inv_freq, uint16_t* __restrict__ q_out,
+    uint16_t* __restrict__ k_out, int64_t T) {
+  __shared__ float cs_tab[AP_WARPS][2][128];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t t = (int64_t)blockIdx.x * AP_WARPS + warp;
+  if (t >= T) return;
   const int d = 256;
-  const uint16_t* src = isq ? proj + t * ldp + (int64_t)hh * 2 * d
-                            : proj + t * ldp + (int64_t)2 * H * d + (int64_t)(hh - H) * d;
-  const float* w = isq ? qw : kw;
-  uint4 raw = *reinterpret_cast<const uint4*>(src + lane * 8);
-  float x[8];
-  const uint32_t r32[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    x[2 * i] = __uint_as_float(r32[i] << 16);
-    x[2 * i + 1] = __uint_as_float(r32[i] & 0xffff0000u);
-  }
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
-  ss = warp_sum(ss);
-  const float inv = 1.f / sqrtf(ss / (float)d + eps);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) x[i] = bf16_round(__fmul_rn(__fmul_rn(x[i], inv), w[lane * 8 + i]));
-  // Partial NeoX rotation on features [0, rot): pairs (i, i + rot/2).
   const int half = rot / 2;
   const int64_t start = cu ? cu[seq_of(cu, nseq, t)] : 0;
   const float pos = (float)(pos_offset + (t - start));
-  float partner[8];
+  for (int f = lane; f < half; f += 32) {
+    const float ang = __fmul_rn(pos, inv_freq[f]);
+    cs_tab[warp][0][f] = cosf(ang);
+    cs_tab[warp][1][f] = sinf(ang);
+  }
+  __syncwarp();
+  const int per = H + Hkv;
   const int lane_half = half / 8;  // lanes covering the first half
+  for (int h0 = 0; h0 < per; h0 += 4) {
+    uint4 raw[4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) partner[i] = __shfl_xor_sync(0xffffffffu, x[i], lane_half);
-  if (lane * 8 < rot) {
+    for (int u = 0; u < 4; ++u) {
+      const int hh = h0 + u;
+      if (hh < per) {
+        const uint16_t* src = hh < H ? proj + t * ldp + (int64_t)hh * 2 * d
+                                     : proj + t * ldp + (int64_t)2 * H * d + (int64_t)(hh - H) * d;
+        raw[u] = *reinterpret_cast<const uint4*>(src + lane * 8);
+      }
+    }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int f = lane * 8 + i;
-      const int fi = f < half ? f : f - half;
-      const float ang = __fmul_rn(pos, inv_freq[fi]);
-      const float c = cosf(ang), sn = sinf(ang);
-      // rotation * cos + rotate_half(rotation) * sin
-      const float rotated = f < half ? -partner[i] : partner[i];
-      x[i] = bf16_round(__fadd_rn(__fmul_rn(x[i], c), __fmul_rn(rotated, sn)));
+    for (int u = 0; u < 4; ++u) {
+      const int hh = h0 + u;
+      if (hh >= per) break;
+      const bool isq = hh < H;
+      const float* wn = isq ? qw : kw;
+      float x[8];
+      const uint32_t r32[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        x[2 * i] = __uint_as_float(r32[i] << 16);
+        x[2 * i + 1] = __uint_as_float(r32[i] & 0xffff0000u);
+      }
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
+      ss = warp_sum(ss);
+      const float inv = 1.f / sqrtf(ss / (float)d + eps);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = bf16_round(__fmul_rn(__fmul_rn(x[i], inv), wn[lane * 8 + i]));
+      // Partial NeoX rotation on features [0, rot): pairs (i, i + rot/2).
+      float partner[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) partner[i] = __shfl_xor_sync(0xffffffffu, x[i], lane_half);
+      if (lane * 8 < rot) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int f = lane * 8 + i;
+          const int fi = f < half ? f : f - half;
+          const float c = cs_tab[warp][0][fi], sn = cs_tab[warp][1][fi];
+          // rotation * cos + rotate_half(rotation) * sin
+          const float rotated = f < half ? -partner[i] : partner[i];
+          x[i] = bf16_round(__fadd_rn(__fmul_rn(x[i], c), __fmul_rn(rotated, sn)));
+        }
+      }
+      uint16_t* dst = isq ? q_out + (t * H + hh) * (int64_t)d : k_out + (t * Hkv + (hh - H)) * (int64_t)d;
+      uint4 ov;
+      ov.x = pack_bf16x2(x[0], x[1]);
+      ov.y = pack_bf16x2(x[2], x[3]);
+      ov.z = pack_bf16x2(x[4], x[5]);
+      ov.w = pack_bf16x2(x[6], x[7]);
+      *reinterpret_cast<uint4*>(dst + lane * 8) = ov;
     }
   }
-  uint16_t* dst = isq ? q_out + (t * H + hh) * (int64_t)d : k_out + (t * Hkv + (hh - H)) * (int64_t)d;
-  uint4 o;
-  o.x = pack_bf16x2(x[0], x[1]);
-  o.y = pack_bf16x2(x[2], x[3]);
-  o.z = pack_bf16x2(x[4], x[5]);
-  o.w = pack_bf16x2(x[6], x[7]);
-  *reinterpret_cast<uint4*>(dst + lane * 8) = o;
 }
 
 // ---- embedding gather (Backbone::forward, qwen.rs:316-317; F32 cast :373) ----
@@ -469,7 +504,7 @@ int launch_delta_epilogue(const float* o, const float* z, int64_t ldz, const flo
   (void)dv;
   const int64_t rows = T * Hv;
   if (rows == 0) return CLEF_OK;
-  delta_epilogue_kernel<<<(unsigned)ceil_div(rows, 8), 256, 0, s>>>(o, z, ldz, w, eps, rows, Hv, y);
+  delta_epilogue_kernel<<<(unsigned)ceil_div(T, 8), 256, 0, s>>>(o, z, ldz, w, eps, T, Hv, y);
   return launch_status("delta_epilogue");
 }
 
@@ -480,7 +515,9 @@ int launch_attention_prologue(const uint16_t* proj, int64_t ldp, const float* qw
   (void)d;
   const int64_t rows = pack.total * (H + Hkv);
   if (rows == 0) return CLEF_OK;
-  attention_prologue_kernel<<<(unsigned)ceil_div(rows, 8), 256, 0, s>>>(
+  CLEF_CHECK(rot % 16 == 0 && rot <= 256, CLEF_ERR_UNSUPPORTED,
+             "attention_prologue: rotary_dim must be a multiple of 16, at most 256");
+  attention_prologue_kernel<<<(unsigned)ceil_div(pack.total, AP_WARPS), AP_WARPS * 32, 0, s>>>(
       proj, ldp, qw, kw, eps, pack.cu_seqlens, pack.nseq, pos_offset, H, Hkv, rot, inv_freq_dev,
       q_out, k_out, pack.total);
   return launch_status("attention_prologue");

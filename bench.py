@@ -58,7 +58,7 @@ def parse():
     ap.add_argument("--cpu-sample-tokens", type=int, default=256)
     ap.add_argument("--profile-op", default=None,
                     choices=["gemm", "gemm_swiglu", "scan", "scan1", "attention", "attention_tc",
-                             "prologue"],
+                             "prologue", "head"],
                     help="run one operator on a profiling-sized case and exit (for ncu)")
     ap.add_argument("--reps", type=int, default=3)
     return ap.parse_args()
@@ -255,6 +255,52 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # Our arm.
 # ---------------------------------------------------------------------------
+def _head_shapes(cfg):
+    """(name, shape) of every joint-head tensor (head.rs:91-145)."""
+    h, w, f = cfg["hidden_size"], cfg["width"], cfg["feedforward"]
+    out = []
+
+    def lin(n, o, i, bias):
+        out.append((f"{n}.weight", (o, i)))
+        if bias:
+            out.append((f"{n}.bias", (o,)))
+
+    def norm(n, k):
+        out.extend([(f"{n}.weight", (k,)), (f"{n}.bias", (k,))])
+
+    def attn(n):
+        out.extend([(f"{n}.in_proj_weight", (3 * w, w)), (f"{n}.in_proj_bias", (3 * w,))])
+        lin(f"{n}.out_proj", w, w, True)
+
+    for r in range(cfg["routing_layers"]):
+        p = f"evidence_layers.{r}"
+        norm(f"{p}.query_norm", w)
+        norm(f"{p}.memory_norm", w)
+        attn(f"{p}.attention")
+        norm(f"{p}.feedforward_norm", w)
+        lin(f"{p}.feedforward.0", f, w, True)
+        lin(f"{p}.feedforward.3", w, f, True)
+    for li in range(cfg["layers"]):
+        p = f"layers.{li}"
+        for n in ("norm1", "norm2", "norm3"):
+            norm(f"{p}.{n}", w)
+        attn(f"{p}.self_attn")
+        attn(f"{p}.multihead_attn")
+        lin(f"{p}.linear1", f, w, True)
+        lin(f"{p}.linear2", w, f, True)
+    norm("hidden_norm", h)
+    for n in ("memory_projection", "question_projection", "option_question_projection", "global_projection",
+              "option_context_projection", "option_lexical_projection"):
+        lin(n, w, h, False)
+    out.append(("type_embedding.weight", (3, w)))
+    for n in ("option_summary_norm", "field_norm", "option_norm"):
+        norm(n, w)
+    lin("residual_scorer.0", w, 4 * w, True)
+    lin("residual_scorer.3", 1, w, True)
+    out += [("prior_logit_scale", ()), ("joint_logit_scale", ()), ("residual_gate", ())]
+    return out
+
+
 def profile_op(args):
     """One operator on a case larger than L2 but a few GB at most: the inputs
     ncu captures (profiles/*.md give the command lines)."""
@@ -330,6 +376,36 @@ def profile_op(args):
         dt, alog = 0.1 * torch.randn(Hv, device=dev), torch.rand(Hv, device=dev) * 2.7
         timed(f"delta_prologue T={T}",
               lambda: cb.delta_prologue(proj, width + Hv * 128, width + Hv * 128 + Hv, conv, dt, alog, Hk, Hv))
+    elif args.profile_op == "head":
+        # The learned joint schema head at the released geometry on one record
+        # of T = 2048 tokens with 4 questions x 4 options (seeded weights).
+        cfg = dict(hidden_size=2560, width=1024, routing_layers=2, layers=4, heads=16, feedforward=4096)
+        head = cb.Head(cfg)
+        rng = np.random.default_rng(5)
+
+        def mat(o, i):
+            return (rng.standard_normal((o, i)) / np.sqrt(i)).astype(np.float32)
+
+        for name, shape in _head_shapes(cfg):
+            n = int(np.prod(shape)) if shape else 1
+            if len(shape) == 2:
+                head.set_weight(name, mat(*shape))
+            elif name.endswith(".weight") and "norm" in name:
+                head.set_weight(name, np.ones(n, np.float32))
+            else:
+                head.set_weight(name, (0.02 * rng.standard_normal(n)).astype(np.float32))
+        head.finalize()
+        T, vocab = 2048, 4096
+        hidden = torch.randn(T, 2560, device=dev)
+        emb = 0.05 * torch.randn(vocab, 2560, device=dev)
+        ids = rng.integers(0, vocab, T).astype(np.int32)
+        qs = [(q % 3, (100 * q, 100 * q + 20), [(100 * q + 20 + 10 * o, 100 * q + 30 + 10 * o) for o in range(4)])
+              for q in range(4)]
+        for _ in range(args.reps):
+            t0 = time.perf_counter()
+            head.forward(hidden, emb, ids, qs)
+            print(f"head T={T} 4x4 options: {1e3 * (time.perf_counter() - t0):.3f} ms (host clock, "
+                  f"includes the metadata upload and the final synchronisation)", flush=True)
     torch.cuda.synchronize()
     print(f"profile-op {args.profile_op}: ok", flush=True)
     return 0
@@ -459,7 +535,7 @@ def main():
     tf = ROOT / "profiles" / "gemm_traffic.txt"
     if tf.exists():
         traffic = json.loads(tf.read_text()).get("bytes_per_launch")
-    roofline = {"bound": "tensor", "kernel": "gemm_kernel (tcgen05 projection GEMMs, all launches)",
+    roofline = {"bound": "tensor", "kernel": "gemm_pair_kernel (tcgen05 cta_group::2 projection GEMMs, all launches)",
                 "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                 "frac": round(achieved / peak, 4), "peak_source": f"{pk_kind} bf16_tflops_sustained",
                 "traffic": traffic,

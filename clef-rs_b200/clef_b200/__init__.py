@@ -37,7 +37,8 @@ EXPORTS = [
     "clef_engine_weight_count", "clef_engine_finalize", "clef_engine_prefill",
     "clef_engine_prefill_device", "clef_engine_launches", "clef_engine_cancel",
     "clef_engine_stage_times", "clef_engine_set_profiling", "clef_engine_destroy",
-    "clef_prefix_tokens", "clef_prefix_bytes", "clef_prefix_destroy", "clef_decide",
+    "clef_prefix_tokens", "clef_prefix_bytes", "clef_prefix_destroy", "clef_head_create",
+    "clef_head_set_weight", "clef_head_finalize", "clef_head_forward", "clef_head_destroy", "clef_decide",
 ]
 
 
@@ -45,6 +46,19 @@ class ClefError(RuntimeError):
     def __init__(self, code: int, msg: str):
         super().__init__(f"{STATUS.get(code, code)}: {msg}")
         self.code = code
+
+
+class HeadConfig(ctypes.Structure):
+    """clef_head_config (HeadConfig, head.rs:26-33)."""
+    _fields_ = [("hidden_size", ctypes.c_int32), ("width", ctypes.c_int32),
+                ("routing_layers", ctypes.c_int32), ("layers", ctypes.c_int32),
+                ("heads", ctypes.c_int32), ("feedforward", ctypes.c_int32)]
+
+
+class HeadQuestion(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_int32), ("instruction_start", ctypes.c_int32),
+                ("instruction_end", ctypes.c_int32), ("option_offset", ctypes.c_int32),
+                ("option_count", ctypes.c_int32)]
 
 
 class Decision(ctypes.Structure):
@@ -95,6 +109,11 @@ def _load():
         "clef_prefix_tokens": (_i64, [_vp]),
         "clef_prefix_bytes": (ctypes.c_uint64, [_vp]),
         "clef_prefix_destroy": (ctypes.c_int, [_vp]),
+        "clef_head_create": (ctypes.c_int, [_vp, _i32, ctypes.POINTER(_vp)]),
+        "clef_head_set_weight": (ctypes.c_int, [_vp, ctypes.c_char_p, _vp, _i64]),
+        "clef_head_finalize": (ctypes.c_int, [_vp]),
+        "clef_head_forward": (ctypes.c_int, [_vp, _vp, _i64, _vp, _i64, _vp, _vp, _i32, _vp, _vp]),
+        "clef_head_destroy": (ctypes.c_int, [_vp]),
         "clef_decide": (ctypes.c_int, [_vp, _i32, _i32, _vp]),
     }
     for name, (res, args) in sig.items():
@@ -398,6 +417,63 @@ class Engine:
         if getattr(self, "handle", None) and lib is not None:
             lib.clef_engine_destroy(self.handle)
             self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Head:
+    """The learned joint schema head (Head::load / Head::forward,
+    head.rs:91-274) on one GPU, F32.
+
+    Usage: h = Head(dict(hidden_size=.., width=.., routing_layers=.., layers=..,
+    heads=.., feedforward=..)); h.set_weight(name, array) for every tensor of
+    joint_head.safetensors; h.finalize(); h.forward(hidden, output_embeddings,
+    ids, questions) with `questions` a list of (kind, (start, end),
+    [(start, end), ...]) and torch CUDA F32 tensors for hidden [T, hidden] and
+    output_embeddings [vocab, hidden]. Returns one numpy array per question.
+    """
+
+    def __init__(self, config, device=0):
+        self.cfg = HeadConfig(**{k: int(config[k]) for k, _ in HeadConfig._fields_})
+        h = _vp()
+        _check(lib.clef_head_create(ctypes.byref(self.cfg), device, ctypes.byref(h)))
+        self.h = h
+
+    def set_weight(self, name, array):
+        a = np.ascontiguousarray(np.asarray(array, dtype=np.float32)).reshape(-1)
+        _check(lib.clef_head_set_weight(self.h, name.encode(), a.ctypes.data, a.size))
+
+    def finalize(self):
+        _check(lib.clef_head_finalize(self.h))
+
+    def forward(self, hidden, output_embeddings, ids, questions):
+        ids = np.ascontiguousarray(np.asarray(ids, dtype=np.int32))
+        qs = (HeadQuestion * len(questions))()
+        spans, off = [], 0
+        for i, (kind, (s, e), options) in enumerate(questions):
+            qs[i] = HeadQuestion(kind, s, e, off, len(options))
+            for (a, b) in options:
+                spans += [a, b]
+            off += len(options)
+        spans = np.ascontiguousarray(np.asarray(spans, dtype=np.int32))
+        out = np.zeros(off, np.float32)
+        _check(lib.clef_head_forward(self.h, _ptr(hidden), int(hidden.shape[0]), _ptr(output_embeddings),
+                                     int(output_embeddings.shape[0]), ids.ctypes.data, qs, len(questions),
+                                     spans.ctypes.data, out.ctypes.data))
+        res, o = [], 0
+        for (_, _, options) in questions:
+            res.append(out[o:o + len(options)].copy())
+            o += len(options)
+        return res
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib.clef_head_destroy(self.h)
+            self.h = None
 
     def __del__(self):
         try:

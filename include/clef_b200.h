@@ -284,6 +284,57 @@ uint64_t clef_prefix_bytes(const clef_prefix* p);
 int clef_prefix_destroy(clef_prefix* p);
 
 /* ------------------------------------------------------------------------ */
+/* Learned joint schema head (Head, crates/core/src/models/head.rs:26-274):   */
+/* span means over the record's instruction and option spans, evidence       */
+/* routing, decoder layers and the joint scorer, in F32.                     */
+/* ------------------------------------------------------------------------ */
+/* HeadConfig (head.rs:26-33). The released head is hidden 2560 or 4096,
+ * width 1024, 2 routing layers, 4 decoder layers, 16 heads, feed-forward 4096
+ * (HeadConfig::validate, head.rs:34-47); other sizes are accepted for tests. */
+typedef struct clef_head_config {
+  int32_t hidden_size;
+  int32_t width;
+  int32_t routing_layers;
+  int32_t layers;
+  int32_t heads;
+  int32_t feedforward;
+} clef_head_config;
+
+/* One EncodedQuestion (encoding.rs): type kind 0..2, instruction token span
+ * [start, end), and its options as entries [option_offset, option_offset +
+ * option_count) of the option-span array (listed in question order). */
+typedef struct clef_head_question {
+  int32_t kind;
+  int32_t instruction_start;
+  int32_t instruction_end;
+  int32_t option_offset;
+  int32_t option_count;
+} clef_head_question;
+
+typedef struct clef_head clef_head;
+
+/* Replaces Head::load (head.rs:91-145): create, load every tensor by its
+ * checkpoint name (joint_head.safetensors names, e.g. "layers.0.norm1.weight",
+ * host F32; scalars prior_logit_scale, joint_logit_scale, residual_gate have
+ * count 1), then finalize. Weights stay F32 on the device. */
+int clef_head_create(const clef_head_config* cfg, int32_t device, clef_head** out);
+int clef_head_set_weight(clef_head* h, const char* name, const float* data, int64_t count);
+int clef_head_finalize(clef_head* h);
+
+/* Replaces Head::forward (head.rs:147-274) for one record.
+ * hidden: device F32 [T, hidden_size] (the backbone's final hidden rows);
+ * output_embeddings: device F32 [vocab, hidden_size]; ids: host int32 [T];
+ * questions: host [nq]; option_spans: host int32 [2 * options] as
+ * (start, end) pairs; logits: host F32 [options], question by question.
+ * Runs on the head's own stream and returns after the logits are on the
+ * host; a nonfinite logit is an error, as in the reference (head.rs:265-267).
+ * T <= 49152; at most 64 options per question. */
+int clef_head_forward(clef_head* h, const float* hidden, int64_t T, const float* output_embeddings,
+                      int64_t vocab, const int32_t* ids, const clef_head_question* questions,
+                      int32_t nq, const int32_t* option_spans, float* logits);
+int clef_head_destroy(clef_head* h);
+
+/* ------------------------------------------------------------------------ */
 /* Decisions from schema-head logits (answers, crates/core/src/types.rs:728-802). */
 /* ------------------------------------------------------------------------ */
 typedef struct clef_decision {

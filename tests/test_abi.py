@@ -156,3 +156,20 @@ def test_decide_matches_answers_rule():
     bad[0, 0] = np.inf
     with pytest.raises(cb.ClefError):
         cb.decide(bad)
+
+
+def test_head_rejects_bad_geometry_before_touching_a_device():
+    """clef_head_create validates HeadConfig (head.rs:26-47) before any CUDA
+    call: head width must divide 256, dimensions positive, handle required."""
+    L = cb.lib
+    h = ctypes.c_void_p()
+    cfg = cb.HeadConfig(hidden_size=2560, width=1024, routing_layers=2, layers=4, heads=16, feedforward=4096)
+    assert L.clef_head_create(None, 0, ctypes.byref(h)) == 1
+    bad = cb.HeadConfig(hidden_size=2560, width=1000, routing_layers=2, layers=4, heads=16, feedforward=4096)
+    assert L.clef_head_create(ctypes.byref(bad), 0, ctypes.byref(h)) == 3
+    bad = cb.HeadConfig(hidden_size=0, width=1024, routing_layers=2, layers=4, heads=16, feedforward=4096)
+    assert L.clef_head_create(ctypes.byref(bad), 0, ctypes.byref(h)) == 1
+    assert L.clef_head_create(ctypes.byref(cfg), 0, None) == 1
+    assert L.clef_head_set_weight(None, b"x", FAKE, 1) == 1
+    assert L.clef_head_finalize(None) == 1
+    assert L.clef_head_destroy(None) == 0

@@ -1,0 +1,125 @@
+"""The learned joint schema head on the GPU (clef_head_*, csrc/head.cu) against
+the reference's pinned fixture and the F32 oracle (oracle/head.py).
+
+- the reference's golden head fixture (models/mod.rs:176-235: hidden [20, 16],
+  three questions of kinds 0, 1, 2), tolerance 1e-5 + 1e-4|e| as the
+  reference's own test (mod.rs:75-86);
+- the released geometry (hidden 2560, width 1024, 16 heads, feed-forward 4096,
+  2 routing and 4 decoder layers) with seeded weights against the oracle on the
+  same inputs: F32 throughout, so the tolerance is F32 summation-order noise,
+  2e-4 + 2e-4|e| on the logits;
+- record validation before any launch (spans, ids, missing tensors).
+"""
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle.head import HeadConfig, Question, head_forward, random_head_weights
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def _make(cfg, weights):
+    import clef_b200 as cb
+    h = cb.Head(vars(cfg) if isinstance(cfg, HeadConfig) else cfg)
+    for k, v in weights.items():
+        h.set_weight(k, v)
+    h.finalize()
+    return h
+
+
+def _as_tuples(questions):
+    return [(q.kind, q.instruction, q.options) for q in questions]
+
+
+def test_head_matches_reference_golden_fixture():
+    z = np.load(Path(__file__).with_name("golden") / "head_fixture.npz")
+    cfg = HeadConfig(**json.loads(bytes(z["config_json"]).decode()))
+    w = {k[2:]: z[k] for k in z.files if k.startswith("w:")}
+    qs = [Question(k, tuple(i), [tuple(o) for o in opts])
+          for k, i, opts in json.loads(bytes(z["questions_json"]).decode())]
+    h = _make(cfg, w)
+    out = h.forward(torch.from_numpy(z["in:hidden"]).cuda(), torch.from_numpy(z["in:output_embeddings"]).cuda(),
+                    z["ids"], _as_tuples(qs))
+    for i, o in enumerate(out):
+        e = z[f"in:logits.{i}"]
+        err = np.abs(o - e)
+        print(f"question {i}: {o} vs {e}, max err {err.max():.2e}")
+        assert np.all(err <= 1e-5 + 1e-4 * np.abs(e))
+    # A second call on the same handle reuses its workspace and must agree.
+    again = h.forward(torch.from_numpy(z["in:hidden"]).cuda(), torch.from_numpy(z["in:output_embeddings"]).cuda(),
+                      z["ids"], _as_tuples(qs))
+    for a, b in zip(out, again):
+        assert np.array_equal(a, b)
+
+
+RELEASED = HeadConfig(hidden_size=2560, width=1024, routing_layers=2, layers=4, heads=16, feedforward=4096)
+
+
+def _record(T, vocab, rng):
+    ids = rng.integers(0, vocab, T).astype(np.int32)
+    qs, t = [], 1
+    for kind, nopt in ((0, 2), (1, 4), (2, 3), (1, 1)):
+        ins = (t, t + 5)
+        t += 5
+        opts = []
+        for _ in range(nopt):
+            n = int(rng.integers(1, 9))
+            opts.append((t, t + n))
+            t += n
+        qs.append(Question(kind, ins, opts))
+    assert t < T
+    return ids, qs
+
+
+@pytest.mark.parametrize("T", [200, 777])
+def test_head_released_geometry_matches_oracle(T):
+    rng = np.random.default_rng(T)
+    w = random_head_weights(RELEASED, seed=11)
+    vocab = 512
+    hidden = rng.standard_normal((T, RELEASED.hidden_size)).astype(np.float32)
+    emb = (0.05 * rng.standard_normal((vocab, RELEASED.hidden_size))).astype(np.float32)
+    ids, qs = _record(T, vocab, rng)
+    ref = head_forward(w, RELEASED, hidden, emb, list(ids), qs)
+    h = _make(RELEASED, w)
+    out = h.forward(torch.from_numpy(hidden).cuda(), torch.from_numpy(emb).cuda(), ids, _as_tuples(qs))
+    for o, e in zip(out, ref):
+        err = np.abs(o - e)
+        print(f"T={T}: {o} vs {e}, max err {err.max():.2e}")
+        assert np.all(np.isfinite(o)) and np.all(err <= 2e-4 + 2e-4 * np.abs(e))
+
+
+def test_head_rejects_bad_records_before_launch():
+    import clef_b200 as cb
+    cfg = HeadConfig(hidden_size=16, width=8, routing_layers=1, layers=1, heads=2, feedforward=32)
+    w = random_head_weights(cfg, seed=3)
+    h = cb.Head(vars(cfg))
+    for k, v in w.items():
+        if k != "residual_gate":
+            h.set_weight(k, v)
+    with pytest.raises(cb.ClefError, match="missing tensor residual_gate"):
+        h.finalize()
+    with pytest.raises(cb.ClefError, match="tensor shape"):
+        h.set_weight("residual_gate", np.zeros(2, np.float32))
+    h.set_weight("residual_gate", w["residual_gate"])
+    h.finalize()
+    T = 12
+    hid = torch.zeros(T, 16, device="cuda")
+    emb = torch.zeros(32, 16, device="cuda")
+    ids = np.arange(T, dtype=np.int32)
+    with pytest.raises(cb.ClefError, match="option span"):
+        h.forward(hid, emb, ids, [(0, (0, 2), [(5, 5)])])
+    with pytest.raises(cb.ClefError, match="instruction span"):
+        h.forward(hid, emb, ids, [(0, (3, 13), [(1, 2)])])
+    with pytest.raises(cb.ClefError, match="kind"):
+        h.forward(hid, emb, ids, [(3, (0, 2), [(1, 2)])])
+    bad = ids.copy()
+    bad[4] = 32
+    with pytest.raises(cb.ClefError, match="token id"):
+        h.forward(hid, emb, bad, [(0, (0, 2), [(1, 2)])])
+    out = h.forward(hid + 1.0, emb, ids, [(0, (0, 2), [(2, 4), (4, 6)])])
+    assert out[0].shape == (2,) and np.all(np.isfinite(out[0]))

@@ -148,3 +148,27 @@ def test_gemm_matches_float64():
     w = rng.standard_normal((50, 96)).astype(np.float32)
     y = oracle.linear(x, w)
     assert np.abs(y - x.astype(np.float64) @ w.astype(np.float64).T).max() < 1e-4
+
+
+def _head_fixture():
+    import json
+    from pathlib import Path
+
+    from oracle.head import HeadConfig, Question
+    z = np.load(Path(__file__).with_name("golden") / "head_fixture.npz")
+    cfg = HeadConfig(**json.loads(bytes(z["config_json"]).decode()))
+    w = {k[2:]: z[k] for k in z.files if k.startswith("w:")}
+    qs = [Question(k, tuple(i), [tuple(o) for o in opts])
+          for k, i, opts in json.loads(bytes(z["questions_json"]).decode())]
+    return z, cfg, w, qs
+
+
+def test_head_oracle_matches_reference_golden():
+    """oracle/head.py against the reference's pinned joint-head fixture
+    (models/mod.rs:176-235), tolerance 1e-5 + 1e-4|e| (:75-86)."""
+    from oracle.head import head_forward
+    z, cfg, w, qs = _head_fixture()
+    out = head_forward(w, cfg, z["in:hidden"], z["in:output_embeddings"], list(z["ids"]), qs)
+    assert len(out) == 3
+    for i, o in enumerate(out):
+        assert_close(o, z[f"in:logits.{i}"])

@@ -10,10 +10,11 @@
 // residual MLP). Every tensor is F32 like the reference's head; products use
 // F32 fused multiply-adds with F32 accumulation.
 //
-// The work of one record is a fixed sequence of small kernels on one stream:
-// the T-row operations (LayerNorm, memory projection, the key/value
-// projections of the memory for all six cross-attention layers) are the bulk;
-// everything per option or per question has at most a few dozen rows.
+// The work of one record is a fixed sequence of small kernels on one stream.
+// The T-row operations are the LayerNorms and the memory projection; the six
+// cross-attention layers are reassociated (qk_fold_kernel) so the memory rows
+// are only read, never projected to keys and values; everything per option or
+// per question has at most a few dozen rows.
 #include <cmath>
 #include <map>
 #include <string>
@@ -29,8 +30,6 @@ struct clef_head {
   std::map<std::string, std::vector<float>> host;     // loaded, not yet uploaded
   std::map<std::string, int64_t> off;                 // name -> float offset in blob
   float* blob = nullptr;
-  float* dec_kv_w = nullptr;  // [layers * 2 * width, width] decoder cross-attention K | V
-  float* dec_kv_b = nullptr;  // [layers * 2 * width]
   bool finalized = false;
   float prior_scale = 0.f, joint_scale = 0.f, gate = 0.f;
   // workspace
@@ -44,56 +43,113 @@ namespace clef {
 namespace {
 
 // ---- F32 GEMM on the CUDA cores --------------------------------------------
-// out[m, n] = res[m, n] + act(X[m, :] . W[n, :] + bias[n]); 64 x 64 tiles,
-// 16-wide K slabs through shared memory, 4 x 4 outputs per thread.
-constexpr int FB_M = 64, FB_N = 64, FB_K = 16;
+// out[m, n] = res[m, n] + act(sum_k X[m, k] W[n, k] + bias[n]) with W stored
+// [N, K] (a Linear weight), or with W stored [K, N] when W_KN. 128 x 128
+// tiles, 8-wide K slabs double-buffered through shared memory (the next slab
+// is fetched into registers while the current one is consumed), 8 x 8 outputs
+// per thread as four 4 x 4 blocks so every shared-memory read is a broadcast
+// or a conflict-free 16-byte load.
+constexpr int SG_M = 128, SG_N = 128, SG_K = 8, SG_PAD = 4;
 
 __device__ __forceinline__ float gelu_erf(float x) {
   // gelu_erf: 0.5 x (1 + erf(x / sqrt 2)).
   return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.f, erff(x * 0.70710678118654752f)));
 }
 
-__global__ void __launch_bounds__(256) f32_gemm_kernel(const float* __restrict__ X, int64_t ldx,
-                                                       const float* __restrict__ W, int64_t ldw, int M,
-                                                       int N, int K, const float* __restrict__ bias,
-                                                       int gelu, const float* res, int64_t ldr, float* out,
-                                                       int64_t ldo) {
-  __shared__ __align__(16) float As[FB_K][FB_M + 4];
-  __shared__ __align__(16) float Ws[FB_K][FB_N + 4];
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-  const int m0 = blockIdx.y * FB_M, n0 = blockIdx.x * FB_N;
-  float acc[4][4];
+template <bool W_KN>
+__global__ void __launch_bounds__(256) sgemm_kernel(const float* __restrict__ X, int64_t ldx,
+                                                    const float* __restrict__ W, int64_t ldw, int M, int N,
+                                                    int K, int kc, int vec, const float* __restrict__ bias,
+                                                    int gelu, const float* res, int64_t ldr, float* out,
+                                                    int64_t ldo) {
+  // Split K: this CTA sums k in [kb, ke); with gridDim.z > 1 it writes plain
+  // partial sums to slice z of `out` (the caller passes no epilogue).
+  const int kb = blockIdx.z * kc, ke = min(K, kb + kc);
+  if (gridDim.z > 1) out += (int64_t)blockIdx.z * M * ldo;
+  __shared__ __align__(16) float As[2][SG_K][SG_M + SG_PAD];
+  __shared__ __align__(16) float Bs[2][SG_K][SG_N + SG_PAD];
+  const int tid = threadIdx.x;
+  const int m0 = blockIdx.y * SG_M, n0 = blockIdx.x * SG_N;
+  // Loader coordinates: X rows (and [N, K] W rows) take 4 consecutive k per
+  // thread; a [K, N] W slab takes 4 consecutive n per thread.
+  const int lr = tid >> 1, lk = (tid & 1) * 4;
+  const int wk = tid >> 5, wn = (tid & 31) * 4;
+  float xa[4], wb[4];
+  auto load = [&](int k0) {
+    const int m = m0 + lr, k = k0 + lk;
+    if (vec && m < M && k < ke) {
+      const float4 v = *reinterpret_cast<const float4*>(X + (int64_t)m * ldx + k);
+      xa[0] = v.x, xa[1] = v.y, xa[2] = v.z, xa[3] = v.w;
+    } else {
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
-  for (int k0 = 0; k0 < K; k0 += FB_K) {
-    for (int i = threadIdx.x; i < FB_M * FB_K; i += 256) {
-      const int r = i / FB_K, kk = i % FB_K, k = k0 + kk;
-      const int m = m0 + r, n = n0 + r;
-      As[kk][r] = (m < M && k < K) ? X[(int64_t)m * ldx + k] : 0.f;
-      Ws[kk][r] = (n < N && k < K) ? W[(int64_t)n * ldw + k] : 0.f;
+      for (int i = 0; i < 4; ++i) xa[i] = (m < M && k + i < ke) ? X[(int64_t)m * ldx + k + i] : 0.f;
     }
-    __syncthreads();
+    if (!W_KN) {
+      const int n = n0 + lr;
+      if (vec && n < N && k < ke) {
+        const float4 v = *reinterpret_cast<const float4*>(W + (int64_t)n * ldw + k);
+        wb[0] = v.x, wb[1] = v.y, wb[2] = v.z, wb[3] = v.w;
+      } else {
 #pragma unroll
-    for (int kk = 0; kk < FB_K; ++kk) {
-      const float4 a = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
-      const float4 b = *reinterpret_cast<const float4*>(&Ws[kk][tx * 4]);
-      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+        for (int i = 0; i < 4; ++i) wb[i] = (n < N && k + i < ke) ? W[(int64_t)n * ldw + k + i] : 0.f;
+      }
+    } else {
+      const int kk = k0 + wk, n = n0 + wn;
+      if (vec && kk < ke && n < N) {
+        const float4 v = *reinterpret_cast<const float4*>(W + (int64_t)kk * ldw + n);
+        wb[0] = v.x, wb[1] = v.y, wb[2] = v.z, wb[3] = v.w;
+      } else {
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        for (int i = 0; i < 4; ++i) wb[i] = (kk < ke && n + i < N) ? W[(int64_t)kk * ldw + n + i] : 0.f;
+      }
     }
+  };
+  auto store = [&](int buf) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) As[buf][lk + i][lr] = xa[i];
+    if (!W_KN) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) Bs[buf][lk + i][lr] = wb[i];
+    } else {
+      *reinterpret_cast<float4*>(&Bs[buf][wk][wn]) = make_float4(wb[0], wb[1], wb[2], wb[3]);
+    }
+  };
+  const int tx = tid & 15, ty = tid >> 4;
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  load(kb);
+  store(0);
+  __syncthreads();
+  for (int k0 = kb, it = 0; k0 < ke; k0 += SG_K, ++it) {
+    const int buf = it & 1;
+    const bool more = k0 + SG_K < ke;
+    if (more) load(k0 + SG_K);
+#pragma unroll
+    for (int kk = 0; kk < SG_K; ++kk) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][64 + ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][kk][64 + tx * 4]);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    if (more) store(buf ^ 1);
     __syncthreads();
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int m = m0 + ty * 4 + i;
+  for (int i = 0; i < 8; ++i) {
+    const int m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
     if (m >= M) continue;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int n = n0 + tx * 4 + j;
+    for (int j = 0; j < 8; ++j) {
+      const int n = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + j - 4);
       if (n >= N) continue;
       float v = acc[i][j];
       if (bias) v = __fadd_rn(v, bias[n]);
@@ -210,6 +266,64 @@ __global__ void __launch_bounds__(256) attention_f32_kernel(const float* __restr
     float o = 0.f;
     for (int gi = 0; gi < groups; ++gi) o = __fadd_rn(o, part[gi * hd + threadIdx.x]);
     out[(int64_t)qi * ldo + (int64_t)h * hd + threadIdx.x] = __fdiv_rn(o, sum);
+  }
+}
+
+// Cross-attention of a few query rows over the T memory rows, reassociated
+// so the memory is never projected to keys and values (MultiAttention::forward,
+// ops.rs:198-224, with k_t = Wk m_t + bk and v_t = Wv m_t + bv):
+//   score(o, h, t) = q_oh . (Wk_h m_t + bk_h) = (Wk_h^T q_oh) . m_t + q_oh . bk_h,
+// and the last term is the same for every t, so it cancels in the softmax;
+//   out(o, h) = sum_t p_t (Wv_h m_t + bv_h) = Wv_h (sum_t p_t m_t) + bv_h,
+// as the probabilities sum to one. Rows of U, S and C are (o, h) pairs.
+
+// U[(o, h), c] = sum_d q[o, h*hd + d] * Wk[h*hd + d, c].
+__global__ void qk_fold_kernel(const float* __restrict__ q, int64_t ldq, const float* __restrict__ Wk, int width,
+                               int heads, int hd, float* __restrict__ U) {
+  __shared__ float qs[256];
+  const int r = blockIdx.x, o = r / heads, h = r % heads;
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) qs[d] = q[(int64_t)o * ldq + (int64_t)h * hd + d];
+  __syncthreads();
+  const float* wk = Wk + (int64_t)h * hd * width;
+  for (int c = threadIdx.x; c < width; c += blockDim.x) {
+    float acc = 0.f;
+    for (int d = 0; d < hd; ++d) acc = fmaf(qs[d], wk[(int64_t)d * width + c], acc);
+    U[(int64_t)r * width + c] = acc;
+  }
+}
+
+// In place: S[r, :] = softmax(S[r, :] * scale) over n columns.
+__global__ void __launch_bounds__(256) softmax_rows_kernel(float* __restrict__ S, int64_t lds, int n,
+                                                           float scale) {
+  __shared__ float red[32];
+  float* row = S + (int64_t)blockIdx.x * lds;
+  float mx = -INFINITY;
+  for (int t = threadIdx.x; t < n; t += blockDim.x) mx = fmaxf(mx, __fmul_rn(row[t], scale));
+  mx = block_max(mx, red);
+  float sum = 0.f;
+  for (int t = threadIdx.x; t < n; t += blockDim.x) {
+    const float e = expf(__fsub_rn(__fmul_rn(row[t], scale), mx));
+    row[t] = e;
+    sum += e;
+  }
+  const float inv_sum = block_sum(sum, red);
+  for (int t = threadIdx.x; t < n; t += blockDim.x) row[t] = __fdiv_rn(row[t], inv_sum);
+}
+
+// out[o, h*hd + d] = sum_c Wv[h*hd + d, c] * C[(o, h), c] + bv[h*hd + d]; one
+// warp per output feature.
+__global__ void __launch_bounds__(256) v_unfold_kernel(const float* __restrict__ C, const float* __restrict__ Wv,
+                                                       const float* __restrict__ bv, int width, int heads, int hd,
+                                                       float* __restrict__ out, int64_t ldo) {
+  const int o = blockIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int f = blockIdx.y * nw + wid; f < width; f += gridDim.y * nw) {
+    const int h = f / hd;
+    const float* cr = C + ((int64_t)o * heads + h) * width;
+    const float* wr = Wv + (int64_t)f * width;
+    float acc = 0.f;
+    for (int c = lane; c < width; c += 32) acc = fmaf(wr[c], cr[c], acc);
+    for (int k = 16; k; k >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, k);
+    if (lane == 0) out[(int64_t)o * ldo + f] = __fadd_rn(acc, bv[f]);
   }
 }
 
@@ -337,13 +451,68 @@ __global__ void logits_kernel(const float* __restrict__ prior, const float* __re
     out[o] = __fadd_rn(prior[o], __fmul_rn(__fadd_rn(__fmul_rn(cosine[o], joint_scale), resid[o]), gate));
 }
 
+// out[m, n] = res[m, n] + act(sum_z P[z, m, n] + bias[n]), slices summed in order.
+__global__ void splitk_reduce_kernel(const float* __restrict__ P, int splits, int M, int N,
+                                     const float* __restrict__ bias, int gelu, const float* res, int64_t ldr,
+                                     float* out, int64_t ldo) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)M * N) return;
+  const int m = (int)(i / N), n = (int)(i % N);
+  float v = P[i];
+  for (int z = 1; z < splits; ++z) v = __fadd_rn(v, P[(int64_t)z * M * N + i]);
+  if (bias) v = __fadd_rn(v, bias[n]);
+  if (gelu) v = gelu_erf(v);
+  if (res) v = __fadd_rn(res[(int64_t)m * ldr + n], v);
+  out[(int64_t)m * ldo + n] = v;
+}
+
+// Split-K partial sums of the head's GEMMs live here (one buffer per device
+// handle, sized at workspace planning).
+struct SplitK {
+  float* part = nullptr;
+  size_t cap = 0;  // floats
+  int sms = 148;
+};
+thread_local SplitK g_split;
+
 int gemm_f32(const float* X, int64_t ldx, const float* W, int64_t ldw, int M, int N, int K, const float* bias,
-             bool gelu, const float* res, int64_t ldr, float* out, int64_t ldo, cudaStream_t s) {
+             bool gelu, const float* res, int64_t ldr, float* out, int64_t ldo, cudaStream_t s, bool w_kn = false) {
   if (M == 0 || N == 0) return CLEF_OK;
-  const dim3 grid((unsigned)ceil_div(N, FB_N), (unsigned)ceil_div(M, FB_M));
+  dim3 grid((unsigned)ceil_div(N, SG_N), (unsigned)ceil_div(M, SG_M), 1);
   CLEF_CHECK(grid.y <= 65535u, CLEF_ERR_UNSUPPORTED, "head: too many rows");
-  f32_gemm_kernel<<<grid, 256, 0, s>>>(X, ldx, W, ldw, M, N, K, bias, gelu ? 1 : 0, res, ldr, out, ldo);
-  return launch_status("head gemm");
+  // 16-byte loads when every row start is 16-byte aligned and K (or N for a
+  // [K, N] weight) is a multiple of 4.
+  const bool vec = (((uintptr_t)X | (uintptr_t)W) & 15) == 0 && ldx % 4 == 0 && ldw % 4 == 0 &&
+                   (w_kn ? (K % 4 == 0 && N % 4 == 0) : K % 4 == 0);
+  // Too few output tiles to fill the GPU: split K into slabs of >= 64 that
+  // sum in a second pass (deterministic order), up to 32 ways.
+  const int64_t tiles = (int64_t)grid.x * grid.y;
+  int splits = 1, kc = K;
+  if (tiles < 2 * g_split.sms && g_split.part) {
+    int want = (int)std::min<int64_t>(32, ceil_div(2 * g_split.sms, tiles));
+    want = std::min<int64_t>(want, std::max<int64_t>(1, K / 64));
+    want = (int)std::min<int64_t>(want, (int64_t)(g_split.cap / ((size_t)M * N)));
+    if (want > 1) {
+      kc = (int)(ceil_div(ceil_div(K, want), SG_K) * SG_K);
+      splits = (int)ceil_div(K, kc);
+    }
+  }
+  grid.z = (unsigned)splits;
+  float* dst = splits > 1 ? g_split.part : out;
+  const int64_t ldd = splits > 1 ? N : ldo;
+  const float* eb = splits > 1 ? nullptr : bias;
+  const float* er = splits > 1 ? nullptr : res;
+  const int eg = splits > 1 ? 0 : (gelu ? 1 : 0);
+  if (w_kn)
+    sgemm_kernel<true><<<grid, 256, 0, s>>>(X, ldx, W, ldw, M, N, K, kc, vec, eb, eg, er, ldr, dst, ldd);
+  else
+    sgemm_kernel<false><<<grid, 256, 0, s>>>(X, ldx, W, ldw, M, N, K, kc, vec, eb, eg, er, ldr, dst, ldd);
+  int rc = launch_status("head gemm");
+  if (rc || splits == 1) return rc;
+  const int64_t n = (int64_t)M * N;
+  splitk_reduce_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(g_split.part, splits, M, N, bias, gelu ? 1 : 0, res,
+                                                                  ldr, out, ldo);
+  return launch_status("head split-k reduce");
 }
 
 int layer_norm(const float* x, int64_t ldx, int rows, int n, const float* w, const float* b, float* out,
@@ -371,6 +540,26 @@ int attention_f32(const float* Q, int64_t ldq, const float* K, int64_t ldk, cons
   attention_f32_kernel<<<dim3((unsigned)nq, (unsigned)heads), 256, smem, s>>>(
       Q, ldq, K, ldk, V, ldv, nk, hd, (float)(1.0 / std::sqrt((double)hd)), out, ldo);
   return launch_status("head attention");
+}
+
+// Reassociated cross-attention (see qk_fold_kernel): q [R0, width] already
+// projected (Wq, bq); memory [T, width]; U, C [R0 * heads, width] and S
+// [R0 * heads, T] are workspace; out [R0, width] before the output projection.
+int cross_attention(const float* q, int R0, const float* mem, int T, const float* Wk, const float* Wv,
+                    const float* bv, int width, int heads, float* U, float* S, float* C, float* out, cudaStream_t s) {
+  if (R0 == 0) return CLEF_OK;
+  const int hd = width / heads, R = R0 * heads;
+  qk_fold_kernel<<<R, 256, 0, s>>>(q, width, Wk, width, heads, hd, U);
+  int rc = launch_status("head qk_fold");
+  if (!rc) rc = gemm_f32(U, width, mem, width, R, T, width, nullptr, false, nullptr, 0, S, T, s);
+  if (rc) return rc;
+  softmax_rows_kernel<<<R, 256, 0, s>>>(S, T, T, (float)(1.0 / std::sqrt((double)hd)));
+  rc = launch_status("head softmax");
+  if (!rc) rc = gemm_f32(S, T, mem, width, R, width, T, nullptr, false, nullptr, 0, C, width, s, true);
+  if (rc) return rc;
+  v_unfold_kernel<<<dim3((unsigned)R0, (unsigned)std::max(1, std::min(32, width / 8))), 256, 0, s>>>(
+      C, Wv, bv, width, heads, hd, out, width);
+  return launch_status("head v_unfold");
 }
 
 // Tensor names and shapes of the head (head.rs:91-145, weights.rs:135-188).
@@ -455,15 +644,17 @@ const float* W(const clef_head* hd, const std::string& name) { return hd->blob +
 
 // Workspace layout for one record; every slot is a multiple of 64 floats.
 struct HeadWs {
-  float *normalized, *memory, *nm, *kv, *qs, *ctx, *lex, *routed, *tq, *q, *att, *ffh, *base, *oq, *summ,
-      *summn, *fields, *gproj, *qkv, *anchor, *opts, *feats, *r1, *resid, *prior, *cosine, *logits;
+  float *normalized, *memory, *nm, *U, *S, *C, *qs, *ctx, *lex, *routed, *tq, *q, *att, *ffh, *base, *oq, *summ,
+      *summn, *fields, *gproj, *qkv, *anchor, *opts, *feats, *r1, *resid, *prior, *cosine, *logits, *part;
 };
+
+constexpr int64_t kSplitCap = 4 << 20;  // floats of split-K partial sums (16 MB)
 
 size_t plan_ws(const clef_head_config& c, int64_t T, int nq, int no, float* base, HeadWs* w) {
   size_t off = 0;
   const int64_t h = c.hidden_size, wd = c.width, ff = c.feedforward;
   const int64_t rows = std::max(nq, no);
-  const int64_t kvw = std::max<int64_t>(2 * wd, 2 * wd * c.layers);
+  const int64_t R = rows * c.heads;
   auto take = [&](float** p, int64_t n) {
     if (w) *p = base + off;
     off += (size_t)((n + 63) / 64 * 64);
@@ -473,7 +664,9 @@ size_t plan_ws(const clef_head_config& c, int64_t T, int nq, int no, float* base
   take(&t->normalized, T * h);
   take(&t->memory, T * wd);
   take(&t->nm, T * wd);
-  take(&t->kv, T * kvw);
+  take(&t->U, R * wd);
+  take(&t->S, R * T);
+  take(&t->C, R * wd);
   take(&t->qs, nq * h);
   take(&t->ctx, no * h);
   take(&t->lex, no * h);
@@ -497,6 +690,7 @@ size_t plan_ws(const clef_head_config& c, int64_t T, int nq, int no, float* base
   take(&t->prior, no);
   take(&t->cosine, no);
   take(&t->logits, no);
+  take(&t->part, kSplitCap);
   return off * sizeof(float);
 }
 
@@ -553,26 +747,12 @@ int clef_head_finalize(clef_head* hd) {
     hd->off[kv.first] = total;
     total += (numel(kv.second) + 63) / 64 * 64;
   }
-  const int64_t kvn = 2 * w * c.layers;  // fused decoder K | V rows
-  const int64_t kvw_off = total;
-  total += (kvn * w + 63) / 64 * 64;
-  const int64_t kvb_off = total;
-  total += (kvn + 63) / 64 * 64;
   DeviceGuardH g(hd->device);
   CLEF_CUDA(cudaMalloc(&hd->blob, sizeof(float) * (size_t)std::max<int64_t>(total, 64)));
   std::vector<float> staging((size_t)total, 0.f);
   for (const auto& kv : hd->host)
     std::copy(kv.second.begin(), kv.second.end(), staging.begin() + hd->off[kv.first]);
-  for (int l = 0; l < c.layers; ++l) {
-    const std::string p = "layers." + std::to_string(l) + ".multihead_attn";
-    const auto& iw = hd->host[p + ".in_proj_weight"];
-    const auto& ib = hd->host[p + ".in_proj_bias"];
-    std::copy(iw.begin() + w * w, iw.end(), staging.begin() + kvw_off + (int64_t)l * 2 * w * w);
-    std::copy(ib.begin() + w, ib.end(), staging.begin() + kvb_off + (int64_t)l * 2 * w);
-  }
   CLEF_CUDA(cudaMemcpy(hd->blob, staging.data(), sizeof(float) * (size_t)total, cudaMemcpyHostToDevice));
-  hd->dec_kv_w = hd->blob + kvw_off;
-  hd->dec_kv_b = hd->blob + kvb_off;
   // Scalars as Head::load derives them (head.rs:128-130).
   const double lim = std::log(100.0);
   hd->prior_scale = (float)std::exp(std::min((double)hd->host["prior_logit_scale"][0], lim));
@@ -665,6 +845,9 @@ int clef_head_forward(clef_head* hd, const float* hidden, int64_t T, const float
     if (rc_) return rc_;        \
   } while (0)
   const int Ti = (int)T;
+  g_split.part = b.part;
+  g_split.cap = (size_t)kSplitCap;
+  g_split.sms = num_sms(hd->device);
   // Memory side (head.rs:154-157).
   RCH(layer_norm(hidden, h, Ti, (int)h, W(hd, "hidden_norm.weight"), W(hd, "hidden_norm.bias"), b.normalized, h, s));
   RCH(gemm_f32(b.normalized, h, W(hd, "memory_projection.weight"), h, Ti, (int)wd, (int)h, nullptr, false, nullptr, 0,
@@ -696,8 +879,8 @@ int clef_head_forward(clef_head* hd, const float* hidden, int64_t T, const float
     const float* iw = W(hd, a + ".in_proj_weight");
     const float* ib = W(hd, a + ".in_proj_bias");
     RCH(gemm_f32(b.tq, wd, iw, wd, no, (int)wd, (int)wd, ib, false, nullptr, 0, b.q, wd, s));
-    RCH(gemm_f32(b.nm, wd, iw + wd * wd, wd, Ti, (int)(2 * wd), (int)wd, ib + wd, false, nullptr, 0, b.kv, 2 * wd, s));
-    RCH(attention_f32(b.q, wd, b.kv, 2 * wd, b.kv + wd, 2 * wd, no, Ti, c.heads, hdim, b.att, wd, s));
+    RCH(cross_attention(b.q, no, b.nm, Ti, iw + wd * wd, iw + 2 * wd * wd, ib + 2 * wd, (int)wd, c.heads, b.U, b.S,
+                        b.C, b.att, s));
     RCH(gemm_f32(b.att, wd, W(hd, a + ".out_proj.weight"), wd, no, (int)wd, (int)wd, W(hd, a + ".out_proj.bias"),
                  false, b.routed, wd, b.routed, wd, s));
     RCH(layer_norm(b.routed, wd, no, (int)wd, W(hd, p + ".feedforward_norm.weight"),
@@ -720,12 +903,8 @@ int clef_head_forward(clef_head* hd, const float* hidden, int64_t T, const float
   fields_kernel<<<nq, 256, 0, s>>>(b.base, b.summn, b.gproj, W(hd, "type_embedding.weight"), d_kind, (int)wd,
                                    b.fields);
   RCH(launch_status("head fields"));
-  // Decoder layers (head.rs:230-241); the memory's keys and values for all of
-  // them come from one projection of the (un-normalised) memory.
-  if (c.layers > 0)
-    RCH(gemm_f32(b.memory, wd, hd->dec_kv_w, wd, Ti, (int)(2 * wd * c.layers), (int)wd, hd->dec_kv_b, false, nullptr,
-                 0, b.kv, 2 * wd * c.layers, s));
-  const int64_t ldkv = 2 * wd * c.layers;
+  // Decoder layers (head.rs:230-241); the cross-attention reads the
+  // un-normalised memory.
   for (int l = 0; l < c.layers; ++l) {
     const std::string p = "layers." + std::to_string(l);
     RCH(layer_norm(b.fields, wd, nq, (int)wd, W(hd, p + ".norm1.weight"), W(hd, p + ".norm1.bias"), b.tq, wd, s));
@@ -738,8 +917,10 @@ int clef_head_forward(clef_head* hd, const float* hidden, int64_t T, const float
     RCH(layer_norm(b.fields, wd, nq, (int)wd, W(hd, p + ".norm2.weight"), W(hd, p + ".norm2.bias"), b.tq, wd, s));
     RCH(gemm_f32(b.tq, wd, W(hd, p + ".multihead_attn.in_proj_weight"), wd, nq, (int)wd, (int)wd,
                  W(hd, p + ".multihead_attn.in_proj_bias"), false, nullptr, 0, b.q, wd, s));
-    const float* kl = b.kv + (int64_t)l * 2 * wd;
-    RCH(attention_f32(b.q, wd, kl, ldkv, kl + wd, ldkv, nq, Ti, c.heads, hdim, b.att, wd, s));
+    const float* mw = W(hd, p + ".multihead_attn.in_proj_weight");
+    RCH(cross_attention(b.q, nq, b.memory, Ti, mw + wd * wd, mw + 2 * wd * wd,
+                        W(hd, p + ".multihead_attn.in_proj_bias") + 2 * wd, (int)wd, c.heads, b.U, b.S, b.C, b.att,
+                        s));
     RCH(gemm_f32(b.att, wd, W(hd, p + ".multihead_attn.out_proj.weight"), wd, nq, (int)wd, (int)wd,
                  W(hd, p + ".multihead_attn.out_proj.bias"), false, b.fields, wd, b.fields, wd, s));
     RCH(layer_norm(b.fields, wd, nq, (int)wd, W(hd, p + ".norm3.weight"), W(hd, p + ".norm3.bias"), b.tq, wd, s));

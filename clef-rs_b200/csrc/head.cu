@@ -160,6 +160,110 @@ __global__ void __launch_bounds__(256) sgemm_kernel(const float* __restrict__ X,
   }
 }
 
+// Skinny GEMM for M <= 16 rows (option and question rows): out[m, n] =
+// res + act(X[m, :] . W[n, :] + bias[n]). A CTA covers 32 output columns
+// (4 per warp) for all rows; X is staged in shared memory 512 columns of K at
+// a time, W rows stream from global memory once, 16-byte loads along K.
+constexpr int SK_M = 16, SK_KC = 512, SK_COLS = 4;
+
+struct SkinnyBatch {
+  int64_t x, w, out, bias;  // per-batch element offsets (blockIdx.z)
+};
+
+__global__ void __launch_bounds__(256) skinny_gemm_kernel(const float* __restrict__ X, int64_t ldx,
+                                                          const float* __restrict__ W, int64_t ldw, int M, int N,
+                                                          int K, int kc, SkinnyBatch bs,
+                                                          const float* __restrict__ bias, int gelu,
+                                                          const float* res, int64_t ldr, float* out, int64_t ldo) {
+  __shared__ __align__(16) float xs[SK_M][SK_KC];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nb = blockIdx.x * 8 * SK_COLS + warp * SK_COLS;
+  // Batch element z = blockIdx.z; K slab [kb, ke) = blockIdx.y. With several
+  // slabs the CTA writes plain partial sums to slice (y, z) of `out` (layout
+  // [slabs][batch][M][N]) and the caller reduces them.
+  const int z = blockIdx.z;
+  X += z * bs.x;
+  W += z * bs.w;
+  const int kb = blockIdx.y * kc, ke = min(K, kb + kc);
+  if (gridDim.y > 1) {
+    out += ((int64_t)blockIdx.y * gridDim.z + z) * M * ldo;
+  } else {
+    out += z * bs.out;
+    if (bias) bias += z * bs.bias;
+  }
+  float acc[SK_M][SK_COLS];
+#pragma unroll
+  for (int m = 0; m < SK_M; ++m)
+#pragma unroll
+    for (int j = 0; j < SK_COLS; ++j) acc[m][j] = 0.f;
+  for (int k0 = kb; k0 < ke; k0 += SK_KC) {
+    const int kn = min(SK_KC, ke - k0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < SK_M * (SK_KC / 4); i += blockDim.x) {
+      const int m = i / (SK_KC / 4), k = (i % (SK_KC / 4)) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (m < M && k < kn) {
+        const float* src = X + (int64_t)m * ldx + k0 + k;
+        v.x = src[0];
+        if (k + 1 < kn) v.y = src[1];
+        if (k + 2 < kn) v.z = src[2];
+        if (k + 3 < kn) v.w = src[3];
+      }
+      *reinterpret_cast<float4*>(&xs[m][k]) = v;
+    }
+    __syncthreads();
+    for (int k = lane * 4; k < kn; k += 128) {
+      float4 wv[SK_COLS];
+#pragma unroll
+      for (int j = 0; j < SK_COLS; ++j) {
+        const int n = nb + j;
+        wv[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (n < N) {
+          const float* src = W + (int64_t)n * ldw + k0 + k;
+          wv[j].x = src[0];
+          if (k + 1 < kn) wv[j].y = src[1];
+          if (k + 2 < kn) wv[j].z = src[2];
+          if (k + 3 < kn) wv[j].w = src[3];
+        }
+      }
+#pragma unroll
+      for (int m = 0; m < SK_M; ++m) {
+        const float4 xv = *reinterpret_cast<const float4*>(&xs[m][k]);
+#pragma unroll
+        for (int j = 0; j < SK_COLS; ++j) {
+          acc[m][j] = fmaf(xv.x, wv[j].x, acc[m][j]);
+          acc[m][j] = fmaf(xv.y, wv[j].y, acc[m][j]);
+          acc[m][j] = fmaf(xv.z, wv[j].z, acc[m][j]);
+          acc[m][j] = fmaf(xv.w, wv[j].w, acc[m][j]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < SK_M; ++m)
+#pragma unroll
+    for (int j = 0; j < SK_COLS; ++j)
+#pragma unroll
+      for (int o = 16; o; o >>= 1) acc[m][j] += __shfl_xor_sync(0xffffffffu, acc[m][j], o);
+  // Lane l writes entries l and l + 32 of the 16 x 4 block.
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int idx = lane + 32 * e, m = idx / SK_COLS, j = idx % SK_COLS, n = nb + j;
+    float v = 0.f;
+#pragma unroll
+    for (int mm = 0; mm < SK_M; ++mm)
+#pragma unroll
+      for (int jj = 0; jj < SK_COLS; ++jj)
+        if (mm * SK_COLS + jj == idx) v = acc[mm][jj];
+    if (m < M && n < N) {
+      if (bias) v = __fadd_rn(v, bias[n]);
+      if (gelu) v = gelu_erf(v);
+      if (res) v = __fadd_rn(res[(int64_t)m * ldr + n], v);
+      out[(int64_t)m * ldo + n] = v;
+    }
+  }
+}
+
 __device__ __forceinline__ float block_sum(float v, float* red) {
   for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
@@ -277,19 +381,34 @@ __global__ void __launch_bounds__(256) attention_f32_kernel(const float* __restr
 //   out(o, h) = sum_t p_t (Wv_h m_t + bv_h) = Wv_h (sum_t p_t m_t) + bv_h,
 // as the probabilities sum to one. Rows of U, S and C are (o, h) pairs.
 
-// U[(o, h), c] = sum_d q[o, h*hd + d] * Wk[h*hd + d, c].
-__global__ void qk_fold_kernel(const float* __restrict__ q, int64_t ldq, const float* __restrict__ Wk, int width,
-                               int heads, int hd, float* __restrict__ U) {
-  __shared__ float qs[256];
-  const int r = blockIdx.x, o = r / heads, h = r % heads;
-  for (int d = threadIdx.x; d < hd; d += blockDim.x) qs[d] = q[(int64_t)o * ldq + (int64_t)h * hd + d];
-  __syncthreads();
-  const float* wk = Wk + (int64_t)h * hd * width;
-  for (int c = threadIdx.x; c < width; c += blockDim.x) {
-    float acc = 0.f;
-    for (int d = 0; d < hd; ++d) acc = fmaf(qs[d], wk[(int64_t)d * width + c], acc);
-    U[(int64_t)r * width + c] = acc;
+// U[(o, h), c] = sum_d q[o, h*hd + d] * Wk[h*hd + d, c]. CTA = (256 columns,
+// head, 16 query rows): the rows' head slice of q sits in shared memory and
+// each Wk element is read once per CTA.
+__global__ void __launch_bounds__(256) qk_fold_kernel(const float* __restrict__ q, int64_t ldq,
+                                                      const float* __restrict__ Wk, int width, int heads, int hd,
+                                                      int R0, float* __restrict__ U) {
+  __shared__ float qs[16][256];
+  const int h = blockIdx.y, r0 = blockIdx.z * 16;
+  const int nr = min(16, R0 - r0);
+  for (int i = threadIdx.x; i < 16 * hd; i += blockDim.x) {
+    const int r = i / hd, d = i % hd;
+    qs[r][d] = r < nr ? q[(int64_t)(r0 + r) * ldq + (int64_t)h * hd + d] : 0.f;
   }
+  __syncthreads();
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= width) return;
+  float acc[16];
+#pragma unroll
+  for (int r = 0; r < 16; ++r) acc[r] = 0.f;
+  const float* wk = Wk + (int64_t)h * hd * width + c;
+  for (int d = 0; d < hd; ++d) {
+    const float w = wk[(int64_t)d * width];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) acc[r] = fmaf(qs[r][d], w, acc[r]);
+  }
+#pragma unroll
+  for (int r = 0; r < 16; ++r)
+    if (r < nr) U[((int64_t)(r0 + r) * heads + h) * width + c] = acc[r];
 }
 
 // In place: S[r, :] = softmax(S[r, :] * scale) over n columns.
@@ -310,18 +429,31 @@ __global__ void __launch_bounds__(256) softmax_rows_kernel(float* __restrict__ S
   for (int t = threadIdx.x; t < n; t += blockDim.x) row[t] = __fdiv_rn(row[t], inv_sum);
 }
 
-// out[o, h*hd + d] = sum_c Wv[h*hd + d, c] * C[(o, h), c] + bv[h*hd + d]; one
-// warp per output feature.
+// out[o, h*hd + d] = sum_c Wv[h*hd + d, c] * C[(o, h), c] + bv[h*hd + d]. One
+// warp per output feature f: its Wv row is read once into registers and
+// dotted with the C rows of all query rows o (head h = f / hd).
 __global__ void __launch_bounds__(256) v_unfold_kernel(const float* __restrict__ C, const float* __restrict__ Wv,
                                                        const float* __restrict__ bv, int width, int heads, int hd,
-                                                       float* __restrict__ out, int64_t ldo) {
-  const int o = blockIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (int f = blockIdx.y * nw + wid; f < width; f += gridDim.y * nw) {
-    const int h = f / hd;
+                                                       int R0, float* __restrict__ out, int64_t ldo) {
+  const int lane = threadIdx.x & 31;
+  const int f = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (f >= width) return;
+  const int h = f / hd;
+  constexpr int MAXW = 64;  // elements per lane: width <= 2048
+  float wr[MAXW];
+#pragma unroll
+  for (int i = 0; i < MAXW; ++i) {
+    const int c = lane + 32 * i;
+    wr[i] = c < width ? Wv[(int64_t)f * width + c] : 0.f;
+  }
+  for (int o = 0; o < R0; ++o) {
     const float* cr = C + ((int64_t)o * heads + h) * width;
-    const float* wr = Wv + (int64_t)f * width;
     float acc = 0.f;
-    for (int c = lane; c < width; c += 32) acc = fmaf(wr[c], cr[c], acc);
+#pragma unroll
+    for (int i = 0; i < MAXW; ++i) {
+      const int c = lane + 32 * i;
+      if (c < width) acc = fmaf(wr[i], cr[c], acc);
+    }
     for (int k = 16; k; k >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, k);
     if (lane == 0) out[(int64_t)o * ldo + f] = __fadd_rn(acc, bv[f]);
   }
@@ -451,18 +583,22 @@ __global__ void logits_kernel(const float* __restrict__ prior, const float* __re
     out[o] = __fadd_rn(prior[o], __fmul_rn(__fadd_rn(__fmul_rn(cosine[o], joint_scale), resid[o]), gate));
 }
 
-// out[m, n] = res[m, n] + act(sum_z P[z, m, n] + bias[n]), slices summed in order.
+// out[m, n] = res[m, n] + act(sum_s P[s, b, m, n] + bias[n]) for batch element
+// b = blockIdx.y, slabs summed in order.
 __global__ void splitk_reduce_kernel(const float* __restrict__ P, int splits, int M, int N,
                                      const float* __restrict__ bias, int gelu, const float* res, int64_t ldr,
-                                     float* out, int64_t ldo) {
+                                     float* out, int64_t ldo, SkinnyBatch bs) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)M * N) return;
+  const int b = blockIdx.y, nb = gridDim.y;
   const int m = (int)(i / N), n = (int)(i % N);
-  float v = P[i];
-  for (int z = 1; z < splits; ++z) v = __fadd_rn(v, P[(int64_t)z * M * N + i]);
-  if (bias) v = __fadd_rn(v, bias[n]);
+  const int64_t mn = (int64_t)M * N;
+  float v = P[(int64_t)b * mn + i];
+  for (int z = 1; z < splits; ++z) v = __fadd_rn(v, P[((int64_t)z * nb + b) * mn + i]);
+  if (bias) v = __fadd_rn(v, bias[b * bs.bias + n]);
   if (gelu) v = gelu_erf(v);
-  if (res) v = __fadd_rn(res[(int64_t)m * ldr + n], v);
+  out += b * bs.out;
+  if (res) v = __fadd_rn(res[b * bs.out + (int64_t)m * ldr + n], v);
   out[(int64_t)m * ldo + n] = v;
 }
 
@@ -475,9 +611,43 @@ struct SplitK {
 };
 thread_local SplitK g_split;
 
+// Skinny GEMM over `batch` independent problems (offsets in bs; `res`, when
+// given, shares the output offsets), split along K when the column tiles
+// alone would not fill the GPU.
+int skinny_gemm(const float* X, int64_t ldx, const float* W, int64_t ldw, int M, int N, int K, const float* bias,
+                bool gelu, const float* res, int64_t ldr, float* out, int64_t ldo, int batch, SkinnyBatch bs,
+                cudaStream_t s) {
+  const int64_t tiles = ceil_div(N, 8 * SK_COLS) * (int64_t)batch;
+  int splits = 1, kc = K;
+  if (tiles < 2 * g_split.sms && g_split.part) {
+    int want = (int)std::min<int64_t>(32, ceil_div(2 * g_split.sms, tiles));
+    want = (int)std::min<int64_t>(want, std::max<int64_t>(1, K / 256));
+    want = (int)std::min<int64_t>(want, (int64_t)(g_split.cap / ((size_t)M * N * batch)));
+    if (want > 1) {
+      kc = (int)(ceil_div(ceil_div(K, want), 4) * 4);
+      splits = (int)ceil_div(K, kc);
+    }
+  }
+  const dim3 grid((unsigned)ceil_div(N, 8 * SK_COLS), (unsigned)splits, (unsigned)batch);
+  if (splits == 1) {
+    CLEF_CHECK(!res || batch == 1, CLEF_ERR_INVALID, "head: batched residual");
+    skinny_gemm_kernel<<<grid, 256, 0, s>>>(X, ldx, W, ldw, M, N, K, kc, bs, bias, gelu ? 1 : 0, res, ldr, out,
+                                            ldo);
+    return launch_status("head skinny gemm");
+  }
+  skinny_gemm_kernel<<<grid, 256, 0, s>>>(X, ldx, W, ldw, M, N, K, kc, bs, nullptr, 0, nullptr, 0, g_split.part, N);
+  int rc = launch_status("head skinny gemm");
+  if (rc) return rc;
+  splitk_reduce_kernel<<<dim3((unsigned)ceil_div((int64_t)M * N, 256), (unsigned)batch), 256, 0, s>>>(
+      g_split.part, splits, M, N, bias, gelu ? 1 : 0, res, ldr, out, ldo, bs);
+  return launch_status("head split-k reduce");
+}
+
 int gemm_f32(const float* X, int64_t ldx, const float* W, int64_t ldw, int M, int N, int K, const float* bias,
              bool gelu, const float* res, int64_t ldr, float* out, int64_t ldo, cudaStream_t s, bool w_kn = false) {
   if (M == 0 || N == 0) return CLEF_OK;
+  if (M <= SK_M && !w_kn) return skinny_gemm(X, ldx, W, ldw, M, N, K, bias, gelu, res, ldr, out, ldo, 1,
+                                              SkinnyBatch{0, 0, 0, 0}, s);
   dim3 grid((unsigned)ceil_div(N, SG_N), (unsigned)ceil_div(M, SG_M), 1);
   CLEF_CHECK(grid.y <= 65535u, CLEF_ERR_UNSUPPORTED, "head: too many rows");
   // 16-byte loads when every row start is 16-byte aligned and K (or N for a
@@ -511,7 +681,7 @@ int gemm_f32(const float* X, int64_t ldx, const float* W, int64_t ldw, int M, in
   if (rc || splits == 1) return rc;
   const int64_t n = (int64_t)M * N;
   splitk_reduce_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(g_split.part, splits, M, N, bias, gelu ? 1 : 0, res,
-                                                                  ldr, out, ldo);
+                                                                  ldr, out, ldo, SkinnyBatch{0, 0, 0, 0});
   return launch_status("head split-k reduce");
 }
 
@@ -549,7 +719,8 @@ int cross_attention(const float* q, int R0, const float* mem, int T, const float
                     const float* bv, int width, int heads, float* U, float* S, float* C, float* out, cudaStream_t s) {
   if (R0 == 0) return CLEF_OK;
   const int hd = width / heads, R = R0 * heads;
-  qk_fold_kernel<<<R, 256, 0, s>>>(q, width, Wk, width, heads, hd, U);
+  qk_fold_kernel<<<dim3((unsigned)ceil_div(width, 256), (unsigned)heads, (unsigned)ceil_div(R0, 16)), 256, 0, s>>>(
+      q, width, Wk, width, heads, hd, R0, U);
   int rc = launch_status("head qk_fold");
   if (!rc) rc = gemm_f32(U, width, mem, width, R, T, width, nullptr, false, nullptr, 0, S, T, s);
   if (rc) return rc;
@@ -557,8 +728,12 @@ int cross_attention(const float* q, int R0, const float* mem, int T, const float
   rc = launch_status("head softmax");
   if (!rc) rc = gemm_f32(S, T, mem, width, R, width, T, nullptr, false, nullptr, 0, C, width, s, true);
   if (rc) return rc;
-  v_unfold_kernel<<<dim3((unsigned)R0, (unsigned)std::max(1, std::min(32, width / 8))), 256, 0, s>>>(
-      C, Wv, bv, width, heads, hd, out, width);
+  if (R0 <= SK_M) {
+    // Per head h: out[:, h*hd .. h*hd+hd) = C[(o, h), :] Wv[h*hd .. h*hd+hd, :]^T + bv.
+    return skinny_gemm(C, (int64_t)heads * width, Wv, width, R0, hd, width, bv, false, nullptr, 0, out, width, heads,
+                       SkinnyBatch{width, (int64_t)hd * width, hd, hd}, s);
+  }
+  v_unfold_kernel<<<(unsigned)ceil_div(width, 8), 256, 0, s>>>(C, Wv, bv, width, heads, hd, R0, out, width);
   return launch_status("head v_unfold");
 }
 
@@ -705,8 +880,8 @@ int clef_head_create(const clef_head_config* cfg, int32_t device, clef_head** ou
   CLEF_CHECK(c.hidden_size > 0 && c.width > 0 && c.heads > 0 && c.feedforward > 0 && c.routing_layers >= 0 &&
                  c.layers >= 0 && c.layers <= 64 && c.routing_layers <= 64,
              CLEF_ERR_INVALID, "head_create: dimensions");
-  CLEF_CHECK(c.width % c.heads == 0 && 256 % (c.width / c.heads) == 0, CLEF_ERR_UNSUPPORTED,
-             "head_create: head width (width / heads) must divide 256");
+  CLEF_CHECK(c.width % c.heads == 0 && 256 % (c.width / c.heads) == 0 && c.width <= 2048, CLEF_ERR_UNSUPPORTED,
+             "head_create: width at most 2048 and head width (width / heads) dividing 256");
   int n = 0;
   CLEF_CUDA(cudaGetDeviceCount(&n));
   CLEF_CHECK(device >= 0 && device < n, CLEF_ERR_INVALID, "head_create: device");

@@ -9,8 +9,8 @@
 //     attention respect sequence boundaries through offset tables.
 //   - Projections that read the same input are fused into one weight matrix
 //     whose named views are the checkpoint tensors: in_proj_qkv | in_proj_z |
-//     in_proj_a | in_proj_b (one F32-output GEMM feeding the DeltaNet
-//     prologue) and q_proj | k_proj | v_proj (one BF16-output GEMM).
+//     in_proj_a | in_proj_b (one BF16-output GEMM feeding the DeltaNet
+//     prologue and epilogue) and q_proj | k_proj | v_proj (one BF16-output GEMM).
 //   - Residual adds are fused into the out_proj / o_proj / down_proj GEMM
 //     epilogues; SwiGLU is fused into the gate/up GEMM epilogue.
 //   - The prefix state (PrefixState, qwen.rs:153-190) lives on the device:
@@ -309,7 +309,7 @@ int ensure_capacity(clef_engine* e, int64_t tokens, int64_t seqs) {
   take(sizeof(int32_t) * M);                              // 0 ids
   take(meta_bytes((size_t)seqs + 1));                     // 1 meta
   take(sizeof(float) * M * hid);                          // 2 h
-  take(std::max(sizeof(float) * M * e->n_in, sizeof(uint16_t) * M * e->n_att));  // 3 proj
+  take(sizeof(uint16_t) * M * std::max(e->n_in, e->n_att));  // 3 proj (BF16)
   take(sizeof(float) * M * e->key);                       // 4 dq
   take(sizeof(float) * M * e->key);                       // 5 dk
   take(sizeof(float) * M * e->value);                     // 6 dv
@@ -536,14 +536,17 @@ int run_pack(clef_engine* e, const int32_t* ids, const int64_t* offsets, int s0,
       RC(launch_rmsnorm(e->h, L.in_eff, M, hid, eps, CLEF_BF16, e->u, s));
     }
     if (!L.attention) {
+      // in_proj_qkv | z | a | b output in BF16: the reference's BF16 path rounds
+      // the projection to the model dtype before widening (qwen.rs:603, 619, 626, 669).
+      uint16_t* pin = reinterpret_cast<uint16_t*>(e->proj);
       {
         STAGE(kStGemm);
-        RC(launch_gemm(e->u, L.w_in, nullptr, M, L.n_in, hid, kEpiF32, e->proj, L.n_in, s));
+        RC(launch_gemm(e->u, L.w_in, nullptr, M, L.n_in, hid, kEpiBF16, pin, L.n_in, s));
       }
       const clef_prefix::Layer* il = init ? &init->layers[li] : nullptr;
       {
         STAGE(kStDeltaPro);
-        RC(launch_delta_prologue(e->proj, L.n_in, e->qkv_w + e->value, e->qkv_w + e->value + hv,
+        RC(launch_delta_prologue(pin, L.n_in, e->qkv_w + e->value, e->qkv_w + e->value + hv,
                                  il ? il->hist : nullptr, il ? il->hist_rows : 0, L.conv, L.dt,
                                  L.alog, pack, hk, hv, 128, 128, e->dq, e->dk, e->dv, e->dg, e->db,
                                  s));
@@ -556,12 +559,12 @@ int run_pack(clef_engine* e, const int32_t* ids, const int64_t* offsets, int s0,
       }
       if (cap) {
         auto& cl = cap->layers[li];
-        RC(launch_copy_rows(e->proj, L.n_in, capture - cl.hist_rows, cl.hist_rows, e->qkv_w, 4,
-                            cl.hist, e->qkv_w, s));
+        RC(launch_rows_bf16_to_f32(pin, L.n_in, capture - cl.hist_rows, cl.hist_rows, e->qkv_w, cl.hist,
+                                   e->qkv_w, s));
       }
       {
         STAGE(kStDeltaEpi);
-        RC(launch_delta_epilogue(e->dout, e->proj + e->qkv_w, L.n_in, L.dnorm, eps, M, hv, 128,
+        RC(launch_delta_epilogue(e->dout, pin + e->qkv_w, L.n_in, L.dnorm, eps, M, hv, 128,
                                  e->y, s));
       }
       {

@@ -29,8 +29,13 @@ int launch_delta_prologue(const float* proj, int64_t ldp, int a_col, int b_col, 
                           int hist_rows, const float* conv_w, const float* dt_bias,
                           const float* a_log, const SeqPack& pack, int Hk, int Hv, int dk, int dv,
                           float* q, float* k, float* v, float* g, float* beta, cudaStream_t s);
+// Same with the BF16 projection rows of the engine (history rows stay F32).
+int launch_delta_prologue(const uint16_t* proj, int64_t ldp, int a_col, int b_col, const float* hist,
+                          int hist_rows, const float* conv_w, const float* dt_bias,
+                          const float* a_log, const SeqPack& pack, int Hk, int Hv, int dk, int dv,
+                          float* q, float* k, float* v, float* g, float* beta, cudaStream_t s);
 // y[t, h*dv + i] = bf16(bf16(rms(bf16(o))*w) * silu(bf16(z))) for each v-head.
-int launch_delta_epilogue(const float* o, const float* z, int64_t ldz, const float* w, float eps,
+int launch_delta_epilogue(const float* o, const uint16_t* z, int64_t ldz, const float* w, float eps,
                           int64_t T, int Hv, int dv, uint16_t* y, cudaStream_t s);
 // Attention prologue: q/k RMSNorm (offset weights already +1) and partial
 // RoPE from the fused BF16 projection; positions = offset + index in sequence.
@@ -47,6 +52,9 @@ int launch_head(const float* h, const float* norm_w, float eps, const SeqPack& p
 // into dst [count, ncols].
 int launch_copy_rows(const void* src, int64_t ld, int64_t r0, int64_t count, int64_t ncols,
                      int elem, void* dst, int64_t ldd, cudaStream_t s);
+// dst rows (F32) = widened BF16 rows [r0, r0 + count) of src.
+int launch_rows_bf16_to_f32(const uint16_t* src, int64_t ld, int64_t r0, int64_t count, int64_t ncols, float* dst,
+                            int64_t ldd, cudaStream_t s);
 
 // ---- delta_scan.cu ----------------------------------------------------------
 // Pipelined scan (prep + carry kernels): workspace = offsets tables + the

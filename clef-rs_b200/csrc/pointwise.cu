@@ -8,6 +8,8 @@
 // shared-memory reduction or block barrier sits on the hot path.
 #include <cmath>
 
+#include <type_traits>
+
 #include "kernels.cuh"
 
 namespace clef {
@@ -113,13 +115,43 @@ __global__ void conv4_kernel(const float* __restrict__ x, int64_t ldx, const flo
 // the gates (qwen.rs:619-627).
 constexpr int PRO_RUN = 12;
 constexpr int PRO_ROWS = PRO_RUN + 3;
-constexpr int PRO_SMEM = PRO_ROWS * 256 * 16;
+
+// Staged element of one thread's 4 channels: F32 (16 bytes, the C-ABI
+// operator) or BF16 (8 bytes, the engine's projection output, which the
+// reference rounds to the model dtype before widening, qwen.rs:603).
+template <typename In>
+struct ProIn;
+template <>
+struct ProIn<float> {
+  using V = float4;
+  __device__ static float4 f4(const float4& v) { return v; }
+  __device__ static float f(float x) { return x; }
+};
+template <>
+struct ProIn<uint16_t> {
+  using V = uint2;
+  __device__ static float4 f4(const uint2& v) {
+    return make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u), __uint_as_float(v.y << 16),
+                       __uint_as_float(v.y & 0xffff0000u));
+  }
+  __device__ static float f(uint16_t x) { return __uint_as_float((uint32_t)x << 16); }
+};
+template <typename In>
+constexpr int pro_smem() {
+  return PRO_ROWS * 256 * (int)sizeof(typename ProIn<In>::V);
+}
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
                "l"(src)
                : "memory");
 }
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_row(float4* dst, const float* src) { cp_async16(dst, src); }
+__device__ __forceinline__ void cp_async_row(uint2* dst, const uint16_t* src) { cp_async8(dst, src); }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
@@ -130,8 +162,8 @@ __device__ __forceinline__ void cp_async_wait() {
 // the correctly rounded quotient; e^-x overflowing gives -0 for very negative x).
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 
-template <int I>
-__device__ __forceinline__ void pro_step(const float4* __restrict__ rows, const float* __restrict__ hist,
+template <int I, typename V>
+__device__ __forceinline__ void pro_step(const V* __restrict__ rows, const float* __restrict__ hist,
                                          int hist_rows, int width, const float (&tw)[4][4], int64_t t,
                                          int64_t start, int c, int key, int Hv, float qscale,
                                          float* __restrict__ q, float* __restrict__ k,
@@ -143,7 +175,7 @@ __device__ __forceinline__ void pro_step(const float4* __restrict__ rows, const 
     const int64_t r = t - (3 - tap);
     float4 xv;
     if (r >= start) {
-      xv = rows[(I + tap) * 256];
+      xv = ProIn<std::conditional_t<sizeof(V) == 16, float, uint16_t>>::f4(rows[(I + tap) * 256]);
     } else {
       const int64_t hr = hist_rows + (r - start);
       if (!hist || hr < 0) continue;  // rows before the sequence are zero
@@ -175,7 +207,8 @@ __device__ __forceinline__ void pro_step(const float4* __restrict__ rows, const 
 template <int I>
 struct ProRun {
   // Token t_begin + I, once copy group I + 3 has landed.
-  __device__ __forceinline__ static void run(const float4* rows, const float* hist, int hist_rows,
+  template <typename V>
+  __device__ __forceinline__ static void run(const V* rows, const float* hist, int hist_rows,
                                              int width, const float (&tw)[4][4], int64_t t_begin,
                                              int64_t t_end, int64_t& start, int64_t& next_start,
                                              int& s, const int64_t* cu, int c, int key, int Hv,
@@ -188,36 +221,40 @@ struct ProRun {
       start = t;
       next_start = cu[s + 1];
     }
-    pro_step<I>(rows, hist, hist_rows, width, tw, t, start, c, key, Hv, qscale, q, k, v);
+    pro_step<I, V>(rows, hist, hist_rows, width, tw, t, start, c, key, Hv, qscale, q, k, v);
     ProRun<I + 1>::run(rows, hist, hist_rows, width, tw, t_begin, t_end, start, next_start, s, cu, c,
                        key, Hv, qscale, q, k, v);
   }
 };
 template <>
 struct ProRun<PRO_RUN> {
-  __device__ __forceinline__ static void run(const float4*, const float*, int, int, const float (&)[4][4],
+  template <typename V>
+  __device__ __forceinline__ static void run(const V*, const float*, int, int, const float (&)[4][4],
                                              int64_t, int64_t, int64_t&, int64_t&, int&, const int64_t*,
                                              int, int, int, float, float*, float*, float*) {}
 };
 
+template <typename In>
 __global__ void __launch_bounds__(256, 3) delta_prologue_kernel(
-    const float* __restrict__ proj, int64_t ldp, int a_col, int b_col,
+    const In* __restrict__ proj, int64_t ldp, int a_col, int b_col,
     const float* __restrict__ hist, int hist_rows, const float* __restrict__ conv_w,
     const float* __restrict__ dt_bias, const float* __restrict__ a_log,
     const int64_t* __restrict__ cu, int nseq, int64_t T, int Hk, int Hv, float qscale,
     float* __restrict__ q, float* __restrict__ k, float* __restrict__ v, float* __restrict__ g,
     float* __restrict__ beta) {
-  extern __shared__ float4 pro_sm[];  // [PRO_ROWS][256]
+  using V = typename ProIn<In>::V;
+  extern __shared__ __align__(16) uint8_t pro_raw[];
+  V* pro_sm = reinterpret_cast<V*>(pro_raw);  // [PRO_ROWS][256]
   const int key = Hk * 128;
   const int width = 2 * key + Hv * 128;
   const int c = blockIdx.x * 1024 + threadIdx.x * 4;
   const int64_t t_begin = (int64_t)blockIdx.y * PRO_RUN;
   const int64_t t_end = min(T, t_begin + PRO_RUN);
-  float4* rows = pro_sm + threadIdx.x;
+  V* rows = pro_sm + threadIdx.x;
 #pragma unroll
   for (int i = 0; i < PRO_ROWS; ++i) {
     const int64_t r = t_begin - 3 + i;
-    if (r >= 0 && r < t_end) cp_async16(rows + i * 256, proj + r * ldp + c);
+    if (r >= 0 && r < t_end) cp_async_row(rows + i * 256, proj + r * ldp + c);
     cp_async_commit();
   }
   // Sequence of the first token.
@@ -233,17 +270,17 @@ __global__ void __launch_bounds__(256, 3) delta_prologue_kernel(
                           {w0.y, w1.y, w2.y, w3.y},
                           {w0.z, w1.z, w2.z, w3.z},
                           {w0.w, w1.w, w2.w, w3.w}};
-  ProRun<0>::run(rows, hist, hist_rows, width, tw, t_begin, t_end, start, next_start, s, cu, c, key, Hv,
+  ProRun<0>::run<V>(rows, hist, hist_rows, width, tw, t_begin, t_end, start, next_start, s, cu, c, key, Hv,
                  qscale, q, k, v);
   cp_async_wait<0>();
   if (blockIdx.x == 0) {
     for (int idx = threadIdx.x; idx < (t_end - t_begin) * Hv; idx += blockDim.x) {
       const int64_t t = t_begin + idx / Hv;
       const int h = idx % Hv;
-      const float a = __fadd_rn(proj[t * ldp + a_col + h], dt_bias[h]);
+      const float a = __fadd_rn(ProIn<In>::f(proj[t * ldp + a_col + h]), dt_bias[h]);
       const float sp = __fadd_rn(fmaxf(a, 0.f), logf(__fadd_rn(expf(-fabsf(a)), 1.f)));
       g[t * Hv + h] = __fmul_rn(sp, -expf(a_log[h]));
-      beta[t * Hv + h] = sigmoid_f(proj[t * ldp + b_col + h]);
+      beta[t * Hv + h] = sigmoid_f(ProIn<In>::f(proj[t * ldp + b_col + h]));
     }
   }
 }
@@ -252,7 +289,7 @@ __global__ void __launch_bounds__(256, 3) delta_prologue_kernel(
 // Rounding points follow the reference run in the BF16 projection dtype:
 // o -> P, norm output -> P, z in P, product -> P.
 __global__ void __launch_bounds__(256) delta_epilogue_kernel(const float* __restrict__ o,
-                                                             const float* __restrict__ z, int64_t ldz,
+                                                             const uint16_t* __restrict__ z, int64_t ldz,
                                                              const float* __restrict__ w, float eps,
                                                              int64_t T, int Hv, uint16_t* __restrict__ y) {
   // One warp per token; its Hv rows of 128 go four at a time with all eight
@@ -263,16 +300,18 @@ __global__ void __launch_bounds__(256) delta_epilogue_kernel(const float* __rest
   const float4 wv = *reinterpret_cast<const float4*>(w + lane * 4);
   for (int h0 = 0; h0 < Hv; h0 += 4) {
     float4 a[4], zv[4];
+    uint2 zr[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       if (h0 + u < Hv) {
         a[u] = *reinterpret_cast<const float4*>(o + (t * Hv + h0 + u) * 128 + lane * 4);
-        zv[u] = *reinterpret_cast<const float4*>(z + t * ldz + (h0 + u) * 128 + lane * 4);
+        zr[u] = *reinterpret_cast<const uint2*>(z + t * ldz + (h0 + u) * 128 + lane * 4);
       }
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       if (h0 + u >= Hv) break;
+      zv[u] = ProIn<uint16_t>::f4(zr[u]);
       const float4 b = make_float4(bf16_round(a[u].x), bf16_round(a[u].y), bf16_round(a[u].z),
                                    bf16_round(a[u].w));
       float ss = b.x * b.x + b.y * b.y + b.z * b.z + b.w * b.w;
@@ -438,6 +477,14 @@ __global__ void copy_rows_kernel(const uint8_t* __restrict__ src, int64_t ld_byt
         *reinterpret_cast<const uint32_t*>(src + r * ld_bytes + i);
 }
 
+// dst[r, i] = float(src[r, i]) for BF16 rows (conv history of a capture).
+__global__ void rows_bf16_to_f32_kernel(const uint16_t* __restrict__ src, int64_t ld, int64_t ncols,
+                                        float* __restrict__ dst, int64_t ldd) {
+  const int64_t r = blockIdx.x;
+  for (int64_t i = threadIdx.x; i < ncols; i += blockDim.x)
+    dst[r * ldd + i] = __uint_as_float((uint32_t)src[r * ld + i] << 16);
+}
+
 template <typename T>
 __global__ void compact_copy_kernel(const T* __restrict__ src, int64_t n, int64_t d1, int64_t d2,
                                     int64_t d3, int64_t s0, int64_t s1, int64_t s2, int64_t s3,
@@ -476,13 +523,11 @@ int launch_conv4(const float* x, int64_t ldx, const float* hist, int hist_rows, 
   return launch_status("conv4");
 }
 
-int launch_delta_prologue(const float* proj, int64_t ldp, int a_col, int b_col, const float* hist,
-                          int hist_rows, const float* conv_w, const float* dt_bias,
-                          const float* a_log, const SeqPack& pack, int Hk, int Hv, int dk, int dv,
-                          float* q, float* k, float* v, float* g, float* beta, cudaStream_t s) {
+template <typename In>
+int launch_delta_prologue_t(const In* proj, int64_t ldp, int a_col, int b_col, const float* hist, int hist_rows,
+                            const float* conv_w, const float* dt_bias, const float* a_log, const SeqPack& pack,
+                            int Hk, int Hv, float* q, float* k, float* v, float* g, float* beta, cudaStream_t s) {
   if (pack.total == 0) return CLEF_OK;
-  (void)dk;
-  (void)dv;
   const float qscale = (float)(1.0 / std::sqrt(128.0));
   const int width = 2 * Hk * 128 + Hv * 128;
   const dim3 grid((unsigned)(width / 1024), (unsigned)ceil_div(pack.total, PRO_RUN));
@@ -490,16 +535,37 @@ int launch_delta_prologue(const float* proj, int64_t ldp, int a_col, int b_col, 
   int dev = 0;
   CLEF_CUDA(cudaGetDevice(&dev));
   if (dev >= 0 && dev < 64 && !attr[dev]) {
-    CLEF_CUDA(cudaFuncSetAttribute(delta_prologue_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PRO_SMEM));
+    CLEF_CUDA(cudaFuncSetAttribute(delta_prologue_kernel<In>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   pro_smem<In>()));
     attr[dev] = true;
   }
-  delta_prologue_kernel<<<grid, 256, PRO_SMEM, s>>>(proj, ldp, a_col, b_col, hist, hist_rows, conv_w,
-                                             dt_bias, a_log, pack.cu_seqlens, pack.nseq,
-                                             pack.total, Hk, Hv, qscale, q, k, v, g, beta);
+  delta_prologue_kernel<In><<<grid, 256, pro_smem<In>(), s>>>(proj, ldp, a_col, b_col, hist, hist_rows, conv_w,
+                                                               dt_bias, a_log, pack.cu_seqlens, pack.nseq,
+                                                               pack.total, Hk, Hv, qscale, q, k, v, g, beta);
   return launch_status("delta_prologue");
 }
 
-int launch_delta_epilogue(const float* o, const float* z, int64_t ldz, const float* w, float eps,
+int launch_delta_prologue(const float* proj, int64_t ldp, int a_col, int b_col, const float* hist,
+                          int hist_rows, const float* conv_w, const float* dt_bias,
+                          const float* a_log, const SeqPack& pack, int Hk, int Hv, int dk, int dv,
+                          float* q, float* k, float* v, float* g, float* beta, cudaStream_t s) {
+  (void)dk;
+  (void)dv;
+  return launch_delta_prologue_t(proj, ldp, a_col, b_col, hist, hist_rows, conv_w, dt_bias, a_log, pack, Hk, Hv, q,
+                                 k, v, g, beta, s);
+}
+
+int launch_delta_prologue(const uint16_t* proj, int64_t ldp, int a_col, int b_col, const float* hist,
+                          int hist_rows, const float* conv_w, const float* dt_bias,
+                          const float* a_log, const SeqPack& pack, int Hk, int Hv, int dk, int dv,
+                          float* q, float* k, float* v, float* g, float* beta, cudaStream_t s) {
+  (void)dk;
+  (void)dv;
+  return launch_delta_prologue_t(proj, ldp, a_col, b_col, hist, hist_rows, conv_w, dt_bias, a_log, pack, Hk, Hv, q,
+                                 k, v, g, beta, s);
+}
+
+int launch_delta_epilogue(const float* o, const uint16_t* z, int64_t ldz, const float* w, float eps,
                           int64_t T, int Hv, int dv, uint16_t* y, cudaStream_t s) {
   (void)dv;
   const int64_t rows = T * Hv;
@@ -535,6 +601,13 @@ int launch_head(const float* h, const float* norm_w, float eps, const SeqPack& p
   head_kernel<<<pack.nseq, 256, hidden * sizeof(float), s>>>(h, norm_w, eps, pack.cu_seqlens, hidden,
                                                              head_w, n_out, logits);
   return launch_status("head");
+}
+
+int launch_rows_bf16_to_f32(const uint16_t* src, int64_t ld, int64_t r0, int64_t count, int64_t ncols, float* dst,
+                            int64_t ldd, cudaStream_t s) {
+  if (count == 0) return CLEF_OK;
+  rows_bf16_to_f32_kernel<<<(unsigned)count, 256, 0, s>>>(src + r0 * ld, ld, ncols, dst, ldd);
+  return launch_status("rows_bf16_to_f32");
 }
 
 int launch_copy_rows(const void* src, int64_t ld, int64_t r0, int64_t count, int64_t ncols, int elem,

@@ -1,5 +1,5 @@
 """The learned joint schema head on the GPU (clef_head_*, csrc/head.cu) against
-the reference's pinned fixture and the F32 oracle (oracle/head.py).
+the reference's pinned fixture and the F32 oracle (oracle/joint_head.py).
 
 - the reference's golden head fixture (models/mod.rs:176-235: hidden [20, 16],
   three questions of kinds 0, 1, 2), tolerance 1e-5 + 1e-4|e| as the
@@ -16,7 +16,7 @@ from pathlib import Path
 import numpy as np
 import pytest
 
-from oracle.head import HeadConfig, Question, head_forward, random_head_weights
+from oracle.joint_head import HeadConfig, Question, head_forward, random_head_weights
 
 pytestmark = pytest.mark.gpu
 

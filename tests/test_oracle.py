@@ -154,7 +154,7 @@ def _head_fixture():
     import json
     from pathlib import Path
 
-    from oracle.head import HeadConfig, Question
+    from oracle.joint_head import HeadConfig, Question
     z = np.load(Path(__file__).with_name("golden") / "head_fixture.npz")
     cfg = HeadConfig(**json.loads(bytes(z["config_json"]).decode()))
     w = {k[2:]: z[k] for k in z.files if k.startswith("w:")}
@@ -164,9 +164,9 @@ def _head_fixture():
 
 
 def test_head_oracle_matches_reference_golden():
-    """oracle/head.py against the reference's pinned joint-head fixture
+    """oracle/joint_head.py against the reference's pinned joint-head fixture
     (models/mod.rs:176-235), tolerance 1e-5 + 1e-4|e| (:75-86)."""
-    from oracle.head import head_forward
+    from oracle.joint_head import head_forward
     z, cfg, w, qs = _head_fixture()
     out = head_forward(w, cfg, z["in:hidden"], z["in:output_embeddings"], list(z["ids"]), qs)
     assert len(out) == 3

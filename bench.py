@@ -46,13 +46,15 @@ def parse():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="config4", choices=["config4", "config5"],
+    ap.add_argument("--workload", default="config4", choices=["config4", "config5", "flash"],
                     help="config4: 256 requests U[256,2048] per GPU; config5: one 16384-token "
                          "prefix computed once per GPU, 64 suffixes U[512,4096] sharded over GPUs")
     ap.add_argument("--shard", action="store_true",
                     help="config4 with one fixed batch shared by all ranks (LPT-sharded, "
                          "strong scaling) instead of a batch per rank")
     ap.add_argument("--requests", type=int, default=256)
+    ap.add_argument("--flash-tokens", type=int, default=4096, choices=[256, 1024, 4096],
+                    help="request length of the flash workload (the reference's published lengths)")
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-tokens", type=int, default=256)
@@ -72,7 +74,20 @@ def peaks():
     return PEAKS_FALLBACK, "fallback"
 
 
+# Published reference number for the `flash` workload: Metal mixed F16 prefill
+# of one 4096-token request at the Flash geometry on an Apple M5 Pro, 1101 tok/s
+# (docs/benchmarks/flash-metal-prefill/report.md:41-43 of the reference).
+FLASH_REFERENCE_TOK_S = {4096: 1101.0, 1024: 1248.0, 256: 1151.0}
+
+
 def workload_config(args, n_gpus):
+    if args.workload == "flash":
+        return {"workload": f"flash geometry: 32-layer hybrid backbone (hidden 4096, intermediate 12288) "
+                            f"+ linear schema head, one {args.flash_tokens}-token request per GPU per step",
+                "vocab": 248320, "layers": args.layers, "hidden": 4096, "intermediate": 12288,
+                "parallelism": f"dp{n_gpus} (one request per rank, weights replicated)",
+                "baseline": "reference Metal mixed F16 on Apple M5 Pro (different hardware)",
+                "l2": "not flushed: every step streams ~17 GB of weights, far above the 126 MB L2"}
     if args.workload == "config5":
         return {"workload": "config5: 32-layer hybrid backbone + linear schema head, prefix reuse",
                 "prefix_tokens": 16384, "suffixes_total": 64, "suffix_len": "U[512,4096]",
@@ -451,7 +466,8 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.SUM)
         return float(t.item())
 
-    cfg = benchmark_config(args.layers, 7)
+    from clef_b200.config import flash_config
+    cfg = flash_config(args.layers, 7) if args.workload == "flash" else benchmark_config(args.layers, 7)
     eng = cb.Engine(cfg, local)
     eng.init_random(3, 0.02)
     eng.finalize()
@@ -464,6 +480,9 @@ def main():
         t0 = time.perf_counter()
         _, _, prefix = eng.prefill([pre_ids], capture=len(pre_ids), logits=False)
         prefix_ms = 1000 * (time.perf_counter() - t0)
+    elif args.workload == "flash":
+        rng = np.random.default_rng(4096 + rank)
+        reqs = [rng.integers(0, cfg.vocab_size, args.flash_tokens).astype(np.int32)]
     elif args.shard:
         batch = workloads.backbone_requests(n=args.requests, seed=3)
         reqs = rank_shard(batch, rank, world, lambda r: flops_per_request(cfg, len(r)))
@@ -546,7 +565,9 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 3),
             "higher_is_better": True,
             "scaling": "strong" if (args.shard or args.workload == "config5") else "weak",
-            "vs_baseline": None, "dtype": "bf16",
+            "vs_baseline": (round(value / FLASH_REFERENCE_TOK_S[args.flash_tokens], 1)
+                            if args.workload == "flash" else None),
+            "dtype": "bf16",
             "data": "synthetic (seeded ids and random-init weights)",
             "decisions_per_s": round(total_reqs / (ms_max / 1000.0), 2),
             "model_tflops": round(allsum(total_flops) / (ms_max / 1000.0) / 1e12, 1),

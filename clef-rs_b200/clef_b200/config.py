@@ -83,6 +83,17 @@ def benchmark_config(layers: int = 32, head_outputs: int = 7) -> ClefConfig:
     return cfg
 
 
+def flash_config(layers: int = 32, head_outputs: int = 7) -> ClefConfig:
+    """The released Flash geometry the reference's published numbers are
+    quoted on (crates/core/fixtures/release/flash-config.json): hidden 4096,
+    intermediate 12288, otherwise as benchmark_config (16/4 x 256 attention,
+    16/32 x 128 DeltaNet, RoPE 1e7 on 64 of 256 features, eps 1e-6)."""
+    cfg = benchmark_config(layers, head_outputs)
+    cfg.hidden_size = 4096
+    cfg.intermediate_size = 12288
+    return cfg
+
+
 def layer_prefix(i: int) -> str:
     return f"model.language_model.layers.{i}"
 

@@ -714,15 +714,20 @@ __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_grou
 __device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void fetch_stage(uint32_t dst, const uint8_t* kq, const uint8_t* tp,
-                                            int tid) {
-  for (int o = tid * 16; o < KQ_IMG; o += THREADS * 16) cp_async16(dst + o, kq + o);
-  for (int o = tid * 16; o < TP_IMG; o += THREADS * 16) cp_async16(dst + KQ_IMG + o, tp + o);
+                                            int tid, int nthreads) {
+  for (int o = tid * 16; o < KQ_IMG; o += nthreads * 16) cp_async16(dst + o, kq + o);
+  for (int o = tid * 16; o < TP_IMG; o += nthreads * 16) cp_async16(dst + KQ_IMG + o, tp + o);
 }
 
+// The value rows of the state never mix (every product is row by row in dv),
+// so a (sequence, value head) may be split over gridDim.y CTAs of
+// 256 / gridDim.y threads, each carrying its own 16-row blocks of S^T: a
+// single long sequence then runs on up to 4x more SMs.
 __global__ void __launch_bounds__(THREADS, 1) delta_carry_kernel(PipeArgs p) {
   extern __shared__ __align__(128) uint8_t sm[];
   const ScanArgs& a = p.a;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int warp = (int)blockIdx.y * (blockDim.x >> 5) + (tid >> 5);  // 16-row block of S^T
   const int h = blockIdx.x % a.Hv;
   const int s = blockIdx.x / a.Hv;
   const int kh = h / (a.Hv / a.Hk);
@@ -733,7 +738,7 @@ __global__ void __launch_bounds__(THREADS, 1) delta_carry_kernel(PipeArgs p) {
 
   float S[16][4];
   load_state(S, init_for(a, s, h), warp, lane);
-  fetch_stage(sbase, kq_of(sq.chunk0), tp_of(sq.chunk0), tid);
+  fetch_stage(sbase, kq_of(sq.chunk0), tp_of(sq.chunk0), tid, blockDim.x);
   cp_commit();
   int64_t done = 0;  // tokens of this sequence before the current chunk
   for (int ci = 0; ci < sq.nchunks; ++ci) {
@@ -745,7 +750,7 @@ __global__ void __launch_bounds__(THREADS, 1) delta_carry_kernel(PipeArgs p) {
     __syncthreads();  // stage ci is in; every warp finished chunk ci - 1
     if (ci + 1 < sq.nchunks) {
       const uint32_t nxt = sbase + ((ci + 1) & 1) * STAGE;
-      fetch_stage(nxt, kq_of(gc + 1), tp_of(gc + 1), tid);
+      fetch_stage(nxt, kq_of(gc + 1), tp_of(gc + 1), tid, blockDim.x);
       cp_commit();
     }
     const uint32_t cur = sbase + (ci & 1) * STAGE;
@@ -868,7 +873,12 @@ int launch_delta_scan_planned(const ScanPlan& plan, const float* q, const float*
   p.tp_img = reinterpret_cast<uint8_t*>(base + l.tp_off);
   delta_prep_kernel<<<dim3((unsigned)plan.nchunks, (unsigned)plan.Hk), THREADS, PREP_SMEM, s>>>(p);
   RC_(launch_status("delta_prep"));
-  delta_carry_kernel<<<(unsigned)(plan.nseq * plan.Hv), THREADS, CARRY_SMEM, s>>>(p);
+  // Few (sequence, head) pairs: split their value rows over 2 or 4 CTAs.
+  int dev = 0;
+  CLEF_CUDA(cudaGetDevice(&dev));
+  const int64_t pairs = (int64_t)plan.nseq * plan.Hv;
+  const int split = pairs * 2 <= num_sms(dev) ? 4 : (pairs <= num_sms(dev) ? 2 : 1);
+  delta_carry_kernel<<<dim3((unsigned)pairs, (unsigned)split), THREADS / split, CARRY_SMEM, s>>>(p);
   return launch_status("delta_carry");
 }
 

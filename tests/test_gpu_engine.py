@@ -166,3 +166,50 @@ def test_every_tensor_initialised_on_a_large_model():
     w = eng.get_weight("clef.head.weight").reshape(7, cfg.hidden_size)
     assert np.abs(lg[0] - w @ hid[-1]).max() <= 1e-4
     eng.close()
+
+
+def test_flash_geometry_block_group_matches_oracle():
+    """The released Flash geometry (hidden 4096, intermediate 12288; the dims of
+    crates/core/fixtures/release/flash-config.json) through one block group on
+    four records packed together. The released weights themselves are absent
+    here; this checks that the engine and its kernels handle the geometry the
+    reference's published numbers are quoted on.
+
+    Gated: hidden relative RMS <= 2e-2 per record (as for the benchmark
+    geometry) and the choice winner wherever the oracle's top-two probability
+    gap exceeds 2e-2 (twice the BF16 maximum error, the reference's winner rule,
+    specs/clef-serving-design.md:629). The reference's probability gates
+    (max 1e-2, mean 2e-3) are defined against its matching BF16 profile over
+    at least 100 records, which this F32 oracle on random weights is not; the
+    probability errors are reported."""
+    import clef_b200 as cb
+    from clef_b200.config import flash_config
+    cfg = flash_config(layers=4, head_outputs=7)
+    cfg.vocab_size = 4096
+    eng = cb.Engine(cfg, 0)
+    eng.init_random(5, 0.02)
+    eng.finalize()
+    ref = oracle.Model(cfg)
+    for name in ref.names():
+        ref.set_weight(name, eng.get_weight(name))
+    ref.check()
+    head_w = eng.get_weight("clef.head.weight").reshape(7, cfg.hidden_size)
+    seqs = [ids(n, 7 + n) for n in (200, 64, 131, 90)]
+    lg, hid, _ = eng.prefill(seqs, hidden=True)
+    eng.close()
+    off = np.cumsum([0] + [len(q) for q in seqs])
+    worst = 0.0
+    for i, q in enumerate(seqs):
+        rh, _ = ref.prefill(q)
+        h = hid[off[i]:off[i + 1]]
+        rel = np.sqrt(((h - rh) ** 2).mean() / (rh ** 2).mean())
+        p_eng, p_ref = probs(lg[i]), probs(oracle.head(rh[-1], head_w)[None])
+        pe = np.abs(p_eng - p_ref)
+        worst = max(worst, float(pe.max()))
+        top = np.sort(p_ref[0, 2:6])[::-1]
+        print(f"flash geometry record {i}: hidden rel-rms {rel:.3e} prob max {pe.max():.3e} "
+              f"mean {pe.mean():.3e} choice gap {top[0] - top[1]:.3e}")
+        assert np.isfinite(h).all() and rel <= 2e-2
+        if top[0] - top[1] > 2e-2:
+            assert np.argmax(p_eng[0, 2:6]) == np.argmax(p_ref[0, 2:6])
+    print(f"flash geometry: worst probability error {worst:.3e}")

@@ -213,3 +213,32 @@ def test_flash_geometry_block_group_matches_oracle():
         if top[0] - top[1] > 2e-2:
             assert np.argmax(p_eng[0, 2:6]) == np.argmax(p_ref[0, 2:6])
     print(f"flash geometry: worst probability error {worst:.3e}")
+
+
+def test_config3_block_group_full_size_matches_oracle():
+    """BASELINE config 3 at its stated size: one random-init block group
+    (3 DeltaNet + 1 attention layer, benchmark dims), a single 4096-token
+    sequence with ids uniform over the full 248320-token vocabulary, weights
+    N(0, 0.02) drawn by the engine with seed 2, against the F32 oracle on the
+    same weights. Same gates as the 300-token block-group test."""
+    import clef_b200 as cb
+    cfg = benchmark_config(layers=4, head_outputs=7)
+    eng = cb.Engine(cfg, 0)
+    eng.init_random(2, 0.02)
+    eng.finalize()
+    ref = oracle.Model(cfg)
+    for name in ref.names():
+        ref.set_weight(name, eng.get_weight(name))
+    ref.check()
+    seq = np.random.default_rng(2).integers(0, cfg.vocab_size, 4096).astype(np.int32)
+    lg, hid, _ = eng.prefill([seq], hidden=True)
+    head_w = eng.get_weight("clef.head.weight").reshape(7, cfg.hidden_size)
+    eng.close()
+    rh, _ = ref.prefill(seq)
+    rl = oracle.head(rh[-1], head_w)
+    rel = np.sqrt(((hid - rh) ** 2).mean() / (rh ** 2).mean())
+    pe = np.abs(probs(lg) - probs(rl[None]))
+    print(f"config3 T=4096: hidden rel-rms {rel:.3e} max-abs {np.abs(hid - rh).max():.3e} "
+          f"logits max-abs {np.abs(lg[0] - rl).max():.3e} prob max {pe.max():.3e}")
+    assert np.isfinite(hid).all() and rel <= 2e-2
+    assert pe.max() <= 1e-2

@@ -167,26 +167,41 @@ __device__ __forceinline__ void put32(uint8_t* base, uint32_t o, uint32_t v) {
 __device__ __forceinline__ void stage_kq(const float* __restrict__ q, const float* __restrict__ k,
                                          int64_t t0, int n, int Hk, int kh, uint8_t* sm_kq,
                                          uint8_t* img, int tid, int nthreads) {
-  for (int idx = tid; idx < C * (DK / 4); idx += nthreads) {
-    const int i = idx >> 5, c4 = (idx & 31) * 4;
-    float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), qv = kv;
-    if (i < n) {
-      const int64_t off = ((t0 + i) * Hk + kh) * DK + c4;
-      kv = *reinterpret_cast<const float4*>(k + off);
-      qv = *reinterpret_cast<const float4*>(q + off);
-    }
-    uint32_t kh0, kl0, kh1, kl1, qh0, ql0, qh1, ql1;
-    split2(kv.x, kv.y, kh0, kl0);
-    split2(kv.z, kv.w, kh1, kl1);
-    split2(qv.x, qv.y, qh0, ql0);
-    split2(qv.z, qv.w, qh1, ql1);
-    const uint32_t o = swz(i, c4, 16);
-    const uint2 w[4] = {make_uint2(kh0, kh1), make_uint2(kl0, kl1), make_uint2(qh0, qh1),
-                        make_uint2(ql0, ql1)};
+  // Four rows' loads are issued before any is used, so a thread has eight
+  // 16-byte loads in flight instead of two.
+  constexpr int U = 4;
+  for (int base = tid; base < C * (DK / 4); base += U * nthreads) {
+    float4 kv[U], qv[U];
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      *reinterpret_cast<uint2*>(sm_kq + t * KQ_BYTES + o) = w[t];
-      if (img) *reinterpret_cast<uint2*>(img + t * KQ_BYTES + o) = w[t];
+    for (int u = 0; u < U; ++u) {
+      const int idx = base + u * nthreads;
+      const int i = idx >> 5, c4 = (idx & 31) * 4;
+      kv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      qv[u] = kv[u];
+      if (idx < C * (DK / 4) && i < n) {
+        const int64_t off = ((t0 + i) * Hk + kh) * DK + c4;
+        kv[u] = *reinterpret_cast<const float4*>(k + off);
+        qv[u] = *reinterpret_cast<const float4*>(q + off);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int idx = base + u * nthreads;
+      if (idx >= C * (DK / 4)) break;
+      const int i = idx >> 5, c4 = (idx & 31) * 4;
+      uint32_t kh0, kl0, kh1, kl1, qh0, ql0, qh1, ql1;
+      split2(kv[u].x, kv[u].y, kh0, kl0);
+      split2(kv[u].z, kv[u].w, kh1, kl1);
+      split2(qv[u].x, qv[u].y, qh0, ql0);
+      split2(qv[u].z, qv[u].w, qh1, ql1);
+      const uint32_t o = swz(i, c4, 16);
+      const uint2 w[4] = {make_uint2(kh0, kh1), make_uint2(kl0, kl1), make_uint2(qh0, qh1),
+                          make_uint2(ql0, ql1)};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        *reinterpret_cast<uint2*>(sm_kq + t * KQ_BYTES + o) = w[t];
+        if (img) *reinterpret_cast<uint2*>(img + t * KQ_BYTES + o) = w[t];
+      }
     }
   }
 }
@@ -656,9 +671,10 @@ constexpr int P_OFF_KQ = 0;
 constexpr int P_OFF_A = KQ_IMG;
 constexpr int P_OFF_T = P_OFF_A + C * AP * 4;
 constexpr int P_OFF_M = P_OFF_T + C * AP * 4;
+constexpr int PREP_MAX_REP = 4;  // value heads per key head whose gates are staged at once
 constexpr int P_OFF_G = P_OFF_M + 3 * 16 * 17 * 4;
-constexpr int P_OFF_B = P_OFF_G + C * 8;
-constexpr int PREP_SMEM = P_OFF_B + C * 4;
+constexpr int P_OFF_B = P_OFF_G + PREP_MAX_REP * C * 8;
+constexpr int PREP_SMEM = P_OFF_B + PREP_MAX_REP * C * 4;
 
 struct PipeArgs {
   ScanArgs a;
@@ -679,18 +695,29 @@ __global__ void __launch_bounds__(THREADS, 2) delta_prep_kernel(PipeArgs p) {
   float* As = reinterpret_cast<float*>(sm + P_OFF_A);
   float* Ts = reinterpret_cast<float*>(sm + P_OFF_T);
   float* Ms = reinterpret_cast<float*>(sm + P_OFF_M);
-  double* Gs = reinterpret_cast<double*>(sm + P_OFF_G);
-  float* bs = reinterpret_cast<float*>(sm + P_OFF_B);
+  double* Gs0 = reinterpret_cast<double*>(sm + P_OFF_G);
+  float* bs0 = reinterpret_cast<float*>(sm + P_OFF_B);
+  double* Gs = Gs0;
+  float* bs = bs0;
   uint8_t* kq = p.kq_img + (gc * a.Hk + kh) * (int64_t)KQ_IMG;
+  const int rep = a.Hv / a.Hk;
+  // The gates of up to PREP_MAX_REP value heads are summed by one warp each
+  // while the other warps stage K and Q.
+  const int staged = rep <= PREP_MAX_REP ? rep : 0;
+  if (warp >= 8 - staged) {
+    const int r = warp - (8 - staged);
+    cumsum_gates(a.g, a.beta, ch.t0, ch.n, a.Hv, kh * rep + r, lane, Gs + r * C, bs + r * C);
+  }
   stage_kq(a.q, a.k, ch.t0, ch.n, a.Hk, kh, sm + P_OFF_KQ, kq, tid, THREADS);
   __syncthreads();
   float kk[4][4], qk[4][4];
   gram_mma(sbase + P_OFF_KQ, warp, lane, kk, qk);
-  const int rep = a.Hv / a.Hk;
   for (int r = 0; r < rep; ++r) {
     const int h = kh * rep + r;
     uint8_t* tp = p.tp_img + (gc * a.Hv + h) * (int64_t)TP_IMG;
-    if (warp == 0) cumsum_gates(a.g, a.beta, ch.t0, ch.n, a.Hv, h, lane, Gs, bs);
+    double* Gs = Gs0 + (staged ? r * C : 0);
+    float* bs = bs0 + (staged ? r * C : 0);
+    if (!staged && warp == 0) cumsum_gates(a.g, a.beta, ch.t0, ch.n, a.Hv, h, lane, Gs, bs);
     __syncthreads();
     const double Glast = Gs[C - 1];
     if (tid < C) {

@@ -21,11 +21,12 @@ int fail(int code, const std::string& msg) {
 int device_errors(int* code) {
   *code = 0;
   CLEF_CUDA(cudaDeviceSynchronize());
-  int v = 0, w = 0;
+  int v = 0, w = 0, x = 0;
   int rc = gemm_device_error(&v);
   if (!rc) rc = attention_tc_device_error(&w);
+  if (!rc) rc = scan_device_error(&x);
   if (rc) return fail(rc, "device error flag read failed");
-  *code = v ? v : w;
+  *code = v ? v : (w ? w : x);
   return CLEF_OK;
 }
 

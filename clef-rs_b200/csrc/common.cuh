@@ -70,6 +70,7 @@ static inline int read_device_error(int* code) {
 int device_errors(int* code);
 int gemm_device_error(int* code);
 int attention_tc_device_error(int* code);
+int scan_device_error(int* code);
 
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;

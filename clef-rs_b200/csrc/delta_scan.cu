@@ -35,6 +35,7 @@
 #include <vector>
 
 #include "kernels.cuh"
+#include "sm100.cuh"
 
 #define RC_(x)           \
   do {                   \
@@ -64,7 +65,7 @@ constexpr int OFF_THI = OFF_QLO + KQ_BYTES;
 constexpr int OFF_TLO = OFF_THI + SQ_BYTES;
 constexpr int OFF_PHI = OFF_TLO + SQ_BYTES;
 constexpr int OFF_PLO = OFF_PHI + SQ_BYTES;
-constexpr int AP = 72;                               // F32 pitch of A and T (8-byte pairs spread over all banks)
+constexpr int AP = 68;                               // F32 pitch of A and T (16-byte row stores spread over all banks)
 constexpr int OFF_A = OFF_PLO + SQ_BYTES;            // F32 [64][65]
 constexpr int OFF_T = OFF_A + C * AP * 4;            // F32 [64][65]
 constexpr int OFF_M = OFF_T + C * AP * 4;            // F32 [3][16][17] scratch
@@ -80,6 +81,15 @@ constexpr int SMEM = OFF_ECAP + C * 4 + 16;
 // eight rows an ldmatrix phase reads hit distinct banks.
 __device__ __forceinline__ uint32_t swz(int row, int col, int cpr) {
   return (uint32_t)(row * cpr * 16 + ((((col >> 3) ^ (row & 7))) << 4) + ((col & 7) << 1));
+}
+
+// Byte offset of element (row, k) of the prep kernel's tcgen05 Gram operand:
+// the canonical K-major layout with the 128-byte swizzle, rows 0..63 = K and
+// 64..127 = Q of the chunk, two 64-wide atoms along dk of [128 rows x 128 B]
+// each (16-byte chunk index XOR row & 7 inside 1024-byte row groups).
+constexpr int GRAM_TILE = 2 * 128 * 128;  // bytes of one (hi or lo) [128 x 128] BF16 operand
+__device__ __forceinline__ uint32_t umma_off(int row, int k) {
+  return (uint32_t)((k >> 6) * (128 * 128) + row * 128 + ((((k & 63) >> 3) ^ (row & 7)) << 4) + ((k & 7) << 1));
 }
 
 __device__ __forceinline__ void split(float x, __nv_bfloat16& hi, __nv_bfloat16& lo) {
@@ -166,7 +176,7 @@ __device__ __forceinline__ void put32(uint8_t* base, uint32_t o, uint32_t v) {
 // and, when `img` is set, the same bytes to a global tile image.
 __device__ __forceinline__ void stage_kq(const float* __restrict__ q, const float* __restrict__ k,
                                          int64_t t0, int n, int Hk, int kh, uint8_t* sm_kq,
-                                         uint8_t* img, int tid, int nthreads) {
+                                         uint8_t* img, int tid, int nthreads, bool umma_smem = false) {
   // Four rows' loads are issued before any is used, so a thread has eight
   // 16-byte loads in flight instead of two.
   constexpr int U = 4;
@@ -197,9 +207,16 @@ __device__ __forceinline__ void stage_kq(const float* __restrict__ q, const floa
       const uint32_t o = swz(i, c4, 16);
       const uint2 w[4] = {make_uint2(kh0, kh1), make_uint2(kl0, kl1), make_uint2(qh0, qh1),
                           make_uint2(ql0, ql1)};
+      if (umma_smem) {
+        // [K; Q] rows of the tcgen05 operand: hi tile, then lo tile.
+        *reinterpret_cast<uint2*>(sm_kq + umma_off(i, c4)) = w[0];
+        *reinterpret_cast<uint2*>(sm_kq + GRAM_TILE + umma_off(i, c4)) = w[1];
+        *reinterpret_cast<uint2*>(sm_kq + umma_off(64 + i, c4)) = w[2];
+        *reinterpret_cast<uint2*>(sm_kq + GRAM_TILE + umma_off(64 + i, c4)) = w[3];
+      }
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
-        *reinterpret_cast<uint2*>(sm_kq + t * KQ_BYTES + o) = w[t];
+        if (!umma_smem) *reinterpret_cast<uint2*>(sm_kq + t * KQ_BYTES + o) = w[t];
         if (img) *reinterpret_cast<uint2*>(img + t * KQ_BYTES + o) = w[t];
       }
     }
@@ -252,6 +269,71 @@ __device__ __forceinline__ void gram_mma(uint32_t kq_base, int warp, int lane, f
       mma3(kk[2 * np + 1], akh, akl, bh[2], bh[3], bl[2], bl[3]);
       mma3(qk[2 * np], aqh, aql, bh[0], bh[1], bl[0], bl[1]);
       mma3(qk[2 * np + 1], aqh, aql, bh[2], bh[3], bl[2], bl[3]);
+    }
+  }
+}
+
+// [K; Q] K^T (128 x 64, F32 in TMEM columns [tmem, tmem + 64)) on the tcgen05
+// tensor core from the split-BF16 operand at `a_base` (umma_off layout):
+// hi*hi + hi*lo + lo*hi, eight 16-wide K steps each. The B operand is rows
+// 0..63 of the same tile (K). One thread issues; completion arrives on `bar`.
+__device__ __forceinline__ void gram_tc_issue(uint32_t a_base, uint32_t tmem, uint64_t* bar) {
+  constexpr uint32_t idesc = sm100::idesc_bf16_f32(128, 64);
+  const uint32_t hi = a_base, lo = a_base + GRAM_TILE;
+  uint32_t acc = 0;
+#pragma unroll
+  for (int term = 0; term < 3; ++term) {
+    const uint32_t A = term == 2 ? lo : hi;
+    const uint32_t B = term == 1 ? lo : hi;
+#pragma unroll
+    for (int kk = 0; kk < DK / 16; ++kk) {
+      const uint32_t off = (uint32_t)((kk >> 2) * (128 * 128) + (kk & 3) * 32);
+      sm100::umma_f16(tmem, sm100::desc_k_sw128(A + off), sm100::desc_k_sw128(B + off), idesc, acc);
+      acc = 1;
+    }
+  }
+  sm100::umma_commit(bar);
+}
+
+// Row-per-thread form of gram_store for the tcgen05 Gram: `g` holds columns
+// [32 half, 32 half + 32) of row `row` of [K K^T; Q K^T]. Rows < 64 give A
+// (F32, strictly lower, beta_i e^{G_i-G_j} k_i.k_j) into As; rows >= 64 give
+// P (lower incl. diagonal, e^{G_i-G_j} q_i.k_j) as hi/lo tiles at p_hi / p_lo.
+template <bool GLOBAL>
+__device__ __forceinline__ void gram_store_rows(const uint32_t (&g)[32], int row, int half, int n,
+                                                const double* Gs, const float* bs, float* As, uint8_t* p_hi,
+                                                uint8_t* p_lo) {
+  const int i = row & 63, c0 = half * 32;
+  const double gi = Gs[i];
+  if (row < 64) {
+    const float bi = bs[i];
+#pragma unroll
+    for (int c = 0; c < 32; c += 4) {
+      float av[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int col = c0 + c + u;
+        const bool lower = col < i && i < n;
+        const float decay = lower ? expf((float)(gi - Gs[col])) : 0.f;
+        av[u] = lower ? bi * (decay * __uint_as_float(g[c + u])) : 0.f;
+      }
+      *reinterpret_cast<float4*>(As + i * AP + c0 + c) = make_float4(av[0], av[1], av[2], av[3]);
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < 32; c += 2) {
+      float pv[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int col = c0 + c + u;
+        const bool lower = col <= i && i < n;
+        pv[u] = lower ? expf((float)(gi - Gs[col])) * __uint_as_float(g[c + u]) : 0.f;
+      }
+      uint32_t ph, pl;
+      split2(pv[0], pv[1], ph, pl);
+      const uint32_t o = swz(i, c0 + c, 8);
+      put32<GLOBAL>(p_hi, o, ph);
+      put32<GLOBAL>(p_lo, o, pl);
     }
   }
 }
@@ -674,7 +756,8 @@ constexpr int P_OFF_M = P_OFF_T + C * AP * 4;
 constexpr int PREP_MAX_REP = 4;  // value heads per key head whose gates are staged at once
 constexpr int P_OFF_G = P_OFF_M + 3 * 16 * 17 * 4;
 constexpr int P_OFF_B = P_OFF_G + PREP_MAX_REP * C * 8;
-constexpr int PREP_SMEM = P_OFF_B + PREP_MAX_REP * C * 4;
+constexpr int P_OFF_BAR = P_OFF_B + PREP_MAX_REP * C * 4;  // mbarrier + TMEM address
+constexpr int PREP_SMEM = 1024 + P_OFF_BAR + 16;  // 1024: alignment of the swizzled operand
 
 struct PipeArgs {
   ScanArgs a;
@@ -685,13 +768,24 @@ struct PipeArgs {
 };
 
 __global__ void __launch_bounds__(THREADS, 2) delta_prep_kernel(PipeArgs p) {
-  extern __shared__ __align__(128) uint8_t sm[];
+  extern __shared__ __align__(128) uint8_t sm_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>(((uintptr_t)sm_raw + 1023) & ~(uintptr_t)1023);
   const ScanArgs& a = p.a;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int kh = blockIdx.y;
   const int64_t gc = blockIdx.x;
   const ScanChunk ch = p.chunks[gc];
   const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(sm);
+  uint64_t* gram_bar = reinterpret_cast<uint64_t*>(sm + P_OFF_BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + P_OFF_BAR + 8);
+  if (tid == 0) {
+    sm100::mbar_init(gram_bar, 1);
+    sm100::fence_barrier_init();
+  }
+  if (warp == 0) {
+    sm100::tmem_alloc(tmem_slot, 64);  // the 128 x 64 F32 Gram accumulator
+    sm100::tmem_relinquish();
+  }
   float* As = reinterpret_cast<float*>(sm + P_OFF_A);
   float* Ts = reinterpret_cast<float*>(sm + P_OFF_T);
   float* Ms = reinterpret_cast<float*>(sm + P_OFF_M);
@@ -708,10 +802,28 @@ __global__ void __launch_bounds__(THREADS, 2) delta_prep_kernel(PipeArgs p) {
     const int r = warp - (8 - staged);
     cumsum_gates(a.g, a.beta, ch.t0, ch.n, a.Hv, kh * rep + r, lane, Gs + r * C, bs + r * C);
   }
-  stage_kq(a.q, a.k, ch.t0, ch.n, a.Hk, kh, sm + P_OFF_KQ, kq, tid, THREADS);
+  stage_kq(a.q, a.k, ch.t0, ch.n, a.Hk, kh, sm + P_OFF_KQ, kq, tid, THREADS, true);
+  // The operand written by st.shared is read by the tensor core (async proxy).
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  sm100::tc_fence_before();
   __syncthreads();
-  float kk[4][4], qk[4][4];
-  gram_mma(sbase + P_OFF_KQ, warp, lane, kk, qk);
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (tid == 0) gram_tc_issue(sbase + P_OFF_KQ, tmem, gram_bar);
+  // Warp w reads TMEM lanes 32 (w % 4) .. (rows of [K K^T; Q K^T]) and columns
+  // 32 (w / 4) .. of the Gram; the wait ends warp-uniformly.
+  const int grow = (warp & 3) * 32 + lane, ghalf = warp >> 2;
+  uint32_t gr[32];
+  const bool gram_ok = __all_sync(0xffffffffu, sm100::mbar_wait(gram_bar, 0));
+  if (gram_ok) {
+    sm100::tc_fence_after();
+    sm100::tmem_ld_32x32b_x32(tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(ghalf * 32), gr);
+    sm100::tmem_ld_wait();
+  } else {
+    if (lane == 0) raise_device_error(kDevScanTimeout);
+#pragma unroll
+    for (int c = 0; c < 32; ++c) gr[c] = 0u;
+  }
   for (int r = 0; r < rep; ++r) {
     const int h = kh * rep + r;
     uint8_t* tp = p.tp_img + (gc * a.Hv + h) * (int64_t)TP_IMG;
@@ -727,12 +839,29 @@ __global__ void __launch_bounds__(THREADS, 2) delta_prep_kernel(PipeArgs p) {
       vec[128 + tid] = tid == 0 ? expf((float)Glast) : 0.f;  // el
       reinterpret_cast<double*>(vec + 192)[tid] = Gs[tid];   // G
     }
-    gram_store<true>(kk, qk, warp, lane, ch.n, Gs, bs, As, tp + 2 * SQ_BYTES, tp + 3 * SQ_BYTES);
+    // P goes through shared memory (the Gram operand's space, free once the
+    // MMAs have completed) so that its image is written with coalesced stores.
+    uint8_t* pst = sm + P_OFF_KQ;
+    gram_store_rows<false>(gr, grow, ghalf, ch.n, Gs, bs, As, pst, pst + SQ_BYTES);
     __syncthreads();
+    for (int o = tid * 16; o < 2 * SQ_BYTES; o += THREADS * 16)
+      *reinterpret_cast<uint4*>(tp + 2 * SQ_BYTES + o) = *reinterpret_cast<const uint4*>(pst + o);
     solve_t<true>(As, Ts, Ms, bs, tp + 0 * SQ_BYTES, tp + 1 * SQ_BYTES, tid, warp, lane, THREADS);
     __syncthreads();  // Gs, bs, As, Ts are reused by the next v-head
   }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, 64);
+  }
 }
+
+}  // namespace
+
+int scan_device_error(int* code) { return read_device_error(code); }
+
+namespace {
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src));

@@ -4,9 +4,12 @@ clef_delta_scan_noalloc serves callers that cannot allocate device memory or
 pass a workspace (an allocator that owns all device memory behind a fixed op
 signature, or a latency-critical loop that must avoid cudaMalloc's implicit
 synchronisation): the per-sequence offsets live in a fixed device array inside
-the library instead. Both entry points run the same kernel, so the outputs are
-compared bit for bit, on two calls in a row with different packings (the
-second call must not see the first call's offsets).
+the library instead. The allocation-free entry runs the fused single-pass scan
+kernel, the workspace entry the two-kernel pipeline whose intra-chunk Gram
+products run on the tcgen05 tensor core; the outputs therefore agree to F32
+summation-order noise: max-abs 1e-5 on the outputs and 1e-4 on the final states
+(the scan's tolerance against the oracle is 1e-3). Checked on two calls in a row
+with different packings (the second call must not see the first call's offsets).
 
 This file is collected last on purpose; it needs nothing from the others and
 also passes alone in a fresh process.
@@ -25,6 +28,10 @@ torch = pytest.importorskip("torch")
 
 def _p(t):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def close(a, b, tol):
+    return bool(np.isfinite(a).all()) and float(np.abs(a - b).max()) <= tol
 
 
 def scan_both(inp, cu, final=True):
@@ -58,20 +65,19 @@ def scan_both(inp, cu, final=True):
 def test_noalloc_scan_matches_workspace_scan_on_two_calls_in_a_row():
     first = workloads.delta_operator_inputs(T=700, seed=21)
     (o_ws, f_ws), (o_na, f_na) = scan_both(first, [0, 1, 65, 200, 700])
-    assert np.isfinite(o_na).all()
-    assert np.array_equal(o_na, o_ws) and np.array_equal(f_na, f_ws)
+    assert close(o_na, o_ws, 1e-5) and close(f_na, f_ws, 1e-4)
     # Second call, different packing and more sequences: the shared array is
     # rewritten for every entry the kernel reads.
     second = workloads.delta_operator_inputs(T=1000, seed=22)
     (o_ws, f_ws), (o_na, f_na) = scan_both(second, [0, 300, 301, 450, 640, 999, 1000])
-    assert np.array_equal(o_na, o_ws) and np.array_equal(f_na, f_ws)
+    assert close(o_na, o_ws, 1e-5) and close(f_na, f_ws, 1e-4)
 
 
 def test_noalloc_scan_single_sequence_and_size_limit():
     import clef_b200 as cb
     inp = workloads.delta_operator_inputs(T=257, seed=23)
     (o_ws, f_ws), (o_na, f_na) = scan_both(inp, [0, 257])
-    assert np.array_equal(o_na, o_ws) and np.array_equal(f_na, f_ws)
+    assert close(o_na, o_ws, 1e-5) and close(f_na, f_ws, 1e-4)
     # More sequences than the fixed array holds: rejected before any launch.
     cu = np.arange(0, 4098, dtype=np.int64)
     fake = ctypes.c_void_p(0x10000)

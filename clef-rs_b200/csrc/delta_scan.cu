@@ -320,20 +320,25 @@ __device__ __forceinline__ void gram_store_rows(const uint32_t (&g)[32], int row
       *reinterpret_cast<float4*>(As + i * AP + c0 + c) = make_float4(av[0], av[1], av[2], av[3]);
     }
   } else {
+    // One 16-byte chunk (8 columns) of the hi and lo tiles per store: the
+    // swizzle puts the 8 rows of a store phase on 8 distinct chunks.
 #pragma unroll
-    for (int c = 0; c < 32; c += 2) {
-      float pv[2];
+    for (int c = 0; c < 32; c += 8) {
+      uint32_t ph[4], pl[4];
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int col = c0 + c + u;
-        const bool lower = col <= i && i < n;
-        pv[u] = lower ? expf((float)(gi - Gs[col])) * __uint_as_float(g[c + u]) : 0.f;
+      for (int u = 0; u < 8; u += 2) {
+        float pv[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int col = c0 + c + u + e;
+          const bool lower = col <= i && i < n;
+          pv[e] = lower ? expf((float)(gi - Gs[col])) * __uint_as_float(g[c + u + e]) : 0.f;
+        }
+        split2(pv[0], pv[1], ph[u / 2], pl[u / 2]);
       }
-      uint32_t ph, pl;
-      split2(pv[0], pv[1], ph, pl);
       const uint32_t o = swz(i, c0 + c, 8);
-      put32<GLOBAL>(p_hi, o, ph);
-      put32<GLOBAL>(p_lo, o, pl);
+      *reinterpret_cast<uint4*>(p_hi + o) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+      *reinterpret_cast<uint4*>(p_lo + o) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
     }
   }
 }

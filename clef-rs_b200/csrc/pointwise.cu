@@ -28,10 +28,39 @@ __device__ __forceinline__ int64_t seq_of(const int64_t* cu, int nseq, int64_t t
 
 // ---- RMSNorm (ops::rms_inner, ops.rs:24-32; clef_rms, pointwise.metal:7-43) --
 // One warp per row: sum of squares, inverse = 1 / sqrt(sum / width + eps),
-// out = (x * inverse) * w.
-template <int OUT_BF16>
+// out = (x * inverse) * w. With NV > 0 (width == 128 * NV) the row is read
+// once into registers, all NV 16-byte loads of a lane in flight together.
+template <int OUT_BF16, int NV>
 __global__ void rms_kernel(const float* __restrict__ x, const float* __restrict__ w, int64_t rows,
                            int width, float eps, void* __restrict__ out) {
+  if constexpr (NV > 0) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const float* xr = x + row * width;
+    float4 a[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) a[j] = *reinterpret_cast<const float4*>(xr + lane * 4 + 128 * j);
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) s += a[j].x * a[j].x + a[j].y * a[j].y + a[j].z * a[j].z + a[j].w * a[j].w;
+    s = warp_sum(s);
+    const float inv = 1.f / sqrtf(s / (float)width + eps);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int i = lane * 4 + 128 * j;
+      const float4 b = *reinterpret_cast<const float4*>(w + i);
+      const float r0 = __fmul_rn(__fmul_rn(a[j].x, inv), b.x), r1 = __fmul_rn(__fmul_rn(a[j].y, inv), b.y);
+      const float r2 = __fmul_rn(__fmul_rn(a[j].z, inv), b.z), r3 = __fmul_rn(__fmul_rn(a[j].w, inv), b.w);
+      if (OUT_BF16) {
+        *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(out) + row * width + i) =
+            make_uint2(pack_bf16x2(r0, r1), pack_bf16x2(r2, r3));
+      } else {
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + row * width + i) = make_float4(r0, r1, r2, r3);
+      }
+    }
+    return;
+  }
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -293,23 +322,24 @@ __global__ void __launch_bounds__(256) delta_epilogue_kernel(const float* __rest
                                                              const float* __restrict__ w, float eps,
                                                              int64_t T, int Hv, uint16_t* __restrict__ y) {
   // One warp per token; its Hv rows of 128 go four at a time with all eight
-  // 16-byte loads of a batch issued before any is used.
+  // loads of a batch (o rows and z rows) issued before any is used.
   const int lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= T) return;
   const float4 wv = *reinterpret_cast<const float4*>(w + lane * 4);
-  for (int h0 = 0; h0 < Hv; h0 += 4) {
-    float4 a[4], zv[4];
-    uint2 zr[4];
+  constexpr int HB = 4;  // heads per batch: 8 loads per lane in flight
+  for (int h0 = 0; h0 < Hv; h0 += HB) {
+    float4 a[HB], zv[HB];
+    uint2 zr[HB];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < HB; ++u) {
       if (h0 + u < Hv) {
         a[u] = *reinterpret_cast<const float4*>(o + (t * Hv + h0 + u) * 128 + lane * 4);
         zr[u] = *reinterpret_cast<const uint2*>(z + t * ldz + (h0 + u) * 128 + lane * 4);
       }
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < HB; ++u) {
       if (h0 + u >= Hv) break;
       zv[u] = ProIn<uint16_t>::f4(zr[u]);
       const float4 b = make_float4(bf16_round(a[u].x), bf16_round(a[u].y), bf16_round(a[u].z),
@@ -508,10 +538,19 @@ int launch_rmsnorm(const float* x, const float* w, int64_t rows, int width, floa
   if (rows == 0) return CLEF_OK;
   const int warps = 8;
   const dim3 grid((unsigned)ceil_div(rows, warps));
-  if (out_dtype == CLEF_BF16)
-    rms_kernel<1><<<grid, warps * 32, 0, s>>>(x, w, rows, width, eps, out);
-  else
-    rms_kernel<0><<<grid, warps * 32, 0, s>>>(x, w, rows, width, eps, out);
+  // Register-resident rows for the backbone widths (hidden 2560 and 4096).
+  const bool al = (((uintptr_t)x | (uintptr_t)w | (uintptr_t)out) & 15) == 0;
+  if (al && width == 2560) {
+    if (out_dtype == CLEF_BF16) rms_kernel<1, 20><<<grid, warps * 32, 0, s>>>(x, w, rows, width, eps, out);
+    else rms_kernel<0, 20><<<grid, warps * 32, 0, s>>>(x, w, rows, width, eps, out);
+  } else if (al && width == 4096) {
+    if (out_dtype == CLEF_BF16) rms_kernel<1, 32><<<grid, warps * 32, 0, s>>>(x, w, rows, width, eps, out);
+    else rms_kernel<0, 32><<<grid, warps * 32, 0, s>>>(x, w, rows, width, eps, out);
+  } else if (out_dtype == CLEF_BF16) {
+    rms_kernel<1, 0><<<grid, warps * 32, 0, s>>>(x, w, rows, width, eps, out);
+  } else {
+    rms_kernel<0, 0><<<grid, warps * 32, 0, s>>>(x, w, rows, width, eps, out);
+  }
   return launch_status("rmsnorm");
 }
 

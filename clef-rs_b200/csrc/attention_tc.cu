@@ -5,14 +5,15 @@
 // softmax(q k^T / 16 + lower-right causal mask) v per query head, kv head
 // h / (H / Hkv), keys = [shared prefix keys] ++ [the sequence's own keys].
 //
-// CTA = 128 query rows of one (sequence, query head); 6 warps:
+// CTA = 128 query rows of one (sequence, query head); 10 warps:
 //   warp 0      TMA producer: the Q tile once, then K and V^T tiles of 64 keys
-//               into a two-stage ring (no multicast);
+//               into a 4-slot ring in consumption order (no multicast);
 //   warp 1      allocates 512 TMEM columns; one thread issues
 //               S_j = Q K_j^T (128 x 64, double-buffered in TMEM) and
 //               O += P_j V_j (128 x 256 accumulator in TMEM), with S_{j+2}
 //               issued while the softmax of block j runs;
-//   warps 2..5  one query row per thread: tcgen05.ld of the S row, mask,
+//   warps 2..9  one query row per thread, two warps per row quarter (each
+//               exponentiates half of every 64-key block): tcgen05.ld of the S row, mask,
 //               online softmax in the log2 domain, P row (BF16) into a
 //               swizzled shared tile for the PV product. The running maximum is
 //               only raised (and O rescaled in TMEM) when a row's maximum grows
@@ -46,8 +47,10 @@ constexpr int OFF_Q = 0;
 constexpr int OFF_RING = OFF_Q + Q_BYTES;               // NSLOT slots
 constexpr int OFF_P = OFF_RING + NSLOT * TILE_BYTES;    // 2 buffers
 constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
-constexpr int SMEM = 1024 + OFF_BAR + 256;
-constexpr int THREADS = 192;
+constexpr int OFF_LSUM = OFF_BAR + 256;                // [2][128] F32 partial row sums
+constexpr int SMEM = 1024 + OFF_LSUM + 2 * BQ * 4;
+constexpr int SOFTMAX_WARPS = 8;                        // two per TMEM lane quarter
+constexpr int THREADS = 64 + SOFTMAX_WARPS * 32;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t COL_O = 0, COL_S = 256;             // S buffers at 256 and 320
 constexpr float RESCALE_THRESHOLD = 8.f;               // log2 units
@@ -122,6 +125,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* g_full = bar + 11;   // gate tile landed in the Q buffer
   uint64_t* full = bar + 12;     // [NSLOT] ring slot loaded
   uint64_t* empty = bar + 12 + NSLOT;  // [NSLOT] ring slot consumed
+  uint64_t* l_bar = bar + 12 + 2 * NSLOT;  // partial row sums exchanged
+  float* l_part = reinterpret_cast<float*>(sm + OFF_LSUM);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y;
@@ -153,11 +158,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);
+      mbar_init(&p_full[i], SOFTMAX_WARPS);
       mbar_init(&pv_done[i], 1);
     }
     mbar_init(o_final, 1);
     mbar_init(drain, 1);
+    mbar_init(l_bar, SOFTMAX_WARPS);
     mbar_init(q_free, 1);
     mbar_init(g_full, 1);
     fence_barrier_init();
@@ -291,7 +297,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // Softmax warps: row r of the query tile; TMEM lane quarter = warp % 4.
+    // Two warps share each quarter: both read the whole S row (so both derive
+    // the same row maximum without exchanging it), and warp half `hf`
+    // exponentiates keys [32 hf, 32 hf + 32) of the block and owns O columns
+    // [128 hf, 128 hf + 128).
     const int quarter = warp & 3;
+    const int hf = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
     const int64_t qi = q0 + r;  // query index within the sequence
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
@@ -304,9 +315,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       ok = __all_sync(0xffffffffu, mbar_wait(&s_full[st], (j >> 1) & 1));
       if (!ok) break;
       tc_fence_after();
+      // sr[0..32): this warp's 32 keys of the block; sr[32..64): the partner's.
       uint32_t sr[64];
-      tmem_ld_32x32b_x32(tmem + lane_off + COL_S + st * BK, *reinterpret_cast<uint32_t(*)[32]>(sr));
-      tmem_ld_32x32b_x32(tmem + lane_off + COL_S + st * BK + 32,
+      tmem_ld_32x32b_x32(tmem + lane_off + COL_S + st * BK + hf * 32, *reinterpret_cast<uint32_t(*)[32]>(sr));
+      tmem_ld_32x32b_x32(tmem + lane_off + COL_S + st * BK + (1 - hf) * 32,
                          *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
       tmem_ld_wait();
       // Visible keys of this row in block j: columns c <= lim. A block every
@@ -317,9 +329,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!full) {
         const int64_t l64 = pre ? P - 1 - kbase : qi - kbase;
         const int lim = l64 < -1 ? -1 : (l64 > 63 ? 63 : (int)l64);
+        const int mine = hf * 32, other = (1 - hf) * 32;  // block columns of sr[0], sr[32]
 #pragma unroll
-        for (int c = 0; c < 64; ++c)
-          if (c > lim) sr[c] = 0xff800000u;  // -inf
+        for (int c = 0; c < 32; ++c) {
+          if (mine + c > lim) sr[c] = 0xff800000u;  // -inf
+          if (other + c > lim) sr[32 + c] = 0xff800000u;
+        }
       }
       // Row maximum of the raw scores (the scale is positive), four chains.
       float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
@@ -343,7 +358,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!ok) break;
         tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = hf * 4; c < hf * 4 + 4; ++c) {
           uint32_t o[32];
           tmem_ld_32x32b_x32(tmem + lane_off + COL_O + c * 32, o);
           tmem_ld_wait();
@@ -364,12 +379,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float neg_m = -m_run;
       float ps[2] = {0.f, 0.f};
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
+      for (int cq = 0; cq < 4; ++cq) {
+        const int ch = hf * 4 + cq;  // this warp's 16-byte chunks of the 128-byte P row
         uint32_t w[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[ch * 8 + 2 * e]), p.sl2, neg_m));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[ch * 8 + 2 * e + 1]), p.sl2, neg_m));
+          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[cq * 8 + 2 * e]), p.sl2, neg_m));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[cq * 8 + 2 * e + 1]), p.sl2, neg_m));
           w[e] = pack_bf16x2(p0, p1);
           ps[0] += __uint_as_float(w[e] << 16);
           ps[1] += __uint_as_float(w[e] & 0xffff0000u);
@@ -384,15 +400,20 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     if (ok && nblk > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_final, 0));
     if (ok && p.gate) ok = __all_sync(0xffffffffu, mbar_wait(g_full, 0));
+    // Row sum = the two warps' partial sums, added in the same order by both.
+    l_part[hf * BQ + r] = l_run;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(l_bar);
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(l_bar, 0));
     if (!ok) {
       raise_device_error(kDevAttentionTimeout);
     } else {
       tc_fence_after();
-      const float inv = 1.f / l_run;
+      const float inv = 1.f / (l_part[r] + l_part[BQ + r]);
       const bool valid = qi < len;
       const int64_t row = start + qi;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = hf * 4; c < hf * 4 + 4; ++c) {
         uint32_t o[32];
         tmem_ld_32x32b_x32(tmem + lane_off + COL_O + c * 32, o);
         tmem_ld_wait();

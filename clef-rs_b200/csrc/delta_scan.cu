@@ -770,6 +770,7 @@ struct PipeArgs {
   const ScanChunk* chunks;
   uint8_t* kq_img;  // [chunks][Hk][KQ_IMG]
   uint8_t* tp_img;  // [chunks][Hv][TP_IMG]
+  const int32_t* order;  // [nseq] carry order: longest sequences first
 };
 
 __global__ void __launch_bounds__(THREADS, 2) delta_prep_kernel(PipeArgs p) {
@@ -890,7 +891,9 @@ __global__ void __launch_bounds__(THREADS, 1) delta_carry_kernel(PipeArgs p) {
   const int tid = threadIdx.x, lane = tid & 31;
   const int warp = (int)blockIdx.y * (blockDim.x >> 5) + (tid >> 5);  // 16-row block of S^T
   const int h = blockIdx.x % a.Hv;
-  const int s = blockIdx.x / a.Hv;
+  // Longest sequences are carried first, so the last wave of CTAs holds the
+  // shortest chains and the tail of the launch stays short.
+  const int s = p.order[blockIdx.x / a.Hv];
   const int kh = h / (a.Hv / a.Hk);
   const ScanSeq sq = p.seqs[s];
   const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(sm);
@@ -943,7 +946,7 @@ size_t delta_scan_fused_workspace(int nseq) {
 namespace {
 size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
 struct PipeLayout {
-  size_t seq_off, chunk_off, kq_off, tp_off, total;
+  size_t seq_off, chunk_off, order_off, kq_off, tp_off, total;
   int64_t max_chunks;
 };
 PipeLayout pipe_layout(int64_t total_tokens, int nseq, int Hk, int Hv) {
@@ -951,7 +954,8 @@ PipeLayout pipe_layout(int64_t total_tokens, int nseq, int Hk, int Hv) {
   l.max_chunks = (total_tokens + C - 1) / C + nseq;
   l.seq_off = 0;
   l.chunk_off = al256(sizeof(ScanSeq) * (size_t)nseq);
-  l.kq_off = al256(l.chunk_off + sizeof(ScanChunk) * (size_t)l.max_chunks);
+  l.order_off = al256(l.chunk_off + sizeof(ScanChunk) * (size_t)l.max_chunks);
+  l.kq_off = al256(l.order_off + sizeof(int32_t) * (size_t)nseq);
   l.tp_off = al256(l.kq_off + (size_t)KQ_IMG * l.max_chunks * Hk);
   l.total = al256(l.tp_off + (size_t)TP_IMG * l.max_chunks * Hv);
   return l;
@@ -996,6 +1000,12 @@ int delta_scan_plan(const int64_t* cu_host, int nseq, int Hk, int Hv, void* ws, 
                             cudaMemcpyHostToDevice, s));
   CLEF_CUDA(cudaMemcpyAsync(base + l.chunk_off, chunks.data(), sizeof(ScanChunk) * chunks.size(),
                             cudaMemcpyHostToDevice, s));
+  std::vector<int32_t> order(nseq);
+  for (int si = 0; si < nseq; ++si) order[si] = si;
+  std::stable_sort(order.begin(), order.end(),
+                   [&](int32_t x, int32_t y) { return seqs[x].nchunks > seqs[y].nchunks; });
+  CLEF_CUDA(cudaMemcpyAsync(base + l.order_off, order.data(), sizeof(int32_t) * order.size(),
+                            cudaMemcpyHostToDevice, s));
   plan->ws = ws;
   plan->nseq = nseq;
   plan->nchunks = (int64_t)chunks.size();
@@ -1032,6 +1042,7 @@ int launch_delta_scan_planned(const ScanPlan& plan, const float* q, const float*
   p.chunks = reinterpret_cast<const ScanChunk*>(base + l.chunk_off);
   p.kq_img = reinterpret_cast<uint8_t*>(base + l.kq_off);
   p.tp_img = reinterpret_cast<uint8_t*>(base + l.tp_off);
+  p.order = reinterpret_cast<const int32_t*>(base + l.order_off);
   delta_prep_kernel<<<dim3((unsigned)plan.nchunks, (unsigned)plan.Hk), THREADS, PREP_SMEM, s>>>(p);
   RC_(launch_status("delta_prep"));
   // Few (sequence, head) pairs: split their value rows over 2 or 4 CTAs.

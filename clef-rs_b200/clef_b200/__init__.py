@@ -38,7 +38,8 @@ EXPORTS = [
     "clef_engine_prefill_device", "clef_engine_launches", "clef_engine_cancel",
     "clef_engine_stage_times", "clef_engine_set_profiling", "clef_engine_destroy",
     "clef_prefix_tokens", "clef_prefix_bytes", "clef_prefix_destroy", "clef_head_create",
-    "clef_head_set_weight", "clef_head_finalize", "clef_head_forward", "clef_head_destroy", "clef_decide",
+    "clef_head_set_weight", "clef_head_finalize", "clef_head_forward", "clef_head_destroy",
+    "clef_selftest_wait_timeout", "clef_decide",
 ]
 
 
@@ -114,6 +115,7 @@ def _load():
         "clef_head_finalize": (ctypes.c_int, [_vp]),
         "clef_head_forward": (ctypes.c_int, [_vp, _vp, _i64, _vp, _i64, _vp, _vp, _i32, _vp, _vp]),
         "clef_head_destroy": (ctypes.c_int, [_vp]),
+        "clef_selftest_wait_timeout": (ctypes.c_int, [_i32, _vp]),
         "clef_decide": (ctypes.c_int, [_vp, _i32, _i32, _vp]),
     }
     for name, (res, args) in sig.items():

@@ -50,6 +50,7 @@ enum DeviceError : int {
   kDevGemmTimeout = 1,
   kDevAttentionTimeout = 2,
   kDevScanTimeout = 3,
+  kDevProbeTimeout = 4,
 };
 static __device__ int g_device_error = 0;  // one flag per translation unit
 

@@ -41,16 +41,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Waits for the phase of parity `parity` to complete; gives up after ~2 s
-// and returns false (the caller records a device error and unwinds).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Waits for the phase of parity `parity` to complete; gives up after
+// `limit_ns` (2 s by default) and returns false (the caller records a device
+// error and unwinds).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          uint64_t limit_ns = 2000000000ull) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (global_ns() - t0 > 2000000000ull) return false;
+    if (global_ns() - t0 > limit_ns) return false;
   }
 }
 

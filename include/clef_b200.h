@@ -334,6 +334,13 @@ int clef_head_forward(clef_head* h, const float* hidden, int64_t T, const float*
                       int32_t nq, const int32_t* option_spans, float* logits);
 int clef_head_destroy(clef_head* h);
 
+/* Diagnostic with no counterpart in the reference: runs the bounded-wait
+ * failure path of the device kernels on purpose (an mbarrier nothing arrives
+ * on, given up after limit_ms in [1, 2000]) and returns the status a stuck
+ * wait produces, CLEF_ERR_DEVICE_TIMEOUT, with the context still usable.
+ * Any other status means the failure path is broken. */
+int clef_selftest_wait_timeout(int32_t limit_ms, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Decisions from schema-head logits (answers, crates/core/src/types.rs:728-802). */
 /* ------------------------------------------------------------------------ */

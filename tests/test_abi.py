@@ -173,3 +173,8 @@ def test_head_rejects_bad_geometry_before_touching_a_device():
     assert L.clef_head_set_weight(None, b"x", FAKE, 1) == 1
     assert L.clef_head_finalize(None) == 1
     assert L.clef_head_destroy(None) == 0
+
+
+def test_selftest_rejects_bad_limit_before_launch():
+    assert cb.lib.clef_selftest_wait_timeout(0, None) == 1
+    assert cb.lib.clef_selftest_wait_timeout(5000, None) == 1

@@ -18,20 +18,22 @@
 // chunk-relative cumulative log-decays, so nothing divides by an underflowed
 // prefix product (a per-token decay of -1000 is exact).
 //
-// One CTA per (sequence, v-head), 8 warps; warp w owns value rows
-// [16w, 16w+16) of S^T as 64 F32 mma accumulators in registers for the whole
-// sequence. The accumulators are re-packed in registers as the A operand of the
-// next product (the C-fragment -> A-fragment identity of m16n8k16), so S never
-// leaves the SM between chunks. Products use BF16 mma.sync with F32
-// accumulation and a two-term BF16 split of both operands
-// (x = hi + lo; x*y ~ hi*hi + hi*lo + lo*hi), which keeps ~16 mantissa bits:
-// the result tracks the F32 per-token recurrence to ~1e-5.
+// Products use BF16 tensor-core MMAs with F32 accumulation and a two-term
+// BF16 split of both operands (x = hi + lo; x*y ~ hi*hi + hi*lo + lo*hi), which
+// keeps ~16 mantissa bits: the result tracks the F32 per-token recurrence to
+// ~1e-5. The workspace path runs two kernels: delta_prep_kernel (chunk-
+// parallel; Gram products on tcgen05) and delta_carry_tc_kernel (the state
+// carry on tcgen05, S^T in TMEM). The allocation-free path runs one fused
+// kernel, delta_scan_kernel (one CTA per (sequence, v-head), 8 warps; warp w
+// keeps value rows [16w, 16w+16) of S^T as mma.sync accumulators in registers,
+// re-packed in registers as the A operand of the next product).
 // The triangular inverse T is computed in F32 by blocked forward substitution
 // (four 16 x 16 diagonal blocks, then the off-diagonal blocks).
 // A capture point inside a chunk does not change the chunking: the state at
 // the capture token is formed from the same chunk quantities, so a prefill with
 // capture is bit-identical to one without.
 #include <algorithm>
+#include <string>
 #include <vector>
 
 #include "kernels.cuh"
@@ -159,6 +161,29 @@ __device__ __forceinline__ void lda(uint32_t base, int m0, int k0, int cpr, int 
   ldsm4(base + swz(m0 + (lane & 15), k0 + (lane >> 4) * 8, cpr), r);
 }
 
+// Byte offset of element (row, col) of K/Q tile t (0 = K hi, 1 = K lo, 2 = Q hi,
+// 3 = Q lo) of a chunk's K/Q operand. UK: the tcgen05 layout of the workspace
+// image and the prep kernel's Gram operand (hi tile [K; Q] then lo tile, in
+// umma_off order); otherwise four [64][128] tiles in the ldmatrix swizzle.
+template <bool UK>
+__device__ __forceinline__ uint32_t kq_off(int t, int row, int col) {
+  if (UK) return (uint32_t)((t & 1) * GRAM_TILE) + umma_off(row + (t >> 1) * 64, col);
+  return (uint32_t)(t * KQ_BYTES) + swz(row, col, 16);
+}
+// B fragments of K/Q tile t read as [n][k] (ldb_nk) or as [k][n] (ldb_kn).
+template <bool UK>
+__device__ __forceinline__ void ldb_kq(uint32_t base, int t, int n0, int k0, int lane, uint32_t (&r)[4]) {
+  const int row = n0 + (lane & 7) + ((lane >> 4) << 3);
+  const int col = k0 + ((lane >> 3) & 1) * 8;
+  ldsm4(base + kq_off<UK>(t, row, col), r);
+}
+template <bool UK>
+__device__ __forceinline__ void ldb_kq_t(uint32_t base, int t, int n0, int k0, int lane, uint32_t (&r)[4]) {
+  const int row = k0 + (lane & 7) + (((lane >> 3) & 1) << 3);
+  const int col = n0 + ((lane >> 4) << 3);
+  ldsm4t(base + kq_off<UK>(t, row, col), r);
+}
+
 // ---------------------------------------------------------------------------
 // Building blocks shared by the fused kernel and the prep/carry pipeline, so
 // both paths perform the same arithmetic in the same order.
@@ -207,17 +232,17 @@ __device__ __forceinline__ void stage_kq(const float* __restrict__ q, const floa
       const uint32_t o = swz(i, c4, 16);
       const uint2 w[4] = {make_uint2(kh0, kh1), make_uint2(kl0, kl1), make_uint2(qh0, qh1),
                           make_uint2(ql0, ql1)};
-      if (umma_smem) {
-        // [K; Q] rows of the tcgen05 operand: hi tile, then lo tile.
-        *reinterpret_cast<uint2*>(sm_kq + umma_off(i, c4)) = w[0];
-        *reinterpret_cast<uint2*>(sm_kq + GRAM_TILE + umma_off(i, c4)) = w[1];
-        *reinterpret_cast<uint2*>(sm_kq + umma_off(64 + i, c4)) = w[2];
-        *reinterpret_cast<uint2*>(sm_kq + GRAM_TILE + umma_off(64 + i, c4)) = w[3];
-      }
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
-        if (!umma_smem) *reinterpret_cast<uint2*>(sm_kq + t * KQ_BYTES + o) = w[t];
-        if (img) *reinterpret_cast<uint2*>(img + t * KQ_BYTES + o) = w[t];
+        if (umma_smem) {
+          // [K; Q] rows of the tcgen05 operand (hi tile, then lo tile); the
+          // workspace image has the same bytes.
+          const uint32_t u = kq_off<true>(t, i, c4);
+          *reinterpret_cast<uint2*>(sm_kq + u) = w[t];
+          if (img) *reinterpret_cast<uint2*>(img + u) = w[t];
+        } else {
+          *reinterpret_cast<uint2*>(sm_kq + t * KQ_BYTES + o) = w[t];
+        }
       }
     }
   }
@@ -468,8 +493,8 @@ __device__ __forceinline__ void carry_step(float (&S)[16][4], const float (&Vr)[
 #pragma unroll
     for (int np = 0; np < 4; ++np) {
       uint32_t bh[4], bl[4];
-      ldb_nk(c.kq + 0 * KQ_BYTES, np * 16, ks * 16, 16, lane, bh);
-      ldb_nk(c.kq + 1 * KQ_BYTES, np * 16, ks * 16, 16, lane, bl);
+      ldb_kq<false>(c.kq, 0, np * 16, ks * 16, lane, bh);
+      ldb_kq<false>(c.kq, 1, np * 16, ks * 16, lane, bl);
       mma3(R[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
       mma3(R[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
     }
@@ -508,8 +533,8 @@ __device__ __forceinline__ void carry_step(float (&S)[16][4], const float (&Vr)[
 #pragma unroll
     for (int np = 0; np < 4; ++np) {
       uint32_t bh[4], bl[4];
-      ldb_nk(c.kq + 2 * KQ_BYTES, np * 16, ks * 16, 16, lane, bh);
-      ldb_nk(c.kq + 3 * KQ_BYTES, np * 16, ks * 16, 16, lane, bl);
+      ldb_kq<false>(c.kq, 2, np * 16, ks * 16, lane, bh);
+      ldb_kq<false>(c.kq, 3, np * 16, ks * 16, lane, bl);
       mma3(R[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
       mma3(R[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
     }
@@ -564,8 +589,8 @@ __device__ __forceinline__ void carry_step(float (&S)[16][4], const float (&Vr)[
 #pragma unroll
         for (int np = 0; np < 4; ++np) {
           uint32_t bh[4], bl[4];
-          ldb_kn(c.kq + 0 * KQ_BYTES, half * 64 + np * 16, ks * 16, 16, lane, bh);
-          ldb_kn(c.kq + 1 * KQ_BYTES, half * 64 + np * 16, ks * 16, 16, lane, bl);
+          ldb_kq_t<false>(c.kq, 0, half * 64 + np * 16, ks * 16, lane, bh);
+          ldb_kq_t<false>(c.kq, 1, half * 64 + np * 16, ks * 16, lane, bl);
           mma3(X[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
           mma3(X[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
         }
@@ -598,8 +623,8 @@ __device__ __forceinline__ void carry_step(float (&S)[16][4], const float (&Vr)[
 #pragma unroll
     for (int np = 0; np < 8; ++np) {
       uint32_t bh[4], bl[4];
-      ldb_kn(c.kq + 0 * KQ_BYTES, np * 16, ks * 16, 16, lane, bh);
-      ldb_kn(c.kq + 1 * KQ_BYTES, np * 16, ks * 16, 16, lane, bl);
+      ldb_kq_t<false>(c.kq, 0, np * 16, ks * 16, lane, bh);
+      ldb_kq_t<false>(c.kq, 1, np * 16, ks * 16, lane, bl);
       mma3(S[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
       mma3(S[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
     }
@@ -729,12 +754,13 @@ __global__ void __launch_bounds__(THREADS, 1) delta_scan_kernel(ScanArgs a) {
 
 // ---------------------------------------------------------------------------
 // Pipelined pair. delta_prep_kernel: one CTA per (chunk, k-head), fully
-// parallel: splits K, Q into hi/lo tiles, forms the Gram products once, and
-// for each v-head of the k-head writes T diag(beta), P and the decay vectors
-// to the workspace as tile images. delta_carry_kernel: one CTA per
-// (sequence, v-head) walks the chunks; every chunk input is independent of the
-// state, so the next chunk's tiles stream in with cp.async while the tensor
-// cores work on the current one.
+// parallel: splits K, Q into hi/lo tiles (the [K; Q] tcgen05 operand, also
+// written to the workspace as the chunk's K/Q image), forms the Gram products
+// once, and for each v-head of the k-head writes T diag(beta), P and the decay
+// vectors to the workspace as the chunk's T/P image. delta_carry_tc_kernel
+// (below) walks the chunks of each (sequence, v-head); every chunk input is
+// independent of the state, so the next chunk's images stream in while the
+// tensor core works on the current one.
 // ---------------------------------------------------------------------------
 struct ScanSeq {
   int32_t chunk0;
@@ -750,8 +776,6 @@ constexpr int TP_TILES = 4 * SQ_BYTES;                   // THI, TLO, PHI, PLO
 constexpr int VEC_BYTES = 64 * 4 + 64 * 4 + 64 * 4 + 64 * 8;  // eg, egd, el, G
 constexpr int TP_IMG = TP_TILES + VEC_BYTES;              // 34048 bytes
 constexpr int KQ_IMG = 4 * KQ_BYTES;                      // 65536 bytes
-constexpr int STAGE = KQ_IMG + TP_IMG;                    // 99584 bytes
-constexpr int CARRY_SMEM = 2 * STAGE;
 
 // prep kernel shared layout
 constexpr int P_OFF_KQ = 0;
@@ -869,71 +893,447 @@ int scan_device_error(int* code) { return read_device_error(code); }
 
 namespace {
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src));
+// ---------------------------------------------------------------------------
+// delta_carry_tc_kernel: the state carry on the tcgen05 tensor core.
+//
+// The chunk algebra of carry_step (three-term split-BF16 products with F32
+// accumulation), with every product accumulated in TMEM and its BF16 A
+// operands written back into TMEM, so no state tile goes through shared
+// memory. The state S^T itself (row dv = TMEM lane) lives in TMEM in F32 and is
+// the accumulator of the state update. Persistent: CTA b carries (sequence,
+// v-head) pairs b, b + grid, ... of the longest-first order; each chunk's K/Q
+// and T/P images stream into one of two shared-memory stages by bulk copies.
+//
+// Warps 0..7 are the epilogue: warp w reads TMEM lane quarter w % 4 and takes
+// half hf = w / 4 of the columns, so thread (w, lane) owns value row
+// dv = 32 (w % 4) + lane, dk columns [64 hf, 64 hf + 64) of S^T and tokens
+// [32 hf, 32 hf + 32) of every chunk. Warp 8 lane 0 issues the MMAs, warp 9
+// lane 0 the bulk copies.
+//
+// TMEM columns (512, one CTA per SM):
+//   [0, 128)    S^T (F32)
+//   [128, 256)  S^T split: hi [128, 192), lo [192, 256)
+//   [256, 320)  R^T = S^T K^T, then X_R (R split in place), then X_D' (split
+//               D^T diag(egd))
+//   [320, 384)  O1 = S^T Q^T
+//   [384, 448)  D^T = X_R (T diag beta)^T, then X_D (D split in place)
+//   [448, 512)  O2 = X_D P^T (a capture chunk first holds X_D'' there)
+// Token-indexed operands (X_R, X_D, X_D', X_D''): warp half hf writes its 32
+// tokens as 16 hi words then 16 lo words in columns [base + 32 hf, +32), so a
+// warp only rewrites columns it has read; K step t (tokens 16t .. 16t + 15)
+// starts at column base + 32 (t / 2) + 8 (t % 2), +16 for lo.
+// Per chunk k (E = epilogue warps, M = MMA issuer):
+//   E a   split S^T -> [128, 256)                           -> a_bar
+//   M     R = S^T K^T                                       -> r_bar
+//   E     output step g of chunk k - 1 (O1, O2 of k - 1)    -> stage k - 1 free
+//   E c   R <- V^T - R diag(e^G); split in place            -> c_bar
+//   M     D = X_R (T diag beta)^T -> d_bar; O1 = S^T Q^T
+//   E e   split D in place; X_D' = split D diag(egd);
+//         S^T <- e^{G_last} S^T                             -> e_bar
+//   M     S^T += X_D' K -> i_bar; O2 = X_D P^T -> f_bar, stage k free
+// ---------------------------------------------------------------------------
+constexpr int TC_STAGE = 100352;  // one chunk's K/Q and T/P images, 1024-aligned
+constexpr int TC_THREADS = 320;
+constexpr int TC_OFF_BAR = 2 * TC_STAGE;
+constexpr int TC_SMEM = 1024 + TC_OFF_BAR + 17 * 8;
+static_assert(KQ_IMG + TP_IMG <= TC_STAGE && TC_STAGE % 1024 == 0, "carry stage layout");
+constexpr uint32_t TC_S = 0, TC_SA = 128, TC_R = 256, TC_O1 = 320, TC_D = 384, TC_O2 = 448;
+
+// x = hi + lo with hi = bf16(x), lo = bf16(x - hi), two values per word (even
+// index in the low half): the same values as split2.
+__device__ __forceinline__ void split_pair(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  hi = pack_bf16x2(x0, x1);
+  lo = pack_bf16x2(x0 - __uint_as_float(hi << 16), x1 - __uint_as_float(hi & 0xffff0000u));
 }
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;"); }
-__device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-__device__ __forceinline__ void fetch_stage(uint32_t dst, const uint8_t* kq, const uint8_t* tp,
-                                            int tid, int nthreads) {
-  for (int o = tid * 16; o < KQ_IMG; o += nthreads * 16) cp_async16(dst + o, kq + o);
-  for (int o = tid * 16; o < TP_IMG; o += nthreads * 16) cp_async16(dst + KQ_IMG + o, tp + o);
-}
-
-// The value rows of the state never mix (every product is row by row in dv),
-// so a (sequence, value head) may be split over gridDim.y CTAs of
-// 256 / gridDim.y threads, each carrying its own 16-row blocks of S^T: a
-// single long sequence then runs on up to 4x more SMs.
-__global__ void __launch_bounds__(THREADS, 1) delta_carry_kernel(PipeArgs p) {
-  extern __shared__ __align__(128) uint8_t sm[];
-  const ScanArgs& a = p.a;
-  const int tid = threadIdx.x, lane = tid & 31;
-  const int warp = (int)blockIdx.y * (blockDim.x >> 5) + (tid >> 5);  // 16-row block of S^T
-  const int h = blockIdx.x % a.Hv;
-  // Longest sequences are carried first, so the last wave of CTAs holds the
-  // shortest chains and the tail of the launch stays short.
-  const int s = p.order[blockIdx.x / a.Hv];
-  const int kh = h / (a.Hv / a.Hk);
-  const ScanSeq sq = p.seqs[s];
-  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(sm);
-  auto kq_of = [&](int64_t gc) { return p.kq_img + (gc * a.Hk + kh) * (int64_t)KQ_IMG; };
-  auto tp_of = [&](int64_t gc) { return p.tp_img + (gc * a.Hv + h) * (int64_t)TP_IMG; };
-
-  float S[16][4];
-  load_state(S, init_for(a, s, h), warp, lane);
-  fetch_stage(sbase, kq_of(sq.chunk0), tp_of(sq.chunk0), tid, blockDim.x);
-  cp_commit();
-  int64_t done = 0;  // tokens of this sequence before the current chunk
-  for (int ci = 0; ci < sq.nchunks; ++ci) {
-    const int64_t gc = sq.chunk0 + ci;
-    const ScanChunk ch = p.chunks[gc];
-    float Vr[8][4];
-    load_v(a.v, ch.t0, ch.n, a.Hv, h, warp, lane, Vr);
-    cp_wait_all();
-    __syncthreads();  // stage ci is in; every warp finished chunk ci - 1
-    if (ci + 1 < sq.nchunks) {
-      const uint32_t nxt = sbase + ((ci + 1) & 1) * STAGE;
-      fetch_stage(nxt, kq_of(gc + 1), tp_of(gc + 1), tid, blockDim.x);
-      cp_commit();
+// Three-term product into TMEM: d (+)= A * B^T with A split in TMEM (column of
+// K step t from a_col(lo, t), 8 columns per 16-wide step) and B split in
+// shared memory (descriptor from b_desc(lo, t)); the small terms go first.
+template <int KSTEPS, typename ACol, typename BDesc>
+__device__ __forceinline__ void tc_mma3(uint32_t d, ACol a_col, uint32_t idesc, BDesc b_desc, bool accumulate) {
+  uint32_t acc = accumulate ? 1u : 0u;
+#pragma unroll
+  for (int term = 0; term < 3; ++term) {
+#pragma unroll
+    for (int t = 0; t < KSTEPS; ++t) {
+      // lo*hi, hi*lo, hi*hi
+      sm100::umma_f16_ts(d, a_col(term == 0, t), b_desc(term == 1, t), idesc, acc);
+      acc = 1;
     }
-    const uint32_t cur = sbase + (ci & 1) * STAGE;
-    const uint8_t* cur_ptr = sm + (ci & 1) * STAGE;
-    const float* vec = reinterpret_cast<const float*>(cur_ptr + KQ_IMG + TP_TILES);
-    ChunkOps ops;
-    ops.kq = cur;
-    ops.tp = cur + KQ_IMG;
-    ops.eg = vec;
-    ops.egd = vec + 64;
-    ops.el = vec[128];
-    ops.G = reinterpret_cast<const double*>(vec + 192);
-    int cap_row = -1;
-    if (a.capture_state && a.capture > done && a.capture <= done + ch.n)
-      cap_row = (int)(a.capture - 1 - done);
-    carry_step(S, Vr, ops, ch.n, ch.t0, a.Hv, h, warp, lane, a.out, cap_row, a.capture_state);
-    done += ch.n;
   }
-  if (a.final_state) store_state(S, a.final_state + ((int64_t)s * a.Hv + h) * DK * DV, warp, lane);
+}
+
+// Column of K step t of a token-indexed operand at TMEM address `base`.
+__device__ __forceinline__ uint32_t tok_col(uint32_t base, bool lo, int t) {
+  return base + 32 * (t >> 1) + 8 * (t & 1) + (lo ? 16 : 0);
+}
+
+__global__ void __launch_bounds__(TC_THREADS, 1) delta_carry_tc_kernel(PipeArgs p, int npairs) {
+  using namespace sm100;
+  extern __shared__ __align__(128) uint8_t sm_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>(((uintptr_t)sm_raw + 1023) & ~(uintptr_t)1023);
+  const ScanArgs& a = p.a;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + TC_OFF_BAR);
+  uint64_t* full = bar + 0;    // [2] stage loaded
+  uint64_t* empty = bar + 2;   // [2] stage consumed (MMA commit + 8 epilogue warps)
+  uint64_t* a_bar = bar + 4;
+  uint64_t* r_bar = bar + 5;
+  uint64_t* c_bar = bar + 6;
+  uint64_t* d_bar = bar + 7;
+  uint64_t* e_bar = bar + 8;
+  uint64_t* f_bar = bar + 9;
+  uint64_t* i_bar = bar + 10;
+  uint64_t* drain = bar + 11;     // error path: completion of this CTA's own MMAs
+  uint64_t* cap_bar = bar + 12;   // capture chunk: captured-state product done
+  uint64_t* capd_bar = bar + 13;  // capture chunk: captured state read by the 8 warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 14);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 15);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 9);
+    }
+    mbar_init(a_bar, 8);
+    mbar_init(r_bar, 1);
+    mbar_init(c_bar, 8);
+    mbar_init(d_bar, 1);
+    mbar_init(e_bar, 8);
+    mbar_init(f_bar, 1);
+    mbar_init(i_bar, 1);
+    mbar_init(drain, 1);
+    mbar_init(cap_bar, 1);
+    mbar_init(capd_bar, 8);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 8) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sbase = smem_u32(sm);
+  // A bounded wait; the first one to time out stops the whole CTA.
+  auto wait = [&](uint64_t* b, uint32_t parity) -> bool {
+    if (*abort_flag) return false;
+    if (mbar_wait(b, parity)) return true;
+    *abort_flag = 1;
+    raise_device_error(kDevScanTimeout);
+    return false;
+  };
+  const int rep = a.Hv / a.Hk;
+  // Capture inside chunk c (single sequence, so the chunk starts at token
+  // c.t0 of it): the row of the last token before the capture, else -1.
+  auto cap_row_of = [&](const ScanChunk& c) -> int {
+    return (a.capture_state && a.capture > c.t0 && a.capture <= c.t0 + c.n) ? (int)(a.capture - 1 - c.t0) : -1;
+  };
+
+  if (warp == 9) {
+    if (lane == 0) {
+      int k = 0, last[2] = {-1, -1};
+      bool ok = true;
+      for (int item = blockIdx.x; item < npairs && ok; item += gridDim.x) {
+        const int s = p.order[item / a.Hv], h = item % a.Hv;
+        const ScanSeq sq = p.seqs[s];
+        for (int ci = 0; ci < sq.nchunks; ++ci, ++k) {
+          const int st = k & 1;
+          if (k >= 2 && !(ok = wait(&empty[st], ((k >> 1) - 1) & 1))) break;
+          const int64_t gc = sq.chunk0 + ci;
+          uint8_t* dst = sm + st * TC_STAGE;
+          mbar_expect_tx(&full[st], KQ_IMG + TP_IMG);
+          bulk_load(dst, p.kq_img + (gc * a.Hk + h / rep) * (int64_t)KQ_IMG, KQ_IMG, &full[st]);
+          bulk_load(dst + KQ_IMG, p.tp_img + (gc * a.Hv + h) * (int64_t)TP_IMG, TP_IMG, &full[st]);
+          last[st] = k;
+        }
+      }
+      if (!ok) {
+        // Let the copies already issued land before the CTA exits (bounded).
+        for (int i = 0; i < 2; ++i)
+          if (last[i] >= 0) mbar_wait(&full[i], (last[i] >> 1) & 1);
+      }
+    }
+  } else if (warp == 8) {
+    if (lane == 0) {
+      constexpr uint32_t id64 = idesc_bf16_f32(128, 64);
+      constexpr uint32_t id128mn = idesc_bf16_f32_bmn(128, 128);
+      auto sa = [&](bool lo, int t) { return tmem + TC_SA + (lo ? 64 : 0) + 8 * t; };
+      int k = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < npairs && ok; item += gridDim.x) {
+        const ScanSeq sq = p.seqs[p.order[item / a.Hv]];
+        for (int ci = 0; ci < sq.nchunks; ++ci, ++k) {
+          const int st = k & 1;
+          const uint32_t kq = sbase + st * TC_STAGE, tp = kq + KQ_IMG;
+          const int cap_row = cap_row_of(p.chunks[sq.chunk0 + ci]);
+          // K (rows 0..63 of the [K; Q] image) as the B operand of R, or of O1 with the Q rows.
+          auto kq_desc = [&](uint32_t rows) {
+            return [=](bool lo, int t) {
+              return desc_k_sw128(rows + (lo ? GRAM_TILE : 0) + (t >> 2) * (128 * 128) + (t & 3) * 32);
+            };
+          };
+          // K read MN-major for the state update: rows are tokens, 64-wide dk atoms 16 KB apart.
+          auto k_mn = [=](bool lo, int t) {
+            return desc_mn_sw128(kq + (lo ? GRAM_TILE : 0) + t * (16 * 128), 128 * 128, 1024);
+          };
+          if (!(ok = wait(&full[st], (k >> 1) & 1) && wait(a_bar, k & 1))) break;
+          tc_fence_after();
+          tc_mma3<8>(tmem + TC_R, sa, id64, kq_desc(kq), false);
+          umma_commit(r_bar);
+          if (!(ok = wait(c_bar, k & 1))) break;
+          tc_fence_after();
+          tc_mma3<4>(tmem + TC_D, [&](bool lo, int t) { return tok_col(tmem + TC_R, lo, t); }, id64,
+                     [&](bool lo, int t) { return desc_k_sw128(tp + (lo ? SQ_BYTES : 0) + t * 32); }, false);
+          umma_commit(d_bar);
+          tc_mma3<8>(tmem + TC_O1, sa, id64, kq_desc(kq + 64 * 128), false);
+          if (!(ok = wait(e_bar, k & 1))) break;
+          tc_fence_after();
+          if (cap_row >= 0) {
+            // The captured state first (into S^T, which holds e^{G_c} S^T);
+            // the carried update once the warps have read it and restored S^T.
+            tc_mma3<4>(tmem + TC_S, [&](bool lo, int t) { return tok_col(tmem + TC_O2, lo, t); }, id128mn, k_mn,
+                       true);
+            umma_commit(cap_bar);
+            if (!(ok = wait(capd_bar, 0))) break;
+            tc_fence_after();
+          }
+          tc_mma3<4>(tmem + TC_S, [&](bool lo, int t) { return tok_col(tmem + TC_R, lo, t); }, id128mn, k_mn, true);
+          umma_commit(i_bar);
+          tc_mma3<4>(tmem + TC_O2, [&](bool lo, int t) { return tok_col(tmem + TC_D, lo, t); }, id64,
+                     [&](bool lo, int t) { return desc_k_sw128(tp + (lo ? 3 : 2) * SQ_BYTES + t * 32); }, false);
+          umma_commit(f_bar);
+          umma_commit(&empty[st]);
+        }
+      }
+      if (!ok) {
+        // Wait (bounded) for the MMAs already issued before TMEM is released.
+        umma_commit(drain);
+        mbar_wait(drain, 0);
+      }
+    }
+  } else {
+    const int q = warp & 3, hf = warp >> 2;
+    const int row = q * 32 + lane;  // dv
+    const uint32_t lq = tmem + ((uint32_t)(q * 32) << 16);
+    const int64_t tstride = (int64_t)a.Hv * DV;  // floats between tokens of v and out
+    // Waits end warp-uniformly: the TMEM accesses after them are .sync.aligned.
+    auto wait_all = [&](uint64_t* b, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, wait(b, parity));
+    };
+    auto arrive = [&](uint64_t* b) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(b);
+    };
+    // This thread's 32 token values of a token-indexed operand, split.
+    auto put_tok = [&](uint32_t col, const float (&v)[32]) {
+      uint32_t hi[16], lo[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) split_pair(v[2 * j], v[2 * j + 1], hi[j], lo[j]);
+      tmem_st_32x32b_x16(lq + col + 32 * hf, hi);
+      tmem_st_32x32b_x16(lq + col + 32 * hf + 16, lo);
+    };
+    // 32 dk columns of S^T (F32 bits) split into the state operand.
+    auto put_sa = [&](int half, const uint32_t (&x)[32]) {
+      uint32_t hi[16], lo[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        split_pair(__uint_as_float(x[2 * j]), __uint_as_float(x[2 * j + 1]), hi[j], lo[j]);
+      tmem_st_32x32b_x16(lq + TC_SA + 32 * hf + 16 * half, hi);
+      tmem_st_32x32b_x16(lq + TC_SA + 64 + 32 * hf + 16 * half, lo);
+    };
+    // g: O^T = (S^T Q^T) diag(e^G) + D^T P^T of chunk c (CTA chunk kc, stage stc).
+    auto do_g = [&](const ScanChunk& c, int stc, int kc, int h) -> bool {
+      if (!wait_all(f_bar, kc & 1)) return false;
+      tc_fence_after();
+      uint32_t o1[32], o2[32];
+      tmem_ld_32x32b_x32(lq + TC_O1 + 32 * hf, o1);
+      tmem_ld_32x32b_x32(lq + TC_O2 + 32 * hf, o2);
+      tmem_ld_wait();
+      const float* eg = reinterpret_cast<const float*>(sm + stc * TC_STAGE + KQ_IMG + TP_TILES) + 32 * hf;
+      const int nmine = c.n - 32 * hf;
+      float* op = a.out + ((c.t0 + 32 * hf) * a.Hv + h) * DV + row;
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < nmine) op[i * tstride] = eg[i] * __uint_as_float(o1[i]) + __uint_as_float(o2[i]);
+      arrive(&empty[stc]);
+      return true;
+    };
+    int k = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < npairs && ok; item += gridDim.x) {
+      const int s = p.order[item / a.Hv], h = item % a.Hv;
+      const ScanSeq sq = p.seqs[s];
+      ScanChunk prev;  // the chunk whose output step is still to do
+      int st_prev = 0;
+      for (int ci = 0; ci < sq.nchunks; ++ci, ++k) {
+        const int st = k & 1;
+        const ScanChunk ch = p.chunks[sq.chunk0 + ci];
+        const int cap_row = cap_row_of(ch);
+        // a: S^T of this chunk (the initial state at the first chunk), split.
+        if (ci == 0) {
+          const float* init = init_for(a, s, h);
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint32_t x[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              x[j] = init ? __float_as_uint(init[(int64_t)(64 * hf + 32 * half + j) * DV + row]) : 0u;
+            tmem_st_32x32b_x32(lq + TC_S + 64 * hf + 32 * half, x);
+            put_sa(half, x);
+          }
+        } else {
+          if (!(ok = wait_all(i_bar, (k - 1) & 1))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint32_t x[32];
+            tmem_ld_32x32b_x32(lq + TC_S + 64 * hf + 32 * half, x);
+            tmem_ld_wait();
+            put_sa(half, x);
+          }
+        }
+        tmem_st_wait();
+        arrive(a_bar);
+        // This chunk's V^T row (tokens [32 hf, 32 hf + 32)), in flight during
+        // the R product and the previous chunk's output step.
+        const int nmine = ch.n - 32 * hf;  // valid tokens of this half
+        float vr[32];
+        {
+          const float* vp = a.v + ((ch.t0 + 32 * hf) * a.Hv + h) * DV + row;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) vr[i] = i < nmine ? vp[i * tstride] : 0.f;
+        }
+        if (ci > 0 && !(ok = do_g(prev, st_prev, k - 1, h))) break;
+        if (!(ok = wait_all(&full[st], (k >> 1) & 1))) break;
+        const float* vec = reinterpret_cast<const float*>(sm + st * TC_STAGE + KQ_IMG + TP_TILES);
+        // c: R^T = V^T - (S^T K^T) diag(e^G), split in place.
+        if (!(ok = wait_all(r_bar, k & 1))) break;
+        tc_fence_after();
+        {
+          uint32_t x[32];
+          tmem_ld_32x32b_x32(lq + TC_R + 32 * hf, x);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) vr[i] -= vec[32 * hf + i] * __uint_as_float(x[i]);
+          put_tok(TC_R, vr);
+          tmem_st_wait();
+        }
+        arrive(c_bar);
+        // e: D^T split in place; D^T diag(egd) split into the R columns (free
+        // since the D product read X_R); S^T <- e^{G_last} S^T for the update.
+        if (!(ok = wait_all(d_bar, k & 1))) break;
+        tc_fence_after();
+        {
+          float d[32], w[32];
+          {
+            uint32_t x[32];
+            tmem_ld_32x32b_x32(lq + TC_D + 32 * hf, x);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) d[i] = __uint_as_float(x[i]);
+          }
+          put_tok(TC_D, d);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) w[i] = d[i] * vec[64 + 32 * hf + i];
+          put_tok(TC_R, w);
+          if (cap_row >= 0) {
+            // X_D'' = split D^T diag(e^{G_c - G_j} [j <= c]) into the O2
+            // columns (the previous chunk's O2 is read, this chunk's not formed).
+            const double* G = reinterpret_cast<const double*>(vec + 192);
+            const double gc = G[cap_row];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int j = 32 * hf + i;
+              w[i] = j <= cap_row ? d[i] * expf((float)(gc - G[j])) : 0.f;
+            }
+            put_tok(TC_O2, w);
+          }
+        }
+        const float el = vec[128];
+        if (cap_row < 0) {
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint32_t x[32];
+            tmem_ld_32x32b_x32(lq + TC_S + 64 * hf + 32 * half, x);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) x[j] = __float_as_uint(el * __uint_as_float(x[j]));
+            tmem_st_32x32b_x32(lq + TC_S + 64 * hf + 32 * half, x);
+          }
+          tmem_st_wait();
+          arrive(e_bar);
+        } else {
+          // S_c = e^{G_c} S^T + X_D''^T K is formed in the S^T columns, read
+          // out, and S^T <- e^{G_last} S^T restored for the carried update,
+          // so the carried state does not depend on whether a capture was
+          // asked for.
+          // This thread's entries of S^T wait in its own entries of the
+          // capture buffer meanwhile.
+          const float ec = expf((float)reinterpret_cast<const double*>(vec + 192)[cap_row]);
+          float* dst = a.capture_state + (int64_t)h * DK * DV;
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint32_t x[32];
+            tmem_ld_32x32b_x32(lq + TC_S + 64 * hf + 32 * half, x);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              dst[(int64_t)(64 * hf + 32 * half + j) * DV + row] = __uint_as_float(x[j]);
+              x[j] = __float_as_uint(ec * __uint_as_float(x[j]));
+            }
+            tmem_st_32x32b_x32(lq + TC_S + 64 * hf + 32 * half, x);
+          }
+          tmem_st_wait();
+          arrive(e_bar);
+          if (!(ok = wait_all(cap_bar, 0))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint32_t x[32], y[32];
+            tmem_ld_32x32b_x32(lq + TC_S + 64 * hf + 32 * half, x);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              float* e = dst + (int64_t)(64 * hf + 32 * half + j) * DV + row;
+              y[j] = __float_as_uint(el * *e);
+              *e = __uint_as_float(x[j]);
+            }
+            tmem_st_32x32b_x32(lq + TC_S + 64 * hf + 32 * half, y);
+          }
+          tmem_st_wait();
+          arrive(capd_bar);
+        }
+        prev = ch;
+        st_prev = st;
+      }
+      if (!ok) break;
+      // Final state (S^T after the last chunk's update), then the last
+      // chunk's output step.
+      if (!(ok = wait_all(i_bar, (k - 1) & 1))) break;
+      tc_fence_after();
+      if (a.final_state) {
+        float* dst = a.final_state + ((int64_t)s * a.Hv + h) * DK * DV;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t x[32];
+          tmem_ld_32x32b_x32(lq + TC_S + 64 * hf + 32 * half, x);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) dst[(int64_t)(64 * hf + 32 * half + j) * DV + row] = __uint_as_float(x[j]);
+        }
+      }
+      if (!(ok = do_g(prev, st_prev, k - 1, h))) break;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
 }
 
 }  // namespace
@@ -968,8 +1368,8 @@ int set_attrs() {
     CLEF_CUDA(cudaFuncSetAttribute(delta_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
     CLEF_CUDA(cudaFuncSetAttribute(delta_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    PREP_SMEM));
-    CLEF_CUDA(cudaFuncSetAttribute(delta_carry_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   CARRY_SMEM));
+    CLEF_CUDA(cudaFuncSetAttribute(delta_carry_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   TC_SMEM));
     g_attr_set[dev] = true;
   }
   return CLEF_OK;
@@ -1045,13 +1445,13 @@ int launch_delta_scan_planned(const ScanPlan& plan, const float* q, const float*
   p.order = reinterpret_cast<const int32_t*>(base + l.order_off);
   delta_prep_kernel<<<dim3((unsigned)plan.nchunks, (unsigned)plan.Hk), THREADS, PREP_SMEM, s>>>(p);
   RC_(launch_status("delta_prep"));
-  // Few (sequence, head) pairs: split their value rows over 2 or 4 CTAs.
   int dev = 0;
   CLEF_CUDA(cudaGetDevice(&dev));
   const int64_t pairs = (int64_t)plan.nseq * plan.Hv;
-  const int split = pairs * 2 <= num_sms(dev) ? 4 : (pairs <= num_sms(dev) ? 2 : 1);
-  delta_carry_kernel<<<dim3((unsigned)pairs, (unsigned)split), THREADS / split, CARRY_SMEM, s>>>(p);
-  return launch_status("delta_carry");
+  // Persistent tcgen05 carry: one CTA per SM at most.
+  const int grid = (int)std::min<int64_t>(pairs, num_sms(dev));
+  delta_carry_tc_kernel<<<grid, TC_THREADS, TC_SMEM, s>>>(p, (int)pairs);
+  return launch_status("delta_carry_tc");
 }
 
 // Fused single-pass path with the offsets already on the device (null = one

@@ -184,6 +184,56 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// Stores: thread i of the warp writes TMEM lane (base lane + i), columns
+// [col, col + 32) or [col, col + 16).
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+      "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+      "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]));
+}
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]));
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy reads (tensor core, bulk copies).
+__device__ __forceinline__ void fence_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// D(tmem) (+)= A(tmem) * B(smem desc)^T, kind::f16, M = 128: A row m is TMEM
+// lane m, its K elements packed two BF16 per 32-bit column (even k in the low
+// half), K = 16 per instruction = 8 columns from `a_tmem`.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// Contiguous global -> shared bulk copy (no tensor map, no multicast);
+// completion counted in bytes on `bar`. Both addresses 16-byte aligned,
+// `bytes` a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
 
 // Shared-memory matrix descriptor for a K-major operand tile stored with the
 // 128-byte swizzle (rows of 64 BF16, 8-row groups 1024 bytes apart):
@@ -199,6 +249,20 @@ __device__ __forceinline__ uint64_t desc_k_sw128(uint32_t saddr) {
   return d;
 }
 
+// Shared-memory matrix descriptor for an MN-major operand stored with the
+// 128-byte swizzle: 64 consecutive MN elements per 128-byte row, one row per
+// K index, 8-row K groups `sbo` bytes apart and 64-wide MN atoms `lbo` bytes
+// apart.
+__device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFF) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
 // Instruction descriptor, kind::f16: F32 accumulator, BF16 A and B, both
 // K-major, shape M x N.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
@@ -207,6 +271,10 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
          | (1u << 10)            // b_format = BF16
          | ((uint32_t)(N >> 3) << 17)
          | ((uint32_t)(M >> 4) << 24);
+}
+// The same with B MN-major (transpose-B bit 16).
+__host__ __device__ constexpr uint32_t idesc_bf16_f32_bmn(int M, int N) {
+  return idesc_bf16_f32(M, N) | (1u << 16);
 }
 
 }  // namespace sm100

@@ -915,7 +915,7 @@ namespace {
 //   [128, 256)  S^T split: hi [128, 192), lo [192, 256)
 //   [256, 320)  R^T = S^T K^T, then X_R (R split in place), then X_D' (split
 //               D^T diag(egd))
-//   [320, 384)  O1 = S^T Q^T
+//   [320, 384)  O1 = S^T Q^T (one N = 128 product with R)
 //   [384, 448)  D^T = X_R (T diag beta)^T, then X_D (D split in place)
 //   [448, 512)  O2 = X_D P^T (a capture chunk first holds X_D'' there)
 // Token-indexed operands (X_R, X_D, X_D', X_D''): warp half hf writes its 32
@@ -923,13 +923,13 @@ namespace {
 // warp only rewrites columns it has read; K step t (tokens 16t .. 16t + 15)
 // starts at column base + 32 (t / 2) + 8 (t % 2), +16 for lo.
 // Per chunk k (E = epilogue warps, M = MMA issuer):
-//   E a   split S^T -> [128, 256)                           -> a_bar
-//   M     R = S^T K^T                                       -> r_bar
-//   E     output step g of chunk k - 1 (O1, O2 of k - 1)    -> stage k - 1 free
+//   E a   O1 of chunk k - 1 out; split S^T -> [128, 256);
+//         S^T <- e^{G_last} S^T ahead of its update         -> a_bar
+//   M     [R | O1] = S^T [K; Q]^T                           -> r_bar
 //   E c   R <- V^T - R diag(e^G); split in place            -> c_bar
-//   M     D = X_R (T diag beta)^T -> d_bar; O1 = S^T Q^T
-//   E e   split D in place; X_D' = split D diag(egd);
-//         S^T <- e^{G_last} S^T                             -> e_bar
+//   M     D = X_R (T diag beta)^T                           -> d_bar
+//   E g   outputs of chunk k - 1 (O1 read in step a)       -> stage k - 1 free
+//   E e   X_D' = split D diag(egd); split D in place        -> e_bar
 //   M     S^T += X_D' K -> i_bar; O2 = X_D P^T -> f_bar, stage k free
 // ---------------------------------------------------------------------------
 constexpr int TC_STAGE = 100352;  // one chunk's K/Q and T/P images, 1024-aligned
@@ -1058,6 +1058,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) delta_carry_tc_kernel(PipeArgs 
   } else if (warp == 8) {
     if (lane == 0) {
       constexpr uint32_t id64 = idesc_bf16_f32(128, 64);
+      constexpr uint32_t id128 = idesc_bf16_f32(128, 128);
       constexpr uint32_t id128mn = idesc_bf16_f32_bmn(128, 128);
       auto sa = [&](bool lo, int t) { return tmem + TC_SA + (lo ? 64 : 0) + 8 * t; };
       int k = 0;
@@ -1068,11 +1069,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) delta_carry_tc_kernel(PipeArgs 
           const int st = k & 1;
           const uint32_t kq = sbase + st * TC_STAGE, tp = kq + KQ_IMG;
           const int cap_row = cap_row_of(p.chunks[sq.chunk0 + ci]);
-          // K (rows 0..63 of the [K; Q] image) as the B operand of R, or of O1 with the Q rows.
-          auto kq_desc = [&](uint32_t rows) {
-            return [=](bool lo, int t) {
-              return desc_k_sw128(rows + (lo ? GRAM_TILE : 0) + (t >> 2) * (128 * 128) + (t & 3) * 32);
-            };
+          // The [K; Q] image (128 rows) as the B operand of [R | O1] = S^T [K; Q]^T.
+          auto kq_desc = [=](bool lo, int t) {
+            return desc_k_sw128(kq + (lo ? GRAM_TILE : 0) + (t >> 2) * (128 * 128) + (t & 3) * 32);
           };
           // K read MN-major for the state update: rows are tokens, 64-wide dk atoms 16 KB apart.
           auto k_mn = [=](bool lo, int t) {
@@ -1080,14 +1079,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) delta_carry_tc_kernel(PipeArgs 
           };
           if (!(ok = wait(&full[st], (k >> 1) & 1) && wait(a_bar, k & 1))) break;
           tc_fence_after();
-          tc_mma3<8>(tmem + TC_R, sa, id64, kq_desc(kq), false);
+          tc_mma3<8>(tmem + TC_R, sa, id128, kq_desc, false);
           umma_commit(r_bar);
-          if (!(ok = wait(c_bar, k & 1))) break;
+          // D overwrites the columns O2 of the previous chunk read (X_D).
+          if (!(ok = wait(c_bar, k & 1) && (k == 0 || wait(f_bar, (k - 1) & 1)))) break;
           tc_fence_after();
           tc_mma3<4>(tmem + TC_D, [&](bool lo, int t) { return tok_col(tmem + TC_R, lo, t); }, id64,
                      [&](bool lo, int t) { return desc_k_sw128(tp + (lo ? SQ_BYTES : 0) + t * 32); }, false);
           umma_commit(d_bar);
-          tc_mma3<8>(tmem + TC_O1, sa, id64, kq_desc(kq + 64 * 128), false);
           if (!(ok = wait(e_bar, k & 1))) break;
           tc_fence_after();
           if (cap_row >= 0) {
@@ -1127,11 +1126,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) delta_carry_tc_kernel(PipeArgs 
       __syncwarp();
       if (lane == 0) mbar_arrive(b);
     };
-    // This thread's 32 token values of a token-indexed operand, split.
-    auto put_tok = [&](uint32_t col, const float (&v)[32]) {
+    // This thread's 32 token values val(0..31) of a token-indexed operand, split.
+    auto put_tok = [&](uint32_t col, auto val) {
       uint32_t hi[16], lo[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) split_pair(v[2 * j], v[2 * j + 1], hi[j], lo[j]);
+      for (int j = 0; j < 16; ++j) split_pair(val(2 * j), val(2 * j + 1), hi[j], lo[j]);
       tmem_st_32x32b_x16(lq + col + 32 * hf, hi);
       tmem_st_32x32b_x16(lq + col + 32 * hf + 16, lo);
     };
@@ -1144,20 +1143,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1) delta_carry_tc_kernel(PipeArgs 
       tmem_st_32x32b_x16(lq + TC_SA + 32 * hf + 16 * half, hi);
       tmem_st_32x32b_x16(lq + TC_SA + 64 + 32 * hf + 16 * half, lo);
     };
-    // g: O^T = (S^T Q^T) diag(e^G) + D^T P^T of chunk c (CTA chunk kc, stage stc).
-    auto do_g = [&](const ScanChunk& c, int stc, int kc, int h) -> bool {
-      if (!wait_all(f_bar, kc & 1)) return false;
-      tc_fence_after();
-      uint32_t o1[32], o2[32];
-      tmem_ld_32x32b_x32(lq + TC_O1 + 32 * hf, o1);
-      tmem_ld_32x32b_x32(lq + TC_O2 + 32 * hf, o2);
+    // This thread's O1 = S^T Q^T of the chunk in stage stc, times e^G.
+    auto read_o1 = [&](int stc, float (&o1s)[32]) {
+      uint32_t y[32];
+      tmem_ld_32x32b_x32(lq + TC_O1 + 32 * hf, y);
       tmem_ld_wait();
       const float* eg = reinterpret_cast<const float*>(sm + stc * TC_STAGE + KQ_IMG + TP_TILES) + 32 * hf;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o1s[i] = eg[i] * __uint_as_float(y[i]);
+    };
+    // g: O^T = (S^T Q^T) diag(e^G) + D^T P^T of chunk c (CTA chunk kc, stage
+    // stc), the first term read earlier into o1s.
+    auto do_g = [&](const ScanChunk& c, int stc, int kc, int h, const float (&o1s)[32]) -> bool {
+      if (!wait_all(f_bar, kc & 1)) return false;
+      tc_fence_after();
+      uint32_t o2[32];
+      tmem_ld_32x32b_x32(lq + TC_O2 + 32 * hf, o2);
+      tmem_ld_wait();
       const int nmine = c.n - 32 * hf;
       float* op = a.out + ((c.t0 + 32 * hf) * a.Hv + h) * DV + row;
 #pragma unroll
       for (int i = 0; i < 32; ++i)
-        if (i < nmine) op[i * tstride] = eg[i] * __uint_as_float(o1[i]) + __uint_as_float(o2[i]);
+        if (i < nmine) op[i * tstride] = o1s[i] + __uint_as_float(o2[i]);
       arrive(&empty[stc]);
       return true;
     };
@@ -1172,33 +1179,42 @@ __global__ void __launch_bounds__(TC_THREADS, 1) delta_carry_tc_kernel(PipeArgs 
         const int st = k & 1;
         const ScanChunk ch = p.chunks[sq.chunk0 + ci];
         const int cap_row = cap_row_of(ch);
-        // a: S^T of this chunk (the initial state at the first chunk), split.
-        if (ci == 0) {
-          const float* init = init_for(a, s, h);
+        // a: S^T of this chunk (the initial state at the first chunk), split,
+        // and S^T <- e^{G_last} S^T ahead of its update (a capture chunk keeps
+        // S^T unscaled until step e). Before it, O1 of the previous chunk is
+        // taken out of its columns, which the next product overwrites.
+        if (!(ok = wait_all(&full[st], (k >> 1) & 1))) break;
+        const float* vec = reinterpret_cast<const float*>(sm + st * TC_STAGE + KQ_IMG + TP_TILES);
+        float o1s[32];
+        const float* init = ci == 0 ? init_for(a, s, h) : nullptr;
+        if (ci > 0) {
+          if (!(ok = wait_all(i_bar, (k - 1) & 1))) break;
+          tc_fence_after();
+          read_o1(st_prev, o1s);
+        }
+        const float f = cap_row < 0 ? vec[128] : 1.f;
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            uint32_t x[32];
+        for (int half = 0; half < 2; ++half) {
+          uint32_t x[32];
+          if (ci == 0) {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
               x[j] = init ? __float_as_uint(init[(int64_t)(64 * hf + 32 * half + j) * DV + row]) : 0u;
-            tmem_st_32x32b_x32(lq + TC_S + 64 * hf + 32 * half, x);
-            put_sa(half, x);
-          }
-        } else {
-          if (!(ok = wait_all(i_bar, (k - 1) & 1))) break;
-          tc_fence_after();
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            uint32_t x[32];
+          } else {
             tmem_ld_32x32b_x32(lq + TC_S + 64 * hf + 32 * half, x);
             tmem_ld_wait();
-            put_sa(half, x);
+          }
+          put_sa(half, x);
+          if (cap_row < 0 || ci == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) x[j] = __float_as_uint(f * __uint_as_float(x[j]));
+            tmem_st_32x32b_x32(lq + TC_S + 64 * hf + 32 * half, x);
           }
         }
         tmem_st_wait();
         arrive(a_bar);
         // This chunk's V^T row (tokens [32 hf, 32 hf + 32)), in flight during
-        // the R product and the previous chunk's output step.
+        // the [R | O1] product.
         const int nmine = ch.n - 32 * hf;  // valid tokens of this half
         float vr[32];
         {
@@ -1206,9 +1222,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) delta_carry_tc_kernel(PipeArgs 
 #pragma unroll
           for (int i = 0; i < 32; ++i) vr[i] = i < nmine ? vp[i * tstride] : 0.f;
         }
-        if (ci > 0 && !(ok = do_g(prev, st_prev, k - 1, h))) break;
-        if (!(ok = wait_all(&full[st], (k >> 1) & 1))) break;
-        const float* vec = reinterpret_cast<const float*>(sm + st * TC_STAGE + KQ_IMG + TP_TILES);
         // c: R^T = V^T - (S^T K^T) diag(e^G), split in place.
         if (!(ok = wait_all(r_bar, k & 1))) break;
         tc_fence_after();
@@ -1218,51 +1231,35 @@ __global__ void __launch_bounds__(TC_THREADS, 1) delta_carry_tc_kernel(PipeArgs 
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 32; ++i) vr[i] -= vec[32 * hf + i] * __uint_as_float(x[i]);
-          put_tok(TC_R, vr);
+          put_tok(TC_R, [&](int i) { return vr[i]; });
           tmem_st_wait();
         }
         arrive(c_bar);
-        // e: D^T split in place; D^T diag(egd) split into the R columns (free
-        // since the D product read X_R); S^T <- e^{G_last} S^T for the update.
+        // The previous chunk's outputs while the D product runs.
+        if (ci > 0 && !(ok = do_g(prev, st_prev, k - 1, h, o1s))) break;
+        // e: D^T diag(egd) split into the R columns (free since the D product
+        // read X_R), then D^T split in place.
         if (!(ok = wait_all(d_bar, k & 1))) break;
         tc_fence_after();
         {
-          float d[32], w[32];
-          {
-            uint32_t x[32];
-            tmem_ld_32x32b_x32(lq + TC_D + 32 * hf, x);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) d[i] = __uint_as_float(x[i]);
-          }
-          put_tok(TC_D, d);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) w[i] = d[i] * vec[64 + 32 * hf + i];
-          put_tok(TC_R, w);
+          uint32_t x[32];
+          tmem_ld_32x32b_x32(lq + TC_D + 32 * hf, x);
+          tmem_ld_wait();
+          put_tok(TC_R, [&](int i) { return __uint_as_float(x[i]) * vec[64 + 32 * hf + i]; });
           if (cap_row >= 0) {
             // X_D'' = split D^T diag(e^{G_c - G_j} [j <= c]) into the O2
             // columns (the previous chunk's O2 is read, this chunk's not formed).
             const double* G = reinterpret_cast<const double*>(vec + 192);
             const double gc = G[cap_row];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
+            put_tok(TC_O2, [&](int i) {
               const int j = 32 * hf + i;
-              w[i] = j <= cap_row ? d[i] * expf((float)(gc - G[j])) : 0.f;
-            }
-            put_tok(TC_O2, w);
+              return j <= cap_row ? __uint_as_float(x[i]) * expf((float)(gc - G[j])) : 0.f;
+            });
           }
+          put_tok(TC_D, [&](int i) { return __uint_as_float(x[i]); });
         }
         const float el = vec[128];
         if (cap_row < 0) {
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            uint32_t x[32];
-            tmem_ld_32x32b_x32(lq + TC_S + 64 * hf + 32 * half, x);
-            tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 32; ++j) x[j] = __float_as_uint(el * __uint_as_float(x[j]));
-            tmem_st_32x32b_x32(lq + TC_S + 64 * hf + 32 * half, x);
-          }
           tmem_st_wait();
           arrive(e_bar);
         } else {
@@ -1325,7 +1322,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) delta_carry_tc_kernel(PipeArgs 
           for (int j = 0; j < 32; ++j) dst[(int64_t)(64 * hf + 32 * half + j) * DV + row] = __uint_as_float(x[j]);
         }
       }
-      if (!(ok = do_g(prev, st_prev, k - 1, h))) break;
+      float o1s[32];
+      read_o1(st_prev, o1s);
+      if (!(ok = do_g(prev, st_prev, k - 1, h, o1s))) break;
     }
   }
   tc_fence_before();

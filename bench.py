@@ -63,6 +63,8 @@ def parse():
                              "prologue", "head"],
                     help="run one operator on a profiling-sized case and exit (for ncu)")
     ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--scan-seqs", type=int, default=64,
+                    help="--profile-op scan: number of 1024-token sequences (ncu captures use 16)")
     return ap.parse_args()
 
 
@@ -347,7 +349,8 @@ def profile_op(args):
         else:
             timed(f"gemm_swiglu {M}x{N}x{K}", lambda: cb.gemm_swiglu(x, w, w2, out=out))
     elif args.profile_op in ("scan", "scan1"):
-        T, cu = (65536, np.arange(0, 65537, 1024, dtype=np.int64)) if args.profile_op == "scan" \
+        n = args.scan_seqs
+        T, cu = (1024 * n, np.arange(0, 1024 * n + 1, 1024, dtype=np.int64)) if args.profile_op == "scan" \
             else (1024, None)
         inp = workloads.delta_operator_inputs(T=T, seed=1)
         qs, ks = workloads.scan_operands(inp)

@@ -778,10 +778,13 @@ constexpr int TP_IMG = TP_TILES + VEC_BYTES;              // 34048 bytes
 constexpr int KQ_IMG = 4 * KQ_BYTES;                      // 65536 bytes
 
 // prep kernel shared layout
+// A, T and the staged P tiles reuse the Gram operand's space once the Gram
+// products have completed: 72 KB per CTA, three CTAs per SM.
 constexpr int P_OFF_KQ = 0;
-constexpr int P_OFF_A = KQ_IMG;
+constexpr int P_OFF_A = 2 * SQ_BYTES;  // after the P hi/lo staging tiles
 constexpr int P_OFF_T = P_OFF_A + C * AP * 4;
-constexpr int P_OFF_M = P_OFF_T + C * AP * 4;
+static_assert(P_OFF_T + C * AP * 4 <= KQ_IMG, "A and T inside the Gram operand's space");
+constexpr int P_OFF_M = KQ_IMG;
 constexpr int PREP_MAX_REP = 4;  // value heads per key head whose gates are staged at once
 constexpr int P_OFF_G = P_OFF_M + 3 * 16 * 17 * 4;
 constexpr int P_OFF_B = P_OFF_G + PREP_MAX_REP * C * 8;
@@ -797,7 +800,7 @@ struct PipeArgs {
   const int32_t* order;  // [nseq] carry order: longest sequences first
 };
 
-__global__ void __launch_bounds__(THREADS, 2) delta_prep_kernel(PipeArgs p) {
+__global__ void __launch_bounds__(THREADS, 3) delta_prep_kernel(PipeArgs p) {
   extern __shared__ __align__(128) uint8_t sm_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>(((uintptr_t)sm_raw + 1023) & ~(uintptr_t)1023);
   const ScanArgs& a = p.a;

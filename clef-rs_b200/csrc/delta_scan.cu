@@ -27,8 +27,9 @@
 // kernel, delta_scan_kernel (one CTA per (sequence, v-head), 8 warps; warp w
 // keeps value rows [16w, 16w+16) of S^T as mma.sync accumulators in registers,
 // re-packed in registers as the A operand of the next product).
-// The triangular inverse T is computed in F32 by blocked forward substitution
-// (four 16 x 16 diagonal blocks, then the off-diagonal blocks).
+// The triangular inverse T is computed by blocked forward substitution: the
+// four 16 x 16 diagonal blocks in F32, then the off-diagonal blocks with the
+// same split-BF16 tensor-core products.
 // A capture point inside a chunk does not change the chunking: the state at
 // the capture token is formed from the same chunk quantities, so a prefill with
 // capture is bit-identical to one without.
@@ -401,7 +402,36 @@ __device__ __forceinline__ void gram_store(const float (&kk)[4][4], const float 
   }
 }
 
-// T = (I + A)^{-1} by blocked forward substitution in F32, then
+// m16n8k16 fragments of F32 tiles in shared memory (leading dimension ld),
+// split into hi/lo BF16: A (16 x 16, row-major) and B (16 x 8, element
+// (k, n) at base[k * ld + n]); g = lane / 4, t = lane % 4.
+__device__ __forceinline__ void frag_a_f32(const float* base, int ld, int lane, uint32_t (&ah)[4],
+                                           uint32_t (&al)[4]) {
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float2 v = *reinterpret_cast<const float2*>(base + (g + (q & 1) * 8) * ld + 2 * t + (q >> 1) * 8);
+    split2(v.x, v.y, ah[q], al[q]);
+  }
+}
+__device__ __forceinline__ void frag_b_f32(const float* base, int ld, int lane, uint32_t (&bh)[2],
+                                           uint32_t (&bl)[2]) {
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int q = 0; q < 2; ++q)
+    split2(base[(2 * t + q * 8) * ld + g], base[(2 * t + 1 + q * 8) * ld + g], bh[q], bl[q]);
+}
+// One n8 accumulator tile (16 x 8) into a shared-memory tile, times `sign`.
+__device__ __forceinline__ void store_c(const float (&c)[4], float* base, int ld, int lane, float sign) {
+  const int g = lane >> 2, t = lane & 3;
+  base[g * ld + 2 * t] = sign * c[0];
+  base[g * ld + 2 * t + 1] = sign * c[1];
+  base[(g + 8) * ld + 2 * t] = sign * c[2];
+  base[(g + 8) * ld + 2 * t + 1] = sign * c[3];
+}
+
+// T = (I + A)^{-1} by blocked forward substitution (diagonal blocks in F32,
+// off-diagonal blocks as split-BF16 mma.sync products), then
 // T diag(beta) split into hi/lo tiles at t_hi / t_lo. Contains block barriers;
 // every thread of the CTA calls it.
 template <bool GLOBAL>
@@ -427,26 +457,29 @@ __device__ __forceinline__ void solve_t(const float* As, float* Ts, float* Ms, c
     if ((j >> 4) > (i >> 4)) Ts[i * AP + j] = 0.f;
   }
   __syncthreads();
-  // Off-diagonal blocks, block row by block row:
-  //   T_bj = -D_b * sum_{k=j}^{b-1} A_bk T_kj.
+  // Off-diagonal blocks, block row by block row, on the tensor cores (split
+  // BF16 operands, F32 accumulation): warp 2j + h forms columns [8h, 8h + 8) of
+  //   M_bj = sum_{k=j}^{b-1} A_bk T_kj,   T_bj = -T_bb M_bj.
   for (int b = 1; b < 4; ++b) {
-    for (int idx = tid; idx < b * 256; idx += nthreads) {
-      const int j = idx >> 8, r = (idx >> 4) & 15, c = idx & 15;
-      float acc = 0.f;
-      for (int kb = j; kb < b; ++kb)
-#pragma unroll
-        for (int q = 0; q < 16; ++q)
-          acc += As[(b * 16 + r) * AP + kb * 16 + q] * Ts[(kb * 16 + q) * AP + j * 16 + c];
-      Ms[(j * 16 + r) * 17 + c] = acc;
-    }
-    __syncthreads();
-    for (int idx = tid; idx < b * 256; idx += nthreads) {
-      const int j = idx >> 8, r = (idx >> 4) & 15, c = idx & 15;
-      float acc = 0.f;
-#pragma unroll
-      for (int q = 0; q <= 15; ++q)
-        acc += Ts[(b * 16 + r) * AP + b * 16 + q] * Ms[(j * 16 + q) * 17 + c];
-      Ts[(b * 16 + r) * AP + j * 16 + c] = -acc;
+    if (warp < 2 * b) {
+      const int j = warp >> 1, nt = warp & 1;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int kb = j; kb < b; ++kb) {
+        uint32_t ah[4], al[4], bh[2], bl[2];
+        frag_a_f32(As + (b * 16) * AP + kb * 16, AP, lane, ah, al);
+        frag_b_f32(Ts + (kb * 16) * AP + j * 16 + nt * 8, AP, lane, bh, bl);
+        mma3(acc, ah, al, bh[0], bh[1], bl[0], bl[1]);
+      }
+      // M_bj goes through this warp's scratch tile (C fragment -> B fragment).
+      float* Mj = Ms + (j * 16) * 17 + nt * 8;
+      store_c(acc, Mj, 17, lane, 1.f);
+      __syncwarp();
+      float t[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t ah[4], al[4], bh[2], bl[2];
+      frag_a_f32(Ts + (b * 16) * AP + b * 16, AP, lane, ah, al);
+      frag_b_f32(Mj, 17, lane, bh, bl);
+      mma3(t, ah, al, bh[0], bh[1], bl[0], bl[1]);
+      store_c(t, Ts + (b * 16) * AP + j * 16 + nt * 8, AP, lane, -1.f);
     }
     __syncthreads();
   }

@@ -149,14 +149,6 @@ __device__ __forceinline__ void ldb_nk(uint32_t base, int n0, int k0, int cpr, i
   const int col = k0 + ((lane >> 3) & 1) * 8;
   ldsm4(base + swz(row, col, cpr), r);
 }
-// B fragments from a row-major [k][n] tile (transposed load): n-tiles n0 and
-// n0+8 at k-step k0.
-__device__ __forceinline__ void ldb_kn(uint32_t base, int n0, int k0, int cpr, int lane,
-                                       uint32_t (&r)[4]) {
-  const int row = k0 + (lane & 7) + (((lane >> 3) & 1) << 3);
-  const int col = n0 + ((lane >> 4) << 3);
-  ldsm4t(base + swz(row, col, cpr), r);
-}
 // A fragments from a row-major [m][k] tile: rows m0..m0+15 at k-step k0.
 __device__ __forceinline__ void lda(uint32_t base, int m0, int k0, int cpr, int lane, uint32_t (&r)[4]) {
   ldsm4(base + swz(m0 + (lane & 15), k0 + (lane >> 4) * 8, cpr), r);
@@ -165,24 +157,24 @@ __device__ __forceinline__ void lda(uint32_t base, int m0, int k0, int cpr, int 
 // Byte offset of element (row, col) of K/Q tile t (0 = K hi, 1 = K lo, 2 = Q hi,
 // 3 = Q lo) of a chunk's K/Q operand. UK: the tcgen05 layout of the workspace
 // image and the prep kernel's Gram operand (hi tile [K; Q] then lo tile, in
-// umma_off order); otherwise four [64][128] tiles in the ldmatrix swizzle.
+// umma_off order); otherwise four [64][128] tiles in the ldmatrix swizzle (the
+// fused kernel's shared-memory tiles).
 template <bool UK>
 __device__ __forceinline__ uint32_t kq_off(int t, int row, int col) {
   if (UK) return (uint32_t)((t & 1) * GRAM_TILE) + umma_off(row + (t >> 1) * 64, col);
   return (uint32_t)(t * KQ_BYTES) + swz(row, col, 16);
 }
-// B fragments of K/Q tile t read as [n][k] (ldb_nk) or as [k][n] (ldb_kn).
-template <bool UK>
+// B fragments of the fused kernel's K/Q tile t for two n-tiles at k-step k0:
+// read as a row-major [n][k] tile (ldb_kq) or, transposed, as [k][n] (ldb_kq_t).
 __device__ __forceinline__ void ldb_kq(uint32_t base, int t, int n0, int k0, int lane, uint32_t (&r)[4]) {
   const int row = n0 + (lane & 7) + ((lane >> 4) << 3);
   const int col = k0 + ((lane >> 3) & 1) * 8;
-  ldsm4(base + kq_off<UK>(t, row, col), r);
+  ldsm4(base + kq_off<false>(t, row, col), r);
 }
-template <bool UK>
 __device__ __forceinline__ void ldb_kq_t(uint32_t base, int t, int n0, int k0, int lane, uint32_t (&r)[4]) {
   const int row = k0 + (lane & 7) + (((lane >> 3) & 1) << 3);
   const int col = n0 + ((lane >> 4) << 3);
-  ldsm4t(base + kq_off<UK>(t, row, col), r);
+  ldsm4t(base + kq_off<false>(t, row, col), r);
 }
 
 // ---------------------------------------------------------------------------
@@ -526,8 +518,8 @@ __device__ __forceinline__ void carry_step(float (&S)[16][4], const float (&Vr)[
 #pragma unroll
     for (int np = 0; np < 4; ++np) {
       uint32_t bh[4], bl[4];
-      ldb_kq<false>(c.kq, 0, np * 16, ks * 16, lane, bh);
-      ldb_kq<false>(c.kq, 1, np * 16, ks * 16, lane, bl);
+      ldb_kq(c.kq, 0, np * 16, ks * 16, lane, bh);
+      ldb_kq(c.kq, 1, np * 16, ks * 16, lane, bl);
       mma3(R[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
       mma3(R[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
     }
@@ -566,8 +558,8 @@ __device__ __forceinline__ void carry_step(float (&S)[16][4], const float (&Vr)[
 #pragma unroll
     for (int np = 0; np < 4; ++np) {
       uint32_t bh[4], bl[4];
-      ldb_kq<false>(c.kq, 2, np * 16, ks * 16, lane, bh);
-      ldb_kq<false>(c.kq, 3, np * 16, ks * 16, lane, bl);
+      ldb_kq(c.kq, 2, np * 16, ks * 16, lane, bh);
+      ldb_kq(c.kq, 3, np * 16, ks * 16, lane, bl);
       mma3(R[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
       mma3(R[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
     }
@@ -622,8 +614,8 @@ __device__ __forceinline__ void carry_step(float (&S)[16][4], const float (&Vr)[
 #pragma unroll
         for (int np = 0; np < 4; ++np) {
           uint32_t bh[4], bl[4];
-          ldb_kq_t<false>(c.kq, 0, half * 64 + np * 16, ks * 16, lane, bh);
-          ldb_kq_t<false>(c.kq, 1, half * 64 + np * 16, ks * 16, lane, bl);
+          ldb_kq_t(c.kq, 0, half * 64 + np * 16, ks * 16, lane, bh);
+          ldb_kq_t(c.kq, 1, half * 64 + np * 16, ks * 16, lane, bl);
           mma3(X[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
           mma3(X[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
         }
@@ -656,8 +648,8 @@ __device__ __forceinline__ void carry_step(float (&S)[16][4], const float (&Vr)[
 #pragma unroll
     for (int np = 0; np < 8; ++np) {
       uint32_t bh[4], bl[4];
-      ldb_kq_t<false>(c.kq, 0, np * 16, ks * 16, lane, bh);
-      ldb_kq_t<false>(c.kq, 1, np * 16, ks * 16, lane, bl);
+      ldb_kq_t(c.kq, 0, np * 16, ks * 16, lane, bh);
+      ldb_kq_t(c.kq, 1, np * 16, ks * 16, lane, bl);
       mma3(S[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
       mma3(S[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
     }

@@ -136,9 +136,9 @@ __global__ void conv4_kernel(const float* __restrict__ x, int64_t ldx, const flo
 // CTA = 256 threads x 4 channels (1024 channels = 8 whole 128-wide heads) over a
 // run of PRO_RUN consecutive tokens. Every thread issues the asynchronous
 // copies of all PRO_RUN + 3 projection rows of its channels (3 rows of conv
-// history) into shared memory up front, one copy group per row, and consumes
-// the rows in order as their groups complete: the whole run is in flight at
-// once without holding it in registers. A warp covers exactly one q/k head and
+// history) into shared memory up front, so the whole run is in flight at once
+// without holding it in registers, then walks the tokens in one rolled loop.
+// Four CTAs per SM (61 registers). A warp covers exactly one q/k head and
 // reduces its L2 norm with shuffles (clef_delta_prepare, pointwise.metal:69-114;
 // l2 and scaling, qwen.rs:837-845). The CTAs of channel block 0 also compute
 // the gates (qwen.rs:619-627).
@@ -191,8 +191,8 @@ __device__ __forceinline__ void cp_async_wait() {
 // the correctly rounded quotient; e^-x overflowing gives -0 for very negative x).
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 
-template <int I, typename V>
-__device__ __forceinline__ void pro_step(const V* __restrict__ rows, const float* __restrict__ hist,
+template <typename V>
+__device__ __forceinline__ void pro_step(const V* __restrict__ rows, int I, const float* __restrict__ hist,
                                          int hist_rows, int width, const float (&tw)[4][4], int64_t t,
                                          int64_t start, int c, int key, int Hv, float qscale,
                                          float* __restrict__ q, float* __restrict__ k,
@@ -233,38 +233,8 @@ __device__ __forceinline__ void pro_step(const V* __restrict__ rows, const float
   }
 }
 
-template <int I>
-struct ProRun {
-  // Token t_begin + I, once copy group I + 3 has landed.
-  template <typename V>
-  __device__ __forceinline__ static void run(const V* rows, const float* hist, int hist_rows,
-                                             int width, const float (&tw)[4][4], int64_t t_begin,
-                                             int64_t t_end, int64_t& start, int64_t& next_start,
-                                             int& s, const int64_t* cu, int c, int key, int Hv,
-                                             float qscale, float* q, float* k, float* v) {
-    const int64_t t = t_begin + I;
-    if (t >= t_end) return;
-    cp_async_wait<PRO_RUN - 1 - I>();
-    if (t == next_start) {  // a new sequence starts: its window holds history or zeros
-      ++s;
-      start = t;
-      next_start = cu[s + 1];
-    }
-    pro_step<I, V>(rows, hist, hist_rows, width, tw, t, start, c, key, Hv, qscale, q, k, v);
-    ProRun<I + 1>::run(rows, hist, hist_rows, width, tw, t_begin, t_end, start, next_start, s, cu, c,
-                       key, Hv, qscale, q, k, v);
-  }
-};
-template <>
-struct ProRun<PRO_RUN> {
-  template <typename V>
-  __device__ __forceinline__ static void run(const V*, const float*, int, int, const float (&)[4][4],
-                                             int64_t, int64_t, int64_t&, int64_t&, int&, const int64_t*,
-                                             int, int, int, float, float*, float*, float*) {}
-};
-
 template <typename In>
-__global__ void __launch_bounds__(256, 3) delta_prologue_kernel(
+__global__ void __launch_bounds__(256, 4) delta_prologue_kernel(
     const In* __restrict__ proj, int64_t ldp, int a_col, int b_col,
     const float* __restrict__ hist, int hist_rows, const float* __restrict__ conv_w,
     const float* __restrict__ dt_bias, const float* __restrict__ a_log,
@@ -284,8 +254,8 @@ __global__ void __launch_bounds__(256, 3) delta_prologue_kernel(
   for (int i = 0; i < PRO_ROWS; ++i) {
     const int64_t r = t_begin - 3 + i;
     if (r >= 0 && r < t_end) cp_async_row(rows + i * 256, proj + r * ldp + c);
-    cp_async_commit();
   }
+  cp_async_commit();
   // Sequence of the first token.
   int s = cu ? (int)seq_of(cu, nseq, t_begin) : 0;
   int64_t start = cu ? cu[s] : 0;
@@ -299,9 +269,18 @@ __global__ void __launch_bounds__(256, 3) delta_prologue_kernel(
                           {w0.y, w1.y, w2.y, w3.y},
                           {w0.z, w1.z, w2.z, w3.z},
                           {w0.w, w1.w, w2.w, w3.w}};
-  ProRun<0>::run<V>(rows, hist, hist_rows, width, tw, t_begin, t_end, start, next_start, s, cu, c, key, Hv,
-                 qscale, q, k, v);
   cp_async_wait<0>();
+#pragma unroll 1
+  for (int i = 0; i < PRO_RUN; ++i) {
+    const int64_t t = t_begin + i;
+    if (t >= t_end) break;
+    if (t == next_start) {  // a new sequence starts: its window holds history or zeros
+      ++s;
+      start = t;
+      next_start = cu[s + 1];
+    }
+    pro_step<V>(rows, i, hist, hist_rows, width, tw, t, start, c, key, Hv, qscale, q, k, v);
+  }
   if (blockIdx.x == 0) {
     for (int idx = threadIdx.x; idx < (t_end - t_begin) * Hv; idx += blockDim.x) {
       const int64_t t = t_begin + idx / Hv;

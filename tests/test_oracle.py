@@ -172,3 +172,45 @@ def test_head_oracle_matches_reference_golden():
     assert len(out) == 3
     for i, o in enumerate(out):
         assert_close(o, z[f"in:logits.{i}"])
+
+
+@pytest.mark.parametrize("T,H", [(1, 2), (31, 2), (64, 1), (65, 2), (139, 2)])
+@pytest.mark.parametrize("decay", [-0.03, -1000.0])
+def test_chunk_form_matches_recurrence(T, H, decay):
+    """The chunked WY/UT algebra the GPU scan evaluates (oracle/chunk_form.py)
+    equals the per-token recurrence on the reference's chunk-test patterns
+    (chunk.rs:182-241 inputs at key = value = 128), decay -1000 included."""
+    from oracle.chunk_form import chunked_scan
+    kd = vd = 128
+    q = (np.sin(np.arange(T * H * kd, dtype=np.float32) * np.float32(0.071)) * np.float32(0.02)).reshape(T, H, kd)
+    k = np.cos(np.arange(T * H * kd, dtype=np.float32) * np.float32(0.037)).reshape(T, H, kd)
+    v = np.sin(np.arange(T * H * vd, dtype=np.float32) * np.float32(0.033)).reshape(T, H, vd)
+    g = np.full((T, H), decay, np.float32)
+    beta = np.full((T, H), 0.65, np.float32)
+    ref_o, ref_s, _ = oracle.delta_recurrence(q, k, v, g, beta)
+    o, s, _ = chunked_scan(q, k, v, g, beta)
+    # F32 recurrence against the float64 chunk form: rounding noise only
+    # (outputs of magnitude ~0.03, observed differences ~3e-8).
+    assert np.abs(o - ref_o).max() < 1e-6
+    assert np.abs(s - ref_s).max() < 1e-6
+
+
+@pytest.mark.parametrize("capture", [1, 16, 63, 64, 65, 128, 140])
+def test_chunk_form_capture_and_gqa(capture):
+    """Captured states inside and at the end of chunks, grouped heads (two value
+    heads per key head), random gates and an initial state."""
+    from oracle.chunk_form import chunked_scan
+    T, hk, hv, kd, vd = 140, 1, 2, 32, 16
+    rng = np.random.default_rng(capture)
+    q = rng.standard_normal((T, hk, kd)).astype(np.float32)
+    k = rng.standard_normal((T, hk, kd)).astype(np.float32)
+    v = rng.standard_normal((T, hv, vd)).astype(np.float32)
+    g = (-np.exp(rng.uniform(-4, 1, (T, hv)))).astype(np.float32)
+    beta = (1 / (1 + np.exp(-rng.standard_normal((T, hv))))).astype(np.float32)
+    s0 = (0.1 * rng.standard_normal((hv, kd, vd))).astype(np.float32)
+    ref_o, ref_s, ref_c = oracle.delta_recurrence(q, k, v, g, beta, state=s0, capture=capture)
+    o, s, c = chunked_scan(q, k, v, g, beta, state=s0, capture=capture)
+    # Magnitudes ~0.2; observed differences below 2e-7.
+    assert np.abs(o - ref_o).max() < 2e-6
+    assert np.abs(s - ref_s).max() < 2e-6
+    assert np.abs(c - ref_c).max() < 2e-6

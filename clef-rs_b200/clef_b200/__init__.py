@@ -37,7 +37,8 @@ EXPORTS = [
     "clef_engine_weight_count", "clef_engine_finalize", "clef_engine_prefill",
     "clef_engine_prefill_device", "clef_engine_launches", "clef_engine_cancel",
     "clef_engine_stage_times", "clef_engine_set_profiling", "clef_engine_destroy",
-    "clef_prefix_tokens", "clef_prefix_bytes", "clef_prefix_destroy", "clef_head_create",
+    "clef_prefix_tokens", "clef_prefix_bytes", "clef_prefix_destroy", "clef_prefix_span_bytes",
+    "clef_prefix_create", "clef_prefix_export", "clef_prefix_import", "clef_head_create",
     "clef_head_set_weight", "clef_head_finalize", "clef_head_forward", "clef_head_destroy",
     "clef_selftest_wait_timeout", "clef_decide",
 ]
@@ -110,6 +111,10 @@ def _load():
         "clef_prefix_tokens": (_i64, [_vp]),
         "clef_prefix_bytes": (ctypes.c_uint64, [_vp]),
         "clef_prefix_destroy": (ctypes.c_int, [_vp]),
+        "clef_prefix_span_bytes": (ctypes.c_uint64, [_vp]),
+        "clef_prefix_create": (ctypes.c_int, [_vp, _i64, ctypes.POINTER(_vp)]),
+        "clef_prefix_export": (ctypes.c_int, [_vp, _vp, ctypes.c_uint64, _vp]),
+        "clef_prefix_import": (ctypes.c_int, [_vp, _vp, ctypes.c_uint64, _vp]),
         "clef_head_create": (ctypes.c_int, [_vp, _i32, ctypes.POINTER(_vp)]),
         "clef_head_set_weight": (ctypes.c_int, [_vp, ctypes.c_char_p, _vp, _i64]),
         "clef_head_finalize": (ctypes.c_int, [_vp]),
@@ -324,6 +329,21 @@ class Prefix:
     def bytes(self) -> int:
         return int(lib.clef_prefix_bytes(self.handle))
 
+    def span_bytes(self) -> int:
+        """Bytes of the prefix's single device allocation."""
+        return int(lib.clef_prefix_span_bytes(self.handle))
+
+    def export_to(self, dst, stream=None) -> None:
+        """Copies the prefix's device allocation into `dst`, a CUDA tensor of
+        span_bytes() bytes on the prefix's device (stream-ordered)."""
+        _check(lib.clef_prefix_export(self.handle, _ptr(dst), dst.numel() * dst.element_size(),
+                                      _stream(stream)))
+
+    def import_from(self, src, stream=None) -> None:
+        """Fills the prefix from a copy made by export_to (stream-ordered)."""
+        _check(lib.clef_prefix_import(self.handle, _ptr(src), src.numel() * src.element_size(),
+                                      _stream(stream)))
+
     def close(self):
         if self.handle and lib is not None:
             lib.clef_prefix_destroy(self.handle)
@@ -414,6 +434,13 @@ class Engine:
 
     def launches(self) -> int:
         return int(lib.clef_engine_launches(self.handle))
+
+    def create_prefix(self, tokens: int) -> Prefix:
+        """An empty prefix of `tokens` tokens with this engine's layout, to be
+        filled by Prefix.import_from."""
+        h = ctypes.c_void_p()
+        _check(lib.clef_prefix_create(self.handle, int(tokens), ctypes.byref(h)))
+        return Prefix(h.value)
 
     def close(self):
         if getattr(self, "handle", None) and lib is not None:

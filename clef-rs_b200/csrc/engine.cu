@@ -72,7 +72,8 @@ struct clef_prefix {
   int hidden = 0;
   int64_t vt_pitch = 0;
   void* blob = nullptr;
-  uint64_t bytes = 0;
+  uint64_t bytes = 0;       // logical state bytes
+  uint64_t span = 0;        // bytes of the device allocation (layout of the engine config)
   float* hidden_rows = nullptr;  // [tokens, hidden]
   struct Layer {
     bool full = false;
@@ -417,6 +418,7 @@ int alloc_prefix(clef_engine* e, int64_t tokens, clef_prefix** out) {
     delete p;
     return fail(CLEF_ERR_NOMEM, "prefix: allocation of " + std::to_string(b) + " bytes");
   }
+  p->span = b;
   char* base = reinterpret_cast<char*>(p->blob);
   int k = 0;
   p->hidden_rows = (float*)(base + o[k++]);
@@ -955,6 +957,34 @@ int clef_engine_destroy(clef_engine* e) {
 }
 
 int64_t clef_prefix_tokens(const clef_prefix* p) { return p ? p->tokens : 0; }
+uint64_t clef_prefix_span_bytes(const clef_prefix* p) { return p ? p->span : 0; }
+
+int clef_prefix_create(clef_engine* e, int64_t tokens, clef_prefix** out) {
+  if (out) *out = nullptr;
+  CLEF_CHECK(e && out, CLEF_ERR_INVALID, "prefix_create: null pointer");
+  CLEF_CHECK(e->finalized, CLEF_ERR_INVALID, "prefix_create: engine not finalized");
+  CLEF_CHECK(tokens > 0, CLEF_ERR_INVALID, "prefix_create: tokens must be positive");
+  DeviceGuard g(e->device);
+  return alloc_prefix(e, tokens, out);
+}
+
+int clef_prefix_export(const clef_prefix* p, void* dst, uint64_t bytes, void* stream) {
+  CLEF_CHECK(p && dst, CLEF_ERR_INVALID, "prefix_export: null pointer");
+  CLEF_CHECK(bytes == p->span, CLEF_ERR_INVALID,
+             "prefix_export: bytes must equal the prefix span (" + std::to_string(p->span) + ")");
+  DeviceGuard g(p->device);
+  CLEF_CUDA(cudaMemcpyAsync(dst, p->blob, bytes, cudaMemcpyDeviceToDevice, as_stream(stream)));
+  return CLEF_OK;
+}
+
+int clef_prefix_import(clef_prefix* p, const void* src, uint64_t bytes, void* stream) {
+  CLEF_CHECK(p && src, CLEF_ERR_INVALID, "prefix_import: null pointer");
+  CLEF_CHECK(bytes == p->span, CLEF_ERR_INVALID,
+             "prefix_import: bytes must equal the prefix span (" + std::to_string(p->span) + ")");
+  DeviceGuard g(p->device);
+  CLEF_CUDA(cudaMemcpyAsync(p->blob, src, bytes, cudaMemcpyDeviceToDevice, as_stream(stream)));
+  return CLEF_OK;
+}
 uint64_t clef_prefix_bytes(const clef_prefix* p) { return p ? p->bytes : 0; }
 int clef_prefix_destroy(clef_prefix* p) {
   if (!p) return CLEF_OK;

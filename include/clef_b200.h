@@ -283,6 +283,22 @@ int64_t clef_prefix_tokens(const clef_prefix* p);
 uint64_t clef_prefix_bytes(const clef_prefix* p);
 int clef_prefix_destroy(clef_prefix* p);
 
+/* Moving a prefix state between devices (no counterpart in the reference,
+ * which serves one device; SURVEY's multi-GPU plan broadcasts the prefix of
+ * config 5 from the rank that computed it instead of recomputing it on every
+ * GPU). A prefix is one device allocation of clef_prefix_span_bytes bytes
+ * whose layout depends only on the engine configuration and the token count:
+ * clef_prefix_export copies it to `dst` (device memory of the prefix's
+ * device, at least that many bytes), clef_prefix_create makes an empty
+ * prefix of `tokens` tokens for engine `e`, and clef_prefix_import fills it
+ * from such a copy (for example after an NCCL broadcast). Both copies are
+ * stream-ordered on `stream` (NULL = default stream); `bytes` must equal the
+ * span. */
+uint64_t clef_prefix_span_bytes(const clef_prefix* p);
+int clef_prefix_create(clef_engine* e, int64_t tokens, clef_prefix** out);
+int clef_prefix_export(const clef_prefix* p, void* dst, uint64_t bytes, void* stream);
+int clef_prefix_import(clef_prefix* p, const void* src, uint64_t bytes, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Learned joint schema head (Head, crates/core/src/models/head.rs:26-274):   */
 /* span means over the record's instruction and option spans, evidence       */

@@ -178,3 +178,15 @@ def test_head_rejects_bad_geometry_before_touching_a_device():
 def test_selftest_rejects_bad_limit_before_launch():
     assert cb.lib.clef_selftest_wait_timeout(0, None) == 1
     assert cb.lib.clef_selftest_wait_timeout(5000, None) == 1
+
+
+def test_prefix_transfer_rejects_before_touching_a_device():
+    lib = cb.lib
+    buf = ctypes.create_string_buffer(16)
+    assert lib.clef_prefix_span_bytes(None) == 0
+    assert lib.clef_prefix_export(None, buf, 16, None) == 1
+    assert "null pointer" in lib.clef_last_error().decode()
+    assert lib.clef_prefix_import(None, buf, 16, None) == 1
+    out = ctypes.c_void_p(0x1)
+    assert lib.clef_prefix_create(None, 16, ctypes.byref(out)) == 1
+    assert out.value is None  # cleared on every path

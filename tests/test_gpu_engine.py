@@ -119,6 +119,36 @@ def test_prefix_capture_and_resume(models, boundary):
     prefix.close()
 
 
+@pytest.mark.parametrize("boundary", [3, 100])
+def test_prefix_moves_through_a_device_copy(models, boundary):
+    """clef_prefix_export / clef_prefix_create / clef_prefix_import (the path of
+    the multi-GPU prefix broadcast): a prefix rebuilt from a copy of another's
+    device allocation continues every suffix bit for bit like the original."""
+    cfg, eng, ref = models
+    seq = ids(200 + 57, 3)
+    _, _, prefix = eng.prefill([seq], capture=boundary)
+    span = prefix.span_bytes()
+    assert span >= prefix.bytes() > 0
+    buf = torch.empty(span, dtype=torch.uint8, device="cuda")
+    prefix.export_to(buf)
+    twin = eng.create_prefix(boundary)
+    assert twin.tokens == boundary and twin.span_bytes() == span
+    twin.import_from(buf)
+    torch.cuda.synchronize()
+    tails = [seq[boundary:], ids(80, 41)]
+    a, ha, _ = eng.prefill(tails[:1], initial=prefix, hidden=True)
+    b, hb, _ = eng.prefill(tails[:1], initial=twin, hidden=True)
+    assert np.array_equal(a, b) and np.array_equal(ha, hb)
+    a, _, _ = eng.prefill(tails, initial=prefix)
+    b, _, _ = eng.prefill(tails, initial=twin)
+    assert np.array_equal(a, b)
+    import clef_b200 as cb
+    with pytest.raises(cb.ClefError, match="span"):
+        twin.import_from(buf[:-16])
+    twin.close()
+    prefix.close()
+
+
 def test_decisions_match_oracle(models):
     import clef_b200 as cb
     cfg, eng, ref = models

@@ -485,26 +485,10 @@ def main():
         reqs = rank_shard(suffixes, rank, world, lambda r: flops_per_request(cfg, len(r), 16384))
         # The prefix state is computed once, on rank 0; the other ranks (same
         # seeded weights) receive its device allocation by one NCCL broadcast.
-        t0 = time.perf_counter()
-        if rank == 0:
-            _, _, prefix = eng.prefill([pre_ids], capture=len(pre_ids), logits=False)
-        else:
-            prefix = eng.create_prefix(len(pre_ids))
-        prefix_ms = 1000 * (time.perf_counter() - t0)
-        if world > 1:
-            buf = torch.empty(prefix.span_bytes(), dtype=torch.uint8, device="cuda")
-            if rank == 0:
-                prefix.export_to(buf)
-            torch.cuda.synchronize()
-            barrier()
-            t1 = time.perf_counter()
-            dist.broadcast(buf, src=0)
-            torch.cuda.synchronize()
-            bcast_ms = 1000 * (time.perf_counter() - t1)
-            if rank != 0:
-                prefix.import_from(buf)
-            torch.cuda.synchronize()
-            del buf
+        from clef_b200.sharding import share_prefix
+        prefix, prefix_ms, bcast_ms = share_prefix(
+            lambda: eng.prefill([pre_ids], capture=len(pre_ids), logits=False)[2],
+            lambda: eng.create_prefix(len(pre_ids)), rank, world, "cuda", torch.cuda.synchronize)
     elif args.workload == "flash":
         rng = np.random.default_rng(4096 + rank)
         reqs = [rng.integers(0, cfg.vocab_size, args.flash_tokens).astype(np.int32)]

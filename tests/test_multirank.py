@@ -108,3 +108,70 @@ def test_lpt_balance_on_the_benchmark_batch(ranks):
     a = lpt_assign(costs, ranks)
     assert sorted(i for s in a for i in s) == list(range(256))
     assert imbalance(costs, a) < 1.02
+
+
+class _FakePrefix:
+    """Host stand-in for clef_b200.Prefix: its 'device allocation' is a CPU
+    byte tensor, so the broadcast logic runs on gloo ranks."""
+
+    def __init__(self, data):
+        import torch
+        self.data = torch.as_tensor(data, dtype=torch.uint8).clone()
+
+    def span_bytes(self):
+        return self.data.numel()
+
+    def export_to(self, buf):
+        buf.copy_(self.data)
+
+    def import_from(self, buf):
+        self.data.copy_(buf)
+
+
+def _share_worker(rank, world, port, q):
+    sys.path.insert(0, str(ROOT / "clef-rs_b200"))
+    from datetime import timedelta
+
+    import numpy as np
+
+    from clef_b200.sharding import share_prefix
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
+    try:
+        computed = []
+        pattern = (np.arange(4096) * 7 % 251).astype(np.uint8)
+
+        def compute():
+            computed.append(rank)
+            return _FakePrefix(pattern)
+
+        p, cms, bms = share_prefix(compute, lambda: _FakePrefix(np.zeros(4096, np.uint8)), rank, world, "cpu")
+        q.put(("ok", rank, computed, p.data.numpy().tobytes() == pattern.tobytes(), cms >= 0, bms is not None))
+    except Exception as e:
+        q.put(("error", rank, repr(e)))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def test_prefix_is_computed_once_and_broadcast():
+    """Config 5's prefix: rank 0 alone computes it, every rank ends with rank
+    0's bytes (share_prefix, the logic bench.py runs over NCCL)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_share_worker, args=(r, 3, port, q)) for r in range(3)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=120) for _ in range(3)]
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert all(o[0] == "ok" for o in out), out
+    for _, rank, computed, same, ok_ms, has_bcast in out:
+        assert computed == ([0] if rank == 0 else [])
+        assert same and ok_ms and has_bcast

@@ -1,15 +1,17 @@
 #!/usr/bin/env python
 """Prefill throughput of the clef-rs B200 backend.
 
-Workload: the full random-init 32-layer hybrid backbone
+Workload (config 4, the default): the full random-init 32-layer hybrid backbone
 ([3 x DeltaNet + 1 x attention] x 8, hidden 2560, intermediate 9216, 16/32
 DeltaNet heads of 128, 16/4 attention heads of 256) plus the linear schema head
-read at each request's last token; a batch of 256 synthetic requests per GPU
-with lengths U[256, 2048] and ids U[0, 248320) (seed 3 + 1000 * rank), BF16
-projections with F32 accumulation and an F32 residual stream and head.
-A step is one prefill of the whole batch. Requests are independent and weights
-are replicated, so each rank serves its own batch with no collective on the
-data path (weak scaling); the max over ranks of the device time is reported.
+read at each request's last token; one batch of 256 synthetic requests with
+lengths U[256, 2048] and ids U[0, 248320) (seed 3), BF16 projections with F32
+accumulation and an F32 residual stream and head. A step is one prefill of the
+whole batch. Requests are independent and weights are replicated, so with N
+GPUs the batch is divided over the ranks by the longest-processing-time rule
+(strong scaling, no collective on the data path); the max over ranks of the
+device time is reported, with each rank's token count and device time.
+`--weak` gives every rank a batch of its own instead (seed 3 + 1000 * rank).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -47,12 +49,12 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="config4", choices=["config4", "config5", "flash"],
-                    help="config4: 256 requests U[256,2048] per GPU; config5: one 16384-token "
+                    help="config4: one batch of 256 requests U[256,2048] divided over the GPUs; config5: one 16384-token "
                          "prefix computed once (rank 0) and broadcast, 64 suffixes U[512,4096] "
                          "sharded over GPUs")
-    ap.add_argument("--shard", action="store_true",
-                    help="config4 with one fixed batch shared by all ranks (LPT-sharded, "
-                         "strong scaling) instead of a batch per rank")
+    ap.add_argument("--weak", action="store_true",
+                    help="config4 with a batch of --requests per rank (weak scaling) instead of "
+                         "one batch divided over the ranks (strong scaling, the default)")
     ap.add_argument("--requests", type=int, default=256)
     ap.add_argument("--flash-tokens", type=int, default=4096, choices=[256, 1024, 4096],
                     help="request length of the flash workload (the reference's published lengths)")
@@ -98,13 +100,15 @@ def workload_config(args, n_gpus):
                 "parallelism": (f"dp{n_gpus} (suffixes LPT-sharded; prefix computed once on rank 0 and "
                                 "broadcast to the other ranks by one NCCL broadcast of its device state)"),
                 "l2": "not flushed: every step streams 8.4 GB of weights, far above the 126 MB L2"}
+    batch = ({"requests_per_gpu": args.requests} if args.weak
+             else {"requests": args.requests, "requests_per_gpu": round(args.requests / n_gpus, 2)})
     return {"workload": "config4: 32-layer hybrid backbone + linear schema head",
-            "requests_per_gpu": args.requests, "prompt_len": "U[256,2048]", "vocab": 248320,
+            **batch, "prompt_len": "U[256,2048]", "vocab": 248320,
             "layers": args.layers, "hidden": 2560, "intermediate": 9216,
             "deltanet_heads": "16qk/32v x 128", "attention_heads": "16q/4kv x 256",
             "chunk": 64,
-            "parallelism": f"dp{n_gpus} (" + ("one batch LPT-sharded over ranks" if args.shard
-                                             else "one batch per rank") + ", weights replicated)",
+            "parallelism": f"dp{n_gpus} (" + ("one batch per rank" if args.weak
+                                             else "one batch LPT-sharded over ranks") + ", weights replicated)",
             "l2": "not flushed: every step streams 8.4 GB of weights and tens of GB of "
                   "activations, far above the 126 MB L2"}
 
@@ -200,7 +204,8 @@ def run_reference(args):
               f"{threads} threads")
     line = {"metric": METRIC, "value": round(tok_s, 3), "unit": "tok/s", "impl": "reference",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": round(ms, 3), "higher_is_better": True,
+            "scaling": "weak" if (args.weak or args.workload == "flash") else "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "decisions_per_s": round(1000.0 / ms, 5),
             "config": workload_config(args, args.gpus),
@@ -208,9 +213,23 @@ def run_reference(args):
                              "kind": "port", "sample": sample},
             "e2e": {"value": round(tok_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
-            "finite": bool(np.isfinite(hidden).all())}
+            "finite": bool(np.isfinite(hidden).all()),
+            "native_libraries": mapped_repo_libraries()}
     print(json.dumps(line), flush=True)
     return 0
+
+
+def mapped_repo_libraries():
+    """Shared objects of this repository mapped into this process (Linux
+    /proc/self/maps): the reference arm must map the oracle only, never the
+    product library."""
+    try:
+        maps = Path("/proc/self/maps").read_text().splitlines()
+    except OSError:
+        return None
+    root = str(ROOT)
+    return sorted({line.split()[-1][len(root) + 1:] for line in maps
+                   if line.split()[-1].startswith(root) and line.endswith(".so")})
 
 
 # ---------------------------------------------------------------------------
@@ -471,6 +490,14 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.SUM)
         return float(t.item())
 
+    def allgather(values):
+        t = torch.tensor(values, dtype=torch.float64, device="cuda")
+        if world == 1:
+            return [t.tolist()]
+        every = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(every, t)
+        return [e.tolist() for e in every]
+
     from clef_b200.config import flash_config
     cfg = flash_config(args.layers, 7) if args.workload == "flash" else benchmark_config(args.layers, 7)
     eng = cb.Engine(cfg, local)
@@ -492,11 +519,11 @@ def main():
     elif args.workload == "flash":
         rng = np.random.default_rng(4096 + rank)
         reqs = [rng.integers(0, cfg.vocab_size, args.flash_tokens).astype(np.int32)]
-    elif args.shard:
+    elif args.weak:
+        reqs = workloads.backbone_requests(n=args.requests, seed=3 + 1000 * rank)
+    else:
         batch = workloads.backbone_requests(n=args.requests, seed=3)
         reqs = rank_shard(batch, rank, world, lambda r: flops_per_request(cfg, len(r)))
-    else:
-        reqs = workloads.backbone_requests(n=args.requests, seed=3 + 1000 * rank)
     lens = np.array([len(r) for r in reqs], np.int64)
     offsets = np.zeros(len(reqs) + 1, np.int64)
     offsets[1:] = np.cumsum(lens)
@@ -532,6 +559,9 @@ def main():
     eng.set_profiling(False)
     logits = logits_dev.cpu().numpy()
     ms_max = allmax(ms)
+    per_rank = [{"rank": r, "tokens": int(v[0]), "requests": int(v[1]), "device_ms": round(v[2], 3),
+                 "gemm_ms": round(v[3], 3)}
+                for r, v in enumerate(allgather([tokens, len(reqs), ms, stages["gemm"] / args.steps]))]
 
     # ---- end to end through the public host API ------------------------------
     ids_pin = torch.from_numpy(ids).pin_memory()
@@ -573,7 +603,7 @@ def main():
     line = {"metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 3),
             "higher_is_better": True,
-            "scaling": "strong" if (args.shard or args.workload == "config5") else "weak",
+            "scaling": "weak" if (args.weak or args.workload == "flash") else "strong",
             "vs_baseline": (round(value / FLASH_REFERENCE_TOK_S[args.flash_tokens], 1)
                             if args.workload == "flash" else None),
             "dtype": "bf16",
@@ -587,6 +617,7 @@ def main():
                     "h2d_bytes_per_step": int(ids.nbytes + offsets.nbytes),
                     "d2h_bytes_per_step": int(lg_np.nbytes)},
             "gpu_launches": int(launches),
+            "ranks": per_rank,
             "prefix_ms_once": None if prefix_ms is None else round(allmax(prefix_ms), 1),
             "prefix_broadcast_ms": None if bcast_ms is None else round(allmax(bcast_ms), 2),
             "clocks": clocks,

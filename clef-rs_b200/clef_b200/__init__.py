@@ -1,8 +1,10 @@
 """Python host mirror of the clef-rs prefill backend's C ABI (libclef_b200.so).
 
 Every compute call goes through the shared library built from csrc/ for
-sm_100a; there is no CPU or framework fallback. If the library is missing or
-cannot be loaded, importing this package raises.
+sm_100a; there is no CPU or framework fallback. The library is mapped on first
+use (not at import, so that host-only modules such as clef_b200.config and
+clef_b200.workloads can be used without it); if it is missing or cannot be
+loaded, that first use raises ImportError.
 
 The operator functions take torch CUDA tensors (torch is only the device
 allocator and stream provider here) and mirror the reference engine's Candle
@@ -130,7 +132,28 @@ def _load():
     return L
 
 
-lib = _load()
+class _LazyLib:
+    """The ctypes handle of libclef_b200.so, loaded on first attribute access."""
+
+    _handle = None
+
+    def __getattr__(self, name):
+        if _LazyLib._handle is None:
+            _LazyLib._handle = _load()
+        return getattr(_LazyLib._handle, name)
+
+    @staticmethod
+    def loaded() -> bool:
+        return _LazyLib._handle is not None
+
+
+lib = _LazyLib()
+
+
+def load():
+    """Maps the library now (raises ImportError if it is missing)."""
+    lib.clef_version
+    return lib
 
 
 def version() -> str:

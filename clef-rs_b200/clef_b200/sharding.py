@@ -52,23 +52,45 @@ def share_prefix(compute, create, rank: int, world: int, device="cuda", sync=Non
     then reaches them by one broadcast (torch.distributed, NCCL on GPUs): a
     prefix exposes span_bytes(), export_to(buf) and import_from(buf) like
     clef_b200.Prefix. `sync` (e.g. torch.cuda.synchronize) orders the copies
-    around the broadcast. Returns (prefix, compute_ms, broadcast_ms or None)."""
+    around the broadcast. Returns (prefix, compute_ms, broadcast_ms or None).
+
+    Every rank takes the same collective steps and the same decision: one
+    all_gather of (ok, span) from all ranks, after which either every rank
+    goes on to the broadcast or every rank raises (a failed compute() or
+    create() on any rank, or ranks whose prefix layouts differ), so no rank is
+    left waiting in a collective that the others never enter."""
     import time
 
     import torch
     import torch.distributed as dist
     sync = sync or (lambda: None)
     t0 = time.perf_counter()
-    prefix = compute() if rank == 0 else create()
-    sync()
+    prefix, error = None, None
+    try:
+        prefix = compute() if rank == 0 else create()
+        sync()
+    except Exception as e:  # reported on every rank after the exchange below
+        error = e
     compute_ms = 1000 * (time.perf_counter() - t0)
     if world == 1:
+        if error is not None:
+            raise error
         return prefix, compute_ms, None
-    span = torch.tensor([prefix.span_bytes()], dtype=torch.int64, device=device)
-    dist.all_reduce(span, op=dist.ReduceOp.MAX)
-    if int(span.item()) != prefix.span_bytes():
-        raise RuntimeError("share_prefix: ranks disagree on the prefix layout")
-    buf = torch.empty(int(span.item()), dtype=torch.uint8, device=device)
+    mine = torch.tensor([0 if error is not None else 1,
+                         prefix.span_bytes() if error is None else -1], dtype=torch.int64, device=device)
+    every = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(every, mine)
+    table = [(int(t[0].item()), int(t[1].item())) for t in every]
+    failed = [r for r, (ok, _) in enumerate(table) if not ok]
+    if failed:
+        why = f" ({error!r})" if error is not None else ""
+        raise RuntimeError(f"share_prefix: prefix set-up failed on rank(s) {failed}{why}")
+    spans = {span for _, span in table}
+    if len(spans) != 1:
+        raise RuntimeError(f"share_prefix: ranks disagree on the prefix layout (span bytes per rank "
+                           f"{[span for _, span in table]})")
+    span = spans.pop()
+    buf = torch.empty(span, dtype=torch.uint8, device=device)
     if rank == 0:
         prefix.export_to(buf)
     sync()

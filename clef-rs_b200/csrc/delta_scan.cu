@@ -34,6 +34,7 @@
 // the capture token is formed from the same chunk quantities, so a prefill with
 // capture is bit-identical to one without.
 #include <algorithm>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -1542,20 +1543,28 @@ static __device__ __align__(256) int64_t g_noalloc_offsets[kNoAllocMaxSeqs + 1];
 
 namespace {
 // Device address of g_noalloc_offsets, resolved once per device with that
-// device current (the first call on a device does this set-up).
+// device current (the first call on a device does this set-up). std::call_once
+// makes concurrent first calls from several host threads on one device wait
+// for a single lookup; a failed lookup is remembered and reported by every
+// later call on that device.
+constexpr int kNoAllocMaxDevices = 64;
 int noalloc_offsets_ptr(int64_t** out) {
-  static int64_t* ptrs[64] = {nullptr};
+  static std::once_flag once[kNoAllocMaxDevices];
+  static int64_t* ptrs[kNoAllocMaxDevices] = {nullptr};
+  static cudaError_t errs[kNoAllocMaxDevices] = {};
   int dev = 0;
   CLEF_CUDA(cudaGetDevice(&dev));
-  CLEF_CHECK(dev >= 0 && dev < 64, CLEF_ERR_UNSUPPORTED, "delta_scan_noalloc: device index >= 64");
-  if (!ptrs[dev]) {
+  CLEF_CHECK(dev >= 0 && dev < kNoAllocMaxDevices, CLEF_ERR_UNSUPPORTED,
+             "delta_scan_noalloc: device index >= 64");
+  std::call_once(once[dev], [dev] {
     void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_offsets);
-    if (e != cudaSuccess || !p)
-      return fail(CLEF_ERR_CUDA, std::string("delta_scan_noalloc: cudaGetSymbolAddress: ") +
-                                     cudaGetErrorString(e));
-    ptrs[dev] = reinterpret_cast<int64_t*>(p);
-  }
+    errs[dev] = cudaGetSymbolAddress(&p, g_noalloc_offsets);
+    if (errs[dev] == cudaSuccess && !p) errs[dev] = cudaErrorInvalidSymbol;
+    if (errs[dev] == cudaSuccess) ptrs[dev] = reinterpret_cast<int64_t*>(p);
+  });
+  if (errs[dev] != cudaSuccess)
+    return fail(CLEF_ERR_CUDA, std::string("delta_scan_noalloc: cudaGetSymbolAddress: ") +
+                                   cudaGetErrorString(errs[dev]));
   *out = ptrs[dev];
   return CLEF_OK;
 }
@@ -1616,6 +1625,9 @@ int clef_delta_scan(const float* q, const float* k, const float* v, const float*
 // sequence offsets are copied into the library's fixed device array (at most
 // 4096 sequences). It allocates nothing. The first call on each device looks
 // up the array's device address and should come before any stream capture.
+// The offsets are copied from cu_seqlens by a copy ordered on `stream`; when
+// cu_seqlens is page-locked that copy runs asynchronously, so the caller keeps
+// the buffer unchanged until the stream has reached this call.
 // Every call shares the one array per device, and each call rewrites the
 // entries [0, nseq] it uses before its kernel reads them (nothing else needs
 // to start at zero); calls whose work overlaps on the GPU (different streams,

@@ -155,8 +155,11 @@ int clef_delta_scan(const float* q, const float* k, const float* v, const float*
  * fixed device array inside this library (at most 4096 sequences per call;
  * more is rejected with CLEF_ERR_UNSUPPORTED). It allocates nothing. The
  * first call on each device resolves the array's device address and should
- * come before any stream capture. All calls on a device share the array:
- * calls whose work overlaps on the GPU race, so serialise them on one stream. */
+ * come before any stream capture. cu_seqlens is read by a copy ordered on
+ * `stream` (asynchronous when the buffer is page-locked): keep it unchanged
+ * until the stream has reached the call. All calls on a device share the
+ * array: calls whose work overlaps on the GPU race, so serialise them on one
+ * stream. */
 int clef_delta_scan_noalloc(const float* q, const float* k, const float* v, const float* g,
                             const float* beta, int64_t T, int32_t Hk, int32_t Hv, int32_t dk,
                             int32_t dv, const int64_t* cu_seqlens, int32_t nseq,

@@ -61,6 +61,7 @@ def lib():
         L.oracle_head.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int, _f32p]
         L.oracle_set_threads.argtypes = [ctypes.c_int]
         L.oracle_max_threads.restype = ctypes.c_int
+        L.oracle_set_rounding.argtypes = [ctypes.c_int]
         _lib = L
     return _lib
 
@@ -80,6 +81,16 @@ def set_threads(n: int) -> None:
 
 def max_threads() -> int:
     return int(lib().oracle_max_threads())
+
+
+# BF16 rounding points of oracle.cpp (kRound*): 0 is the reference's F32 path.
+ROUND_OPERAND, ROUND_PROJ, ROUND_ATTN_QKV, ROUND_P, ROUND_FLOW = 1, 2, 4, 8, 16
+
+
+def set_rounding(mask: int) -> None:
+    """Rounds the chosen intermediates to BF16 in every later prefill (a
+    measuring aid for BF16 device profiles; 0 restores the F32 path)."""
+    lib().oracle_set_rounding(int(mask))
 
 
 def linear(x, w):

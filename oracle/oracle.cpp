@@ -42,6 +42,47 @@ int fail(const std::string& m) {
 }
 
 // ---------------------------------------------------------------------------
+// Optional BF16 rounding points (default off: the reference's F32 path). A
+// mask set by oracle_set_rounding() rounds chosen intermediates to BF16
+// (nearest, ties to even) so tests can measure how much of a BF16 device
+// profile's distance from the F32 path each rounding point contributes, and
+// can check a device path against the F32 path with exactly its own
+// rounding points:
+//   kRoundOperand  GEMM A operands: normed inputs, gated DeltaNet output,
+//                  gated attention output, SwiGLU activation
+//   kRoundProj     projection outputs (in_proj_qkv/z/a/b, q/k/v_proj)
+//   kRoundAttnQKV  attention q, k (after norm and rotary) and v
+//   kRoundP        attention probabilities as the P.V product reads them
+//   kRoundFlow     the remaining model-dtype casts of the reference's
+//                  mixed-precision path (qwen.rs:671-676, 463-524): DeltaNet
+//                  o and norm output, q/k norm output, sigmoid(gate), attention
+//                  output before the gate product
+// ---------------------------------------------------------------------------
+enum {
+  kRoundOperand = 1,
+  kRoundProj = 2,
+  kRoundAttnQKV = 4,
+  kRoundP = 8,
+  kRoundFlow = 16,
+};
+int g_round = 0;
+
+inline float bf16r(float x) {
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  u &= 0xffff0000u;
+  float r;
+  memcpy(&r, &u, 4);
+  return r;
+}
+inline void round_if(int bit, float* x, size_t n) {
+  if (!(g_round & bit)) return;
+  for (size_t i = 0; i < n; ++i) x[i] = bf16r(x[i]);
+}
+inline void round_if(int bit, std::vector<float>& v) { round_if(bit, v.data(), v.size()); }
+
+// ---------------------------------------------------------------------------
 // Dense F32 GEMM: out[M,N] = x[M,K] * W[N,K]^T  (candle_nn::Linear without
 // bias, projection.rs:82-95). W is packed once into 16-column panels
 // [N/16][K][16] so the micro-kernel broadcasts x and streams W.
@@ -245,7 +286,8 @@ void attention(const float* q, const float* k, const float* v, int heads, int kv
           float* a = acc.data() + i * vw;
           for (int c = 0; c < vw; ++c) a[c] = a[c] * rescale;
           for (int64_t j = 0; j < keys; ++j) {
-            const float p = std::exp(sc[i * keys + j] - nm);
+            float p = std::exp(sc[i * keys + j] - nm);
+            if (g_round & kRoundP) p = bf16r(p);
             psum += p;
             const float* vr = v + ((size_t)kh * kn + ks + j) * vw;
             for (int c = 0; c < vw; ++c) a[c] += p * vr[c];
@@ -395,6 +437,7 @@ void delta_forward(const Model& m, int li, const float* x, int64_t t, const Laye
   const int taps = c.linear_conv_kernel_dim;
   std::vector<float> proj;
   linear(m, p + ".in_proj_qkv.weight", x, t, proj);
+  round_if(kRoundProj, proj);
   const int64_t hist = init ? init->history_rows : 0;
   std::vector<float> projected((size_t)(hist + t) * width);
   if (hist) memcpy(projected.data(), init->history.data(), sizeof(float) * hist * width);
@@ -407,6 +450,8 @@ void delta_forward(const Model& m, int li, const float* x, int64_t t, const Laye
   std::vector<float> a, b;
   linear(m, p + ".in_proj_a.weight", x, t, a);
   linear(m, p + ".in_proj_b.weight", x, t, b);
+  round_if(kRoundProj, a);
+  round_if(kRoundProj, b);
   const auto& dt = W(m, p + ".dt_bias").data;
   const auto& alog = W(m, p + ".A_log").data;
   std::vector<float> g((size_t)t * hv), beta((size_t)t * hv);
@@ -435,11 +480,15 @@ void delta_forward(const Model& m, int li, const float* x, int64_t t, const Laye
   // norm(out) (no offset, qwen.rs:581-586) * silu(z) (qwen.rs:671-676).
   std::vector<float> z;
   linear(m, p + ".in_proj_z.weight", x, t, z);
+  round_if(kRoundProj, z);
   const std::vector<float> nw = norm_weight(m, p + ".norm.weight", false);
   std::vector<float> normed((size_t)t * value);
+  round_if(kRoundFlow, out);
   rms_rows(out.data(), nw.data(), t * hv, vd, c.rms_norm_eps, normed.data());
+  round_if(kRoundFlow, normed);
   std::vector<float> gated((size_t)t * value);
   for (int64_t i = 0; i < t * value; ++i) gated[i] = normed[i] * siluf_(z[i]);
+  round_if(kRoundOperand, gated);
   if (capture && saved) {
     saved->full = false;
     saved->recurrent = captured;
@@ -463,6 +512,9 @@ void attention_forward(const Model& m, int li, const float* x, int64_t t,
   linear(m, p + ".q_proj.weight", x, t, proj);  // [t, heads, 2d]
   linear(m, p + ".k_proj.weight", x, t, kp);    // [t, kvh, d]
   linear(m, p + ".v_proj.weight", x, t, vp);    // [t, kvh, d]
+  round_if(kRoundProj, proj);
+  round_if(kRoundProj, kp);
+  round_if(kRoundProj | kRoundAttnQKV, vp);
   std::vector<float> gate((size_t)t * heads * d), qraw((size_t)t * heads * d);
   for (int64_t i = 0; i < t; ++i)
     for (int h = 0; h < heads; ++h) {
@@ -474,8 +526,12 @@ void attention_forward(const Model& m, int li, const float* x, int64_t t,
   std::vector<float> qn(qraw.size()), kn(kp.size());
   rms_rows(qraw.data(), qw.data(), t * heads, d, c.rms_norm_eps, qn.data());
   rms_rows(kp.data(), kw.data(), t * kvh, d, c.rms_norm_eps, kn.data());
+  round_if(kRoundFlow, qn);
+  round_if(kRoundFlow, kn);
   rotary(qn.data(), t, heads, d, positions, c.rotary_dim, c.rope_theta);
   rotary(kn.data(), t, kvh, d, positions, c.rotary_dim, c.rope_theta);
+  round_if(kRoundAttnQKV, qn);
+  round_if(kRoundAttnQKV, kn);
   const int64_t pre = init ? init->kv_tokens : 0, kn_total = pre + t;
   // Transpose to [heads, tokens, d]; prefix K/V first (qwen.rs:497-503).
   std::vector<float> qt((size_t)heads * t * d), kt((size_t)kvh * kn_total * d),
@@ -514,8 +570,14 @@ void attention_forward(const Model& m, int li, const float* x, int64_t t,
     for (int h = 0; h < heads; ++h)
       for (int e = 0; e < d; ++e) {
         size_t idx = (i * heads + h) * d + e;
-        o[idx] = att[((size_t)h * t + i) * d + e] * sigmoidf_(gate[idx]);
+        float av = att[((size_t)h * t + i) * d + e], gv = sigmoidf_(gate[idx]);
+        if (g_round & kRoundFlow) {
+          av = bf16r(av);
+          gv = bf16r(gv);
+        }
+        o[idx] = av * gv;
       }
+  round_if(kRoundOperand, o);
   linear(m, p + ".o_proj.weight", o.data(), t, mixed_out);
 }
 
@@ -550,6 +612,7 @@ int prefill(const Model& m, const int32_t* ids, int64_t t, const Prefix* init, i
     const std::string p = L(li);
     const std::vector<float> wi = norm_weight(m, p + ".input_layernorm.weight", true);
     rms_rows(h.data(), wi.data(), t, hsz, c.rms_norm_eps, u.data());
+    round_if(kRoundOperand, u);
     const LayerState* st = init ? &init->layers[li] : nullptr;
     LayerState* sv = saved ? &saved->layers[li] : nullptr;
     if (c.layer_types[li])
@@ -559,10 +622,12 @@ int prefill(const Model& m, const int32_t* ids, int64_t t, const Prefix* init, i
     for (int64_t i = 0; i < t * hsz; ++i) h[i] = h[i] + mixed[i];
     const std::vector<float> wp = norm_weight(m, p + ".post_attention_layernorm.weight", true);
     rms_rows(h.data(), wp.data(), t, hsz, c.rms_norm_eps, u.data());
+    round_if(kRoundOperand, u);
     std::vector<float> gt, up;
     linear(m, p + ".mlp.gate_proj.weight", u.data(), t, gt);
     linear(m, p + ".mlp.up_proj.weight", u.data(), t, up);
     for (size_t i = 0; i < gt.size(); ++i) gt[i] = siluf_(gt[i]) * up[i];
+    round_if(kRoundOperand, gt);
     linear(m, p + ".mlp.down_proj.weight", gt.data(), t, ff);
     for (int64_t i = 0; i < t * hsz; ++i) h[i] = h[i] + ff[i];
   }
@@ -594,6 +659,10 @@ void oracle_set_threads(int n) {
   if (n > 0) omp_set_num_threads(n);
 }
 int oracle_max_threads(void) { return omp_get_max_threads(); }
+// BF16 rounding points (mask of kRound* bits); 0, the default, is the
+// reference's F32 path. Process-wide: set it before a prefill.
+void oracle_set_rounding(int mask) { g_round = mask; }
+int oracle_rounding(void) { return g_round; }
 
 void oracle_linear(const float* x, int64_t m, const float* w, int64_t n, int64_t k, float* out) {
   gemm_plain(x, m, w, n, k, out);

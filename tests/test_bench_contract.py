@@ -30,7 +30,7 @@ def test_reference_arm_prints_the_contract_line():
     d = json.loads(lines[0])
     assert d["impl"] == "reference" and d["metric"] == "prefill tok/s" and d["unit"] == "tok/s"
     assert d["value"] > 0 and d["ms_per_step"] > 0 and d["higher_is_better"] is True
-    assert d["steps"] == 1 and d["warmup"] == 3 and d["n_gpus"] == 1 and d["scaling"] == "weak"
+    assert d["steps"] == 1 and d["warmup"] == 3 and d["n_gpus"] == 1 and d["scaling"] == "strong"
     assert "workload" in d["config"] and d["vs_baseline"] is None
     cb = d["cpu_baseline"]
     assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
@@ -38,6 +38,9 @@ def test_reference_arm_prints_the_contract_line():
     assert e2e["value"] == d["value"] and e2e["unit"] == d["unit"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
     assert d["finite"] is True
+    # The reference arm runs the oracle alone: the product library is never
+    # mapped into its process.
+    assert d["native_libraries"] == ["oracle/liboracle.so"], d["native_libraries"]
 
 
 def test_reference_arm_other_ranks_exit_silently():

@@ -246,7 +246,7 @@ def test_flash_geometry_block_group_matches_oracle():
 
 
 def test_config3_block_group_full_size_matches_oracle():
-    """BASELINE config 3 at its stated size: one random-init block group
+    """Config 3 at its stated size: one random-init block group
     (3 DeltaNet + 1 attention layer, benchmark dims), a single 4096-token
     sequence with ids uniform over the full 248320-token vocabulary, weights
     N(0, 0.02) drawn by the engine with seed 2, against the F32 oracle on the

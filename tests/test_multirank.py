@@ -175,3 +175,63 @@ def test_prefix_is_computed_once_and_broadcast():
     for _, rank, computed, same, ok_ms, has_bcast in out:
         assert computed == ([0] if rank == 0 else [])
         assert same and ok_ms and has_bcast
+
+
+def _share_fail_worker(rank, world, port, q, mode):
+    sys.path.insert(0, str(ROOT / "clef-rs_b200"))
+    import time
+    from datetime import timedelta
+
+    import numpy as np
+
+    from clef_b200.sharding import share_prefix
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    t0 = time.perf_counter()
+    try:
+        def compute():
+            if mode == "compute_raises":
+                raise ValueError("prefix prefill failed")
+            return _FakePrefix(np.ones(4096, np.uint8))
+
+        def create():
+            n = 4096 + (16 if (mode == "span_differs" and rank == world - 1) else 0)
+            return _FakePrefix(np.zeros(n, np.uint8))
+
+        share_prefix(compute, create, rank, world, "cpu")
+        q.put(("no error", rank, time.perf_counter() - t0, ""))
+    except Exception as e:
+        q.put(("raised", rank, time.perf_counter() - t0, str(e)))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+@pytest.mark.parametrize("mode", ["span_differs", "compute_raises"])
+def test_share_prefix_fails_on_every_rank_together(mode):
+    """A layout that differs on one rank (rank 0 holding the largest span is
+    the case a one-sided check misses) or a prefill that raises on rank 0: all
+    ranks raise, promptly, instead of some waiting in the broadcast."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    world = 3
+    procs = [ctx.Process(target=_share_fail_worker, args=(r, world, port, q, mode)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert sorted(o[1] for o in out) == list(range(world))
+    for status, rank, seconds, msg in out:
+        assert status == "raised", (rank, msg)
+        assert seconds < 30, (rank, seconds)
+        if mode == "span_differs":
+            assert "disagree" in msg
+        else:
+            assert "failed on rank(s) [0]" in msg

@@ -66,6 +66,20 @@ enum Stage { kStEmbed, kStNorm, kStGemm, kStDeltaPro, kStDeltaScan, kStDeltaEpi,
 
 }  // namespace
 
+// Layout descriptor in the first 256 bytes of a prefix's device allocation:
+// travels with every export, so an import can tell a copy made for another
+// layout or token count from a matching one.
+struct PrefixDescriptor {
+  uint64_t magic = 0x3158464650464c43ull;  // "CLEFPFX1"
+  int64_t tokens = 0;
+  int64_t vt_pitch = 0;
+  uint64_t span = 0;
+  int32_t layers = 0, hidden = 0, value_heads = 0, kv_width = 0, qkv_width = 0, pad = 0;
+  uint64_t attention_layers[2] = {0, 0};  // bit i: layer i is full attention
+  bool operator==(const PrefixDescriptor& o) const { return memcmp(this, &o, sizeof(*this)) == 0; }
+};
+static_assert(sizeof(PrefixDescriptor) <= 256, "prefix descriptor exceeds its slot");
+
 struct clef_prefix {
   int device = 0;
   int64_t tokens = 0;
@@ -74,6 +88,8 @@ struct clef_prefix {
   void* blob = nullptr;
   uint64_t bytes = 0;       // logical state bytes
   uint64_t span = 0;        // bytes of the device allocation (layout of the engine config)
+  bool filled = false;      // set by a capture or a successful import
+  PrefixDescriptor desc;    // host copy of the descriptor at the start of `blob`
   float* hidden_rows = nullptr;  // [tokens, hidden]
   struct Layer {
     bool full = false;
@@ -398,6 +414,7 @@ int alloc_prefix(clef_engine* e, int64_t tokens, clef_prefix** out) {
     o.push_back(b);
     b = a256(b + n);
   };
+  take(sizeof(PrefixDescriptor));
   take(sizeof(float) * tokens * c.hidden_size);
   uint64_t logical = sizeof(float) * tokens * c.hidden_size;
   p->vt_pitch = (tokens + 63) / 64 * 64;
@@ -420,7 +437,7 @@ int alloc_prefix(clef_engine* e, int64_t tokens, clef_prefix** out) {
   }
   p->span = b;
   char* base = reinterpret_cast<char*>(p->blob);
-  int k = 0;
+  int k = 1;  // o[0]: the descriptor
   p->hidden_rows = (float*)(base + o[k++]);
   for (int i = 0; i < c.num_hidden_layers; ++i) {
     auto& L = p->layers[i];
@@ -435,6 +452,24 @@ int alloc_prefix(clef_engine* e, int64_t tokens, clef_prefix** out) {
     }
   }
   p->bytes = logical;
+  PrefixDescriptor& d = p->desc;
+  d.tokens = tokens;
+  d.vt_pitch = p->vt_pitch;
+  d.span = p->span;
+  d.layers = c.num_hidden_layers;
+  d.hidden = c.hidden_size;
+  d.value_heads = c.linear_num_value_heads;
+  d.kv_width = e->att_kv;
+  d.qkv_width = e->qkv_w;
+  for (int i = 0; i < c.num_hidden_layers; ++i)
+    if (c.layer_types[i]) d.attention_layers[i / 64] |= 1ull << (i % 64);
+  // Pageable source: the call returns once the bytes are staged, so the host
+  // copy in `p` may change afterwards; the device copy is stream-ordered.
+  if (cudaMemcpyAsync(p->blob, &d, sizeof(d), cudaMemcpyHostToDevice, e->stream) != cudaSuccess) {
+    cudaFree(p->blob);
+    delete p;
+    return fail(CLEF_ERR_CUDA, "prefix: descriptor copy");
+  }
   *out = p;
   return CLEF_OK;
 }
@@ -842,6 +877,8 @@ int clef_engine_prefill(clef_engine* e, const int32_t* ids, const int64_t* offse
     CLEF_CHECK(initial->device == e->device && (int)initial->layers.size() == c.num_hidden_layers &&
                    initial->hidden == c.hidden_size,
                CLEF_ERR_INVALID, "prefill: prefix state does not match this engine");
+    CLEF_CHECK(initial->filled, CLEF_ERR_INVALID,
+               "prefill: the prefix holds no state (created but never imported)");
   }
   if (captured) *captured = nullptr;
   DeviceGuard g(e->device);
@@ -877,6 +914,7 @@ int clef_engine_prefill(clef_engine* e, const int32_t* ids, const int64_t* offse
     if (cap) clef_prefix_destroy(cap);
     return rc;
   }
+  if (cap) cap->filled = true;
   if (captured) *captured = cap;
   return CLEF_OK;
 }
@@ -892,10 +930,13 @@ int clef_engine_prefill_device(clef_engine* e, const int32_t* ids_device, const 
     CLEF_CHECK(offsets[i + 1] > offsets[i], CLEF_ERR_INVALID,
                "prefill_device: empty or unordered sequence");
   CLEF_CHECK(e->cfg.head_outputs > 0, CLEF_ERR_INVALID, "prefill_device: model has no head");
-  if (initial)
+  if (initial) {
     CLEF_CHECK(initial->device == e->device &&
                    (int)initial->layers.size() == e->cfg.num_hidden_layers,
                CLEF_ERR_INVALID, "prefill_device: prefix state does not match this engine");
+    CLEF_CHECK(initial->filled, CLEF_ERR_INVALID,
+               "prefill_device: the prefix holds no state (created but never imported)");
+  }
   DeviceGuard g(e->device);
   cudaStream_t user = as_stream(stream);
   cudaStream_t own = e->stream;
@@ -965,11 +1006,19 @@ int clef_prefix_create(clef_engine* e, int64_t tokens, clef_prefix** out) {
   CLEF_CHECK(e->finalized, CLEF_ERR_INVALID, "prefix_create: engine not finalized");
   CLEF_CHECK(tokens > 0, CLEF_ERR_INVALID, "prefix_create: tokens must be positive");
   DeviceGuard g(e->device);
-  return alloc_prefix(e, tokens, out);
+  RC(alloc_prefix(e, tokens, out));
+  // The descriptor copy must land before an import on another stream reads it back.
+  if (cudaStreamSynchronize(e->stream) != cudaSuccess) {
+    clef_prefix_destroy(*out);
+    *out = nullptr;
+    return fail(CLEF_ERR_CUDA, "prefix_create: descriptor copy");
+  }
+  return CLEF_OK;
 }
 
 int clef_prefix_export(const clef_prefix* p, void* dst, uint64_t bytes, void* stream) {
   CLEF_CHECK(p && dst, CLEF_ERR_INVALID, "prefix_export: null pointer");
+  CLEF_CHECK(p->filled, CLEF_ERR_INVALID, "prefix_export: the prefix holds no state");
   CLEF_CHECK(bytes == p->span, CLEF_ERR_INVALID,
              "prefix_export: bytes must equal the prefix span (" + std::to_string(p->span) + ")");
   DeviceGuard g(p->device);
@@ -982,7 +1031,21 @@ int clef_prefix_import(clef_prefix* p, const void* src, uint64_t bytes, void* st
   CLEF_CHECK(bytes == p->span, CLEF_ERR_INVALID,
              "prefix_import: bytes must equal the prefix span (" + std::to_string(p->span) + ")");
   DeviceGuard g(p->device);
-  CLEF_CUDA(cudaMemcpyAsync(p->blob, src, bytes, cudaMemcpyDeviceToDevice, as_stream(stream)));
+  p->filled = false;
+  cudaStream_t s = as_stream(stream);
+  CLEF_CUDA(cudaMemcpyAsync(p->blob, src, bytes, cudaMemcpyDeviceToDevice, s));
+  PrefixDescriptor got;
+  CLEF_CUDA(cudaMemcpyAsync(&got, p->blob, sizeof(got), cudaMemcpyDeviceToHost, s));
+  CLEF_CUDA(cudaStreamSynchronize(s));
+  if (!(got == p->desc)) {
+    // Put this prefix's own descriptor back so a later import or export sees it.
+    CLEF_CUDA(cudaMemcpy(p->blob, &p->desc, sizeof(p->desc), cudaMemcpyHostToDevice));
+    return fail(CLEF_ERR_INVALID, "prefix_import: the copy was made for another layout or token count (" +
+                                      std::to_string(got.tokens) + " tokens, " + std::to_string(got.layers) +
+                                      " layers; this prefix: " + std::to_string(p->desc.tokens) + " tokens, " +
+                                      std::to_string(p->desc.layers) + " layers)");
+  }
+  p->filled = true;
   return CLEF_OK;
 }
 uint64_t clef_prefix_bytes(const clef_prefix* p) { return p ? p->bytes : 0; }

@@ -287,16 +287,20 @@ uint64_t clef_prefix_bytes(const clef_prefix* p);
 int clef_prefix_destroy(clef_prefix* p);
 
 /* Moving a prefix state between devices (no counterpart in the reference,
- * which serves one device; SURVEY's multi-GPU plan broadcasts the prefix of
- * config 5 from the rank that computed it instead of recomputing it on every
- * GPU). A prefix is one device allocation of clef_prefix_span_bytes bytes
- * whose layout depends only on the engine configuration and the token count:
+ * which serves one device; a multi-GPU server computes a shared prefix once
+ * and broadcasts it to the other GPUs instead of recomputing it on each).
+ * A prefix is one device allocation of clef_prefix_span_bytes bytes whose
+ * layout depends only on the engine configuration and the token count; its
+ * first 256 bytes are a layout descriptor (layer kinds, widths, token count).
  * clef_prefix_export copies it to `dst` (device memory of the prefix's
- * device, at least that many bytes), clef_prefix_create makes an empty
- * prefix of `tokens` tokens for engine `e`, and clef_prefix_import fills it
- * from such a copy (for example after an NCCL broadcast). Both copies are
- * stream-ordered on `stream` (NULL = default stream); `bytes` must equal the
- * span. */
+ * device, `bytes` = the span), stream-ordered on `stream` (NULL = default
+ * stream). clef_prefix_create makes an empty prefix of `tokens` tokens for
+ * engine `e`; it cannot be used as an initial state until filled.
+ * clef_prefix_import fills it from such a copy (for example after an NCCL
+ * broadcast): it copies on `stream`, then waits for that stream and checks
+ * the copied descriptor against the prefix's own, returning
+ * CLEF_ERR_INVALID (and leaving the prefix unfilled) when the copy was made
+ * for another layout or token count. */
 uint64_t clef_prefix_span_bytes(const clef_prefix* p);
 int clef_prefix_create(clef_engine* e, int64_t tokens, clef_prefix** out);
 int clef_prefix_export(const clef_prefix* p, void* dst, uint64_t bytes, void* stream);

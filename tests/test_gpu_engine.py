@@ -149,6 +149,41 @@ def test_prefix_moves_through_a_device_copy(models, boundary):
     prefix.close()
 
 
+def test_prefix_import_checks_the_layout(models):
+    """A created prefix cannot seed a prefill before it is filled, and an
+    import of a copy made for another layout (here: the same span, but the
+    attention layer first instead of last) is refused and leaves it unfilled."""
+    import clef_b200 as cb
+    cfg, eng, _ = models
+    seq = ids(257, 3)
+    _, _, prefix = eng.prefill([seq], capture=100)
+    empty = eng.create_prefix(100)
+    with pytest.raises(cb.ClefError, match="no state"):
+        eng.prefill([seq[100:]], initial=empty)
+    other_cfg = benchmark_config(layers=4, head_outputs=7)
+    other_cfg.vocab_size = 4096
+    for i, kind in enumerate((1, 0, 0, 0)):
+        other_cfg.layer_types[i] = kind
+    other = cb.Engine(other_cfg, 0)
+    other.init_random(2, 0.02)
+    other.finalize()
+    foreign = other.create_prefix(100)
+    assert foreign.span_bytes() == prefix.span_bytes()
+    buf = torch.empty(prefix.span_bytes(), dtype=torch.uint8, device="cuda")
+    prefix.export_to(buf)
+    with pytest.raises(cb.ClefError, match="another layout"):
+        foreign.import_from(buf)
+    with pytest.raises(cb.ClefError, match="no state"):
+        other.prefill([seq[100:]], initial=foreign)
+    empty.import_from(buf)
+    a, _, _ = eng.prefill([seq[100:]], initial=empty)
+    b, _, _ = eng.prefill([seq[100:]], initial=prefix)
+    assert np.array_equal(a, b)
+    for p in (foreign, empty, prefix):
+        p.close()
+    other.close()
+
+
 def test_decisions_match_oracle(models):
     import clef_b200 as cb
     cfg, eng, ref = models

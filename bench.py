@@ -56,6 +56,9 @@ def parse():
                     help="config4 with a batch of --requests per rank (weak scaling) instead of "
                          "one batch divided over the ranks (strong scaling, the default)")
     ap.add_argument("--requests", type=int, default=256)
+    ap.add_argument("--precision", default="bf16", choices=["bf16", "split"],
+                    help="bf16: BF16 GEMM operands (default); split: split-BF16 activation operands and "
+                         "F32 projection outputs (F32-class projections, twice the tensor work)")
     ap.add_argument("--flash-tokens", type=int, default=4096, choices=[256, 1024, 4096],
                     help="request length of the flash workload (the reference's published lengths)")
     ap.add_argument("--layers", type=int, default=32)
@@ -87,14 +90,14 @@ FLASH_REFERENCE_TOK_S = {4096: 1101.0, 1024: 1248.0, 256: 1151.0}
 
 def workload_config(args, n_gpus):
     if args.workload == "flash":
-        return {"workload": f"flash geometry: 32-layer hybrid backbone (hidden 4096, intermediate 12288) "
+        return {"precision": args.precision, "workload": f"flash geometry: 32-layer hybrid backbone (hidden 4096, intermediate 12288) "
                             f"+ linear schema head, one {args.flash_tokens}-token request per GPU per step",
                 "vocab": 248320, "layers": args.layers, "hidden": 4096, "intermediate": 12288,
                 "parallelism": f"dp{n_gpus} (one request per rank, weights replicated)",
                 "baseline": "reference Metal mixed F16 on Apple M5 Pro (different hardware)",
                 "l2": "not flushed: every step streams ~17 GB of weights, far above the 126 MB L2"}
     if args.workload == "config5":
-        return {"workload": "config5: 32-layer hybrid backbone + linear schema head, prefix reuse",
+        return {"precision": args.precision, "workload": "config5: 32-layer hybrid backbone + linear schema head, prefix reuse",
                 "prefix_tokens": 16384, "suffixes_total": 64, "suffix_len": "U[512,4096]",
                 "vocab": 248320, "layers": args.layers, "hidden": 2560, "intermediate": 9216,
                 "parallelism": (f"dp{n_gpus} (suffixes LPT-sharded; prefix computed once on rank 0 and "
@@ -103,7 +106,7 @@ def workload_config(args, n_gpus):
     batch = ({"requests_per_gpu": args.requests} if args.weak
              else {"requests": args.requests, "requests_per_gpu": round(args.requests / n_gpus, 2)})
     return {"workload": "config4: 32-layer hybrid backbone + linear schema head",
-            **batch, "prompt_len": "U[256,2048]", "vocab": 248320,
+            "precision": args.precision, **batch, "prompt_len": "U[256,2048]", "vocab": 248320,
             "layers": args.layers, "hidden": 2560, "intermediate": 9216,
             "deltanet_heads": "16qk/32v x 128", "attention_heads": "16q/4kv x 256",
             "chunk": 64,
@@ -503,6 +506,8 @@ def main():
     eng = cb.Engine(cfg, local)
     eng.init_random(3, 0.02)
     eng.finalize()
+    split = args.precision == "split"
+    eng.set_precision(cb.PRECISION_SPLIT if split else cb.PRECISION_BF16)
     from clef_b200.sharding import rank_shard
     prefix = None
     prefix_ms = None
@@ -585,7 +590,9 @@ def main():
 
     # ---- roofline of the dominant kernel (the projection GEMMs) --------------
     pk, pk_kind = peaks()
-    lin_flops = tokens * linear_flops_per_token(cfg)
+    # Tensor-core work of the projections: twice the model's FLOPs when every
+    # activation operand is a split (hi + lo) pair.
+    lin_flops = tokens * linear_flops_per_token(cfg) * (2 if split else 1)
     gemm_ms = stages["gemm"] / args.steps
     achieved = lin_flops / (gemm_ms / 1000.0) / 1e12
     peak = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")))
@@ -593,7 +600,8 @@ def main():
     tf = ROOT / "profiles" / "gemm_traffic.txt"
     if tf.exists():
         traffic = json.loads(tf.read_text()).get("bytes_per_launch")
-    roofline = {"bound": "tensor", "kernel": "gemm_pair_kernel (tcgen05 cta_group::2 projection GEMMs, all launches)",
+    roofline = {"bound": "tensor", "kernel": "gemm_pair_kernel (tcgen05 cta_group::2 projection GEMMs, all launches)"
+                + (" with split-BF16 operands (tensor FLOPs = 2x model FLOPs)" if split else ""),
                 "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                 "frac": round(achieved / peak, 4), "peak_source": f"{pk_kind} bf16_tflops_sustained",
                 "traffic": traffic,

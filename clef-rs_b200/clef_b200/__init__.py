@@ -22,6 +22,7 @@ HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE.parent / "libclef_b200.so"
 
 F32, BF16 = 0, 1
+PRECISION_BF16, PRECISION_SPLIT = 0, 1
 EPI_BF16, EPI_F32, EPI_ADD_F32 = 0, 1, 2
 STATUS = {0: "OK", 1: "INVALID", 2: "CUDA", 3: "UNSUPPORTED", 4: "NOMEM", 5: "CANCELLED",
           6: "DEVICE_TIMEOUT"}
@@ -32,12 +33,13 @@ STAGES = ["embed", "norm", "gemm", "delta_prologue", "delta_scan", "delta_epilog
 EXPORTS = [
     "clef_last_error", "clef_version", "clef_config_validate", "clef_rmsnorm", "clef_conv4",
     "clef_delta_prologue", "clef_delta_scan_workspace_size", "clef_delta_scan",
-    "clef_delta_scan_noalloc", "clef_gemm_bf16",
+    "clef_delta_scan_noalloc", "clef_gemm_bf16", "clef_gemm_bf16_split",
     "clef_gemm_swiglu", "clef_attention_gqa", "clef_attention_gqa_vt", "clef_compact_copy",
     "clef_engine_create",
     "clef_engine_set_weight", "clef_engine_init_random", "clef_engine_get_weight",
     "clef_engine_weight_count", "clef_engine_finalize", "clef_engine_prefill",
-    "clef_engine_prefill_device", "clef_engine_launches", "clef_engine_cancel",
+    "clef_engine_prefill_device", "clef_engine_set_precision", "clef_engine_precision",
+    "clef_engine_launches", "clef_engine_cancel",
     "clef_engine_stage_times", "clef_engine_set_profiling", "clef_engine_destroy",
     "clef_prefix_tokens", "clef_prefix_bytes", "clef_prefix_destroy", "clef_prefix_span_bytes",
     "clef_prefix_create", "clef_prefix_export", "clef_prefix_import", "clef_head_create",
@@ -91,6 +93,7 @@ def _load():
         "clef_delta_scan_noalloc": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32,
                                                    _vp, _i32, _vp, _i32, _i64, _vp, _vp, _vp, _vp]),
         "clef_gemm_bf16": (ctypes.c_int, [_vp, _vp, _i64, _i32, _i32, _i32, _vp, _i64, _vp]),
+        "clef_gemm_bf16_split": (ctypes.c_int, [_vp, _vp, _i64, _i32, _i32, _i32, _vp, _i64, _vp]),
         "clef_gemm_swiglu": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i32, _i32, _vp, _vp]),
         "clef_attention_gqa": (ctypes.c_int, [_vp, _vp, _vp, _i32, _i32, _i64, _i64, _i32, _vp, _vp]),
         "clef_attention_gqa_vt": (ctypes.c_int, [_vp, _vp, _vp, _i32, _i32, _i64, _i64, _i32, _i64, _vp,
@@ -106,6 +109,8 @@ def _load():
                                                _vp, _vp]),
         "clef_engine_prefill_device": (ctypes.c_int, [_vp, _vp, _vp, _i32, _vp, _vp, _vp]),
         "clef_engine_launches": (_i64, [_vp]),
+        "clef_engine_set_precision": (ctypes.c_int, [_vp, _i32]),
+        "clef_engine_precision": (_i32, [_vp]),
         "clef_engine_cancel": (ctypes.c_int, [_vp, _i32]),
         "clef_engine_stage_times": (ctypes.c_int, [_vp, _vp, _i32]),
         "clef_engine_set_profiling": (ctypes.c_int, [_vp, _i32]),
@@ -269,6 +274,28 @@ def gemm(x, w, epilogue=EPI_BF16, out=None, stream=None):
     return out
 
 
+def split_bf16(x):
+    """(hi | lo) BF16 pair of an F32 tensor [M, K] as one [M, 2K] tensor:
+    hi = bf16(x), lo = bf16(x - hi)."""
+    import torch
+    hi = x.float().bfloat16()
+    lo = (x.float() - hi.float()).bfloat16()
+    return torch.cat([hi, lo], dim=1).contiguous()
+
+
+def gemm_split(x2, w, epilogue=EPI_F32, out=None, stream=None):
+    """x2 BF16 [M, 2K] split pair (split_bf16), w BF16 [N, K]: (hi + lo) w^T."""
+    import torch
+    M, K2 = x2.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16 if epilogue == EPI_BF16 else torch.float32,
+                          device=x2.device)
+    _check(lib.clef_gemm_bf16_split(_ptr(x2), _ptr(w), M, N, K2 // 2, epilogue, _ptr(out), out.stride(0),
+                                    _stream(stream)))
+    return out
+
+
 def gemm_swiglu(x, wg, wu, out=None, stream=None):
     """gated TileKernel / Projection::gated_forward: silu(x wg^T) * (x wu^T)."""
     import torch
@@ -404,6 +431,15 @@ class Engine:
 
     def finalize(self) -> None:
         _check(lib.clef_engine_finalize(self.handle))
+
+    def set_precision(self, precision: int) -> None:
+        """PRECISION_BF16 (default) or PRECISION_SPLIT (split-BF16 operands and
+        F32 projection outputs: F32-class projections at twice the tensor work)."""
+        _check(lib.clef_engine_set_precision(self.handle, int(precision)))
+
+    @property
+    def precision(self) -> int:
+        return int(lib.clef_engine_precision(self.handle))
 
     def set_profiling(self, on: bool) -> None:
         _check(lib.clef_engine_set_profiling(self.handle, int(on)))

@@ -414,10 +414,11 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint32_t ow[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const float g0 = bf16_round(sigmoid_f(__uint_as_float(gw[e] << 16)));
-              const float g1 = bf16_round(sigmoid_f(__uint_as_float(gw[e] & 0xffff0000u)));
-              const float v0 = bf16_round(__uint_as_float(o[e4 * 8 + 2 * e]) * inv);
-              const float v1 = bf16_round(__uint_as_float(o[e4 * 8 + 2 * e + 1]) * inv);
+              // o * sigmoid(gate) in F32, rounded once (the o_proj operand).
+              const float g0 = sigmoid_f(__uint_as_float(gw[e] << 16));
+              const float g1 = sigmoid_f(__uint_as_float(gw[e] & 0xffff0000u));
+              const float v0 = __uint_as_float(o[e4 * 8 + 2 * e]) * inv;
+              const float v1 = __uint_as_float(o[e4 * 8 + 2 * e + 1]) * inv;
               ow[e] = pack_bf16x2(v0 * g0, v1 * g1);
             }
             *reinterpret_cast<uint4*>(op + e4 * 8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
@@ -442,8 +443,16 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // V^T: vt[kvh * 256 + e][vt_off(s) + j] = v[(cu[s] + j) * v_ts + kvh * v_hs + e], one
-// 64-key x 256-feature tile per CTA through shared memory.
-__global__ void transpose_v_kernel(const uint16_t* __restrict__ v, int64_t v_ts, int64_t v_hs,
+// 64-key x 256-feature tile per CTA through shared memory. V is BF16, or F32
+// (rounded to the BF16 operand here).
+__device__ __forceinline__ uint4 load_v8(const uint16_t* p) { return *reinterpret_cast<const uint4*>(p); }
+__device__ __forceinline__ uint4 load_v8(const float* p) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  return make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(b.x, b.y), pack_bf16x2(b.z, b.w));
+}
+
+template <typename In>
+__global__ void transpose_v_kernel(const In* __restrict__ v, int64_t v_ts, int64_t v_hs,
                                    const int64_t* __restrict__ cu, const int64_t* __restrict__ cu_vt,
                                    const int32_t* __restrict__ cu_kb, int nseq, int64_t total,
                                    uint16_t* __restrict__ vt, int64_t vt_pitch) {
@@ -463,7 +472,7 @@ __global__ void transpose_v_kernel(const uint16_t* __restrict__ v, int64_t v_ts,
   for (int idx = threadIdx.x; idx < 64 * (D / 8); idx += blockDim.x) {
     const int j = idx / (D / 8), e8 = (idx % (D / 8)) * 8;
     uint4 val = make_uint4(0, 0, 0, 0);
-    if (j0 + j < len) val = *reinterpret_cast<const uint4*>(v + (start + j0 + j) * v_ts + kvh * v_hs + e8);
+    if (j0 + j < len) val = load_v8(v + (start + j0 + j) * v_ts + kvh * v_hs + e8);
     const uint32_t w[4] = {val.x, val.y, val.z, val.w};
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
@@ -515,13 +524,24 @@ int map2d(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t cols, uint64_
 
 }  // namespace
 
-int launch_transpose_v(const uint16_t* v, int64_t v_ts, int64_t v_hs, const SeqPackVT& pk, int Hkv,
-                       uint16_t* vt, int64_t vt_pitch, cudaStream_t s) {
+template <typename In>
+int launch_transpose_v_t(const In* v, int64_t v_ts, int64_t v_hs, const SeqPackVT& pk, int Hkv,
+                         uint16_t* vt, int64_t vt_pitch, cudaStream_t s) {
   if (pk.total == 0) return CLEF_OK;
   const unsigned blocks = pk.cu ? (unsigned)pk.kblocks : (unsigned)ceil_div(pk.total, 64);
-  transpose_v_kernel<<<dim3(blocks, (unsigned)Hkv), 256, 0, s>>>(v, v_ts, v_hs, pk.cu, pk.cu_vt, pk.cu_kb,
-                                                              pk.nseq, pk.total, vt, vt_pitch);
+  transpose_v_kernel<In><<<dim3(blocks, (unsigned)Hkv), 256, 0, s>>>(v, v_ts, v_hs, pk.cu, pk.cu_vt, pk.cu_kb,
+                                                                  pk.nseq, pk.total, vt, vt_pitch);
   return launch_status("transpose_v");
+}
+
+int launch_transpose_v(const uint16_t* v, int64_t v_ts, int64_t v_hs, const SeqPackVT& pk, int Hkv,
+                       uint16_t* vt, int64_t vt_pitch, cudaStream_t s) {
+  return launch_transpose_v_t(v, v_ts, v_hs, pk, Hkv, vt, vt_pitch, s);
+}
+
+int launch_transpose_v(const float* v, int64_t v_ts, int64_t v_hs, const SeqPackVT& pk, int Hkv,
+                       uint16_t* vt, int64_t vt_pitch, cudaStream_t s) {
+  return launch_transpose_v_t(v, v_ts, v_hs, pk, Hkv, vt, vt_pitch, s);
 }
 
 int launch_attention_tc(const AttnTcArgs& a, const SeqPackVT& pk, cudaStream_t s) {

@@ -100,6 +100,12 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return r;
 }
 
+// Split BF16 pair of two floats: hi = bf16(x), lo = bf16(x - hi) (x - hi is
+// exact in F32), so hi + lo carries x to about 2^-17 relative.
+__device__ __forceinline__ uint32_t split_lo_bf16x2(float a, float b, uint32_t hi) {
+  return pack_bf16x2(a - __uint_as_float(hi << 16), b - __uint_as_float(hi & 0xffff0000u));
+}
+
 // Candle's CPU definitions: sigmoid = 1 / (1 + exp(-x)), silu = x / (1 + exp(-x)).
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
 __device__ __forceinline__ float silu_f(float x) { return x / (1.f + expf(-x)); }

@@ -16,8 +16,16 @@
 //   - The prefix state (PrefixState, qwen.rs:153-190) lives on the device:
 //     recurrent S and the last <= 3 conv rows per DeltaNet layer, K/V rows per
 //     attention layer, and the captured final-normed hidden rows.
-// The residual stream is F32 and projections are BF16 with F32 accumulation,
-// as in the reference's mixed-precision device profiles.
+// The residual stream is F32 and projections are BF16 with F32 accumulation.
+// Two precisions (clef_engine_set_precision):
+//   CLEF_PRECISION_BF16   every GEMM operand is BF16, the fused in-projection
+//                         and attention q/k/v projection outputs are BF16;
+//   CLEF_PRECISION_SPLIT  every GEMM activation operand is a split BF16 pair
+//                         (hi + lo, twice the tensor work) and the projection
+//                         outputs are F32, so the projections match F32
+//                         arithmetic to ~2^-17; only the attention's q, k, v
+//                         and probabilities stay single BF16 operands.
+// Everything between the GEMMs (norms, conv, gates, scan, gating) is F32 in both.
 #include <algorithm>
 #include <atomic>
 #include <cmath>
@@ -114,6 +122,8 @@ struct clef_engine {
   void* wblob = nullptr;
   float* inv_freq = nullptr;
   bool finalized = false;
+  int precision = CLEF_PRECISION_BF16;
+  int arena_precision = -1;  // precision the activation arena was sized for
   std::atomic<int> cancel{0};
   // geometry
   int key = 0, value = 0, qkv_w = 0, n_in = 0, att_n = 0, att_kv = 0, n_att = 0;
@@ -310,7 +320,9 @@ size_t meta_bytes(size_t n1) {
 }
 
 int ensure_capacity(clef_engine* e, int64_t tokens, int64_t seqs) {
-  if (tokens <= e->cap_tokens && seqs <= e->cap_seqs && e->arena) return CLEF_OK;
+  if (tokens <= e->cap_tokens && seqs <= e->cap_seqs && e->arena && e->arena_precision == e->precision)
+    return CLEF_OK;
+  const int x2 = e->precision == CLEF_PRECISION_SPLIT ? 2 : 1;  // split operands: hi | lo
   const clef_config& c = e->cfg;
   tokens = std::max(tokens, e->cap_tokens);
   seqs = std::max(seqs, e->cap_seqs);
@@ -326,18 +338,18 @@ int ensure_capacity(clef_engine* e, int64_t tokens, int64_t seqs) {
   take(sizeof(int32_t) * M);                              // 0 ids
   take(meta_bytes((size_t)seqs + 1));                     // 1 meta
   take(sizeof(float) * M * hid);                          // 2 h
-  take(sizeof(uint16_t) * M * std::max(e->n_in, e->n_att));  // 3 proj (BF16)
+  take(sizeof(uint16_t) * x2 * M * std::max(e->n_in, e->n_att));  // 3 proj (BF16, or F32 when split)
   take(sizeof(float) * M * e->key);                       // 4 dq
   take(sizeof(float) * M * e->key);                       // 5 dk
   take(sizeof(float) * M * e->value);                     // 6 dv
   take(sizeof(float) * M * hv);                           // 7 dg
   take(sizeof(float) * M * hv);                           // 8 db
-  take(sizeof(float) * M * e->value);                     // 9 dout
-  take(sizeof(uint16_t) * M * hid);                       // 10 u
-  take(sizeof(uint16_t) * M * std::max(e->value, e->att_n));  // 11 y
+  take(sizeof(float) * M * std::max(e->value, e->att_n));  // 9 dout (scan out; F32 attention out when split)
+  take(sizeof(uint16_t) * x2 * M * hid);                  // 10 u
+  take(sizeof(uint16_t) * x2 * M * std::max(e->value, e->att_n));  // 11 y
   take(sizeof(uint16_t) * M * e->att_n);                  // 12 qatt
   take(sizeof(uint16_t) * M * e->att_kv);                 // 13 katt
-  take(sizeof(uint16_t) * M * c.intermediate_size);       // 14 act
+  take(sizeof(uint16_t) * x2 * M * c.intermediate_size);  // 14 act
   take(sizeof(float) * seqs * std::max(1, c.head_outputs));  // 15 logits
   const size_t ws = delta_scan_workspace(M, (int)seqs, c.linear_num_key_heads, hv);
   take(ws);                                               // 16 scan ws
@@ -369,6 +381,7 @@ int ensure_capacity(clef_engine* e, int64_t tokens, int64_t seqs) {
   e->vt_pitch = vt_pitch;
   e->scan_ws_bytes = ws;
   e->arena_bytes = b;
+  e->arena_precision = e->precision;
   e->cap_tokens = tokens;
   e->cap_seqs = seqs;
   return CLEF_OK;
@@ -543,7 +556,10 @@ int run_pack(clef_engine* e, const int32_t* ids, const int64_t* offsets, int s0,
   else CLEF_CUDA(cudaMemcpyAsync(e->ids_d, ids + t0, sizeof(int32_t) * M, cudaMemcpyHostToDevice, s));
   {
     int64_t n = 2;  // embed + head
-    for (int li = 0; li < c.num_hidden_layers; ++li) n += 9;  // 2 norms, 4 GEMMs, 3 mixer kernels
+    for (int li = 0; li < c.num_hidden_layers; ++li) {
+      n += 9;  // 2 norms, 4 GEMMs, 3 mixer kernels
+      if (c.layer_types[li] && e->precision == CLEF_PRECISION_SPLIT) n += 1;  // gate split
+    }
     if (hidden || cap) n += 1;
     e->launches += n;
   }
@@ -562,6 +578,9 @@ int run_pack(clef_engine* e, const int32_t* ids, const int64_t* offsets, int s0,
     STAGE(kStEmbed);
     RC(launch_embed(e->embed, ids_src, M, hid, e->h, s));
   }
+  const bool split = e->precision == CLEF_PRECISION_SPLIT;
+  const int x2 = split ? 2 : 1;
+  const int norm_out = split ? kOutBF16Split : CLEF_BF16;
   for (int li = 0; li < c.num_hidden_layers; ++li) {
     if (e->cancel.load()) {
       cudaStreamSynchronize(s);
@@ -570,23 +589,32 @@ int run_pack(clef_engine* e, const int32_t* ids, const int64_t* offsets, int s0,
     const LayerW& L = e->layers[li];
     {
       STAGE(kStNorm);
-      RC(launch_rmsnorm(e->h, L.in_eff, M, hid, eps, CLEF_BF16, e->u, s));
+      RC(launch_rmsnorm(e->h, L.in_eff, M, hid, eps, norm_out, e->u, s));
     }
     if (!L.attention) {
-      // in_proj_qkv | z | a | b output in BF16: the reference's BF16 path rounds
-      // the projection to the model dtype before widening (qwen.rs:603, 619, 626, 669).
+      // in_proj_qkv | z | a | b: BF16 output in the default precision (the
+      // model dtype of the reference's mixed-precision path, qwen.rs:603, 619,
+      // 626, 669), F32 in the split precision.
       uint16_t* pin = reinterpret_cast<uint16_t*>(e->proj);
+      float* pin32 = e->proj;
       {
         STAGE(kStGemm);
-        RC(launch_gemm(e->u, L.w_in, nullptr, M, L.n_in, hid, kEpiBF16, pin, L.n_in, s));
+        if (split) RC(launch_gemm(e->u, L.w_in, nullptr, M, L.n_in, hid, kEpiF32, pin32, L.n_in, s, 1));
+        else RC(launch_gemm(e->u, L.w_in, nullptr, M, L.n_in, hid, kEpiBF16, pin, L.n_in, s));
       }
       const clef_prefix::Layer* il = init ? &init->layers[li] : nullptr;
       {
         STAGE(kStDeltaPro);
-        RC(launch_delta_prologue(pin, L.n_in, e->qkv_w + e->value, e->qkv_w + e->value + hv,
-                                 il ? il->hist : nullptr, il ? il->hist_rows : 0, L.conv, L.dt,
-                                 L.alog, pack, hk, hv, 128, 128, e->dq, e->dk, e->dv, e->dg, e->db,
-                                 s));
+        if (split)
+          RC(launch_delta_prologue(pin32, L.n_in, e->qkv_w + e->value, e->qkv_w + e->value + hv,
+                                   il ? il->hist : nullptr, il ? il->hist_rows : 0, L.conv, L.dt,
+                                   L.alog, pack, hk, hv, 128, 128, e->dq, e->dk, e->dv, e->dg, e->db,
+                                   s));
+        else
+          RC(launch_delta_prologue(pin, L.n_in, e->qkv_w + e->value, e->qkv_w + e->value + hv,
+                                   il ? il->hist : nullptr, il ? il->hist_rows : 0, L.conv, L.dt,
+                                   L.alog, pack, hk, hv, 128, 128, e->dq, e->dk, e->dv, e->dg, e->db,
+                                   s));
       }
       {
         STAGE(kStDeltaScan);
@@ -596,33 +624,46 @@ int run_pack(clef_engine* e, const int32_t* ids, const int64_t* offsets, int s0,
       }
       if (cap) {
         auto& cl = cap->layers[li];
-        RC(launch_rows_bf16_to_f32(pin, L.n_in, capture - cl.hist_rows, cl.hist_rows, e->qkv_w, cl.hist,
-                                   e->qkv_w, s));
+        if (split)
+          RC(launch_copy_rows(pin32, L.n_in, capture - cl.hist_rows, cl.hist_rows, e->qkv_w, 4, cl.hist,
+                              e->qkv_w, s));
+        else
+          RC(launch_rows_bf16_to_f32(pin, L.n_in, capture - cl.hist_rows, cl.hist_rows, e->qkv_w, cl.hist,
+                                     e->qkv_w, s));
       }
       {
         STAGE(kStDeltaEpi);
-        RC(launch_delta_epilogue(e->dout, pin + e->qkv_w, L.n_in, L.dnorm, eps, M, hv, 128,
-                                 e->y, s));
+        if (split)
+          RC(launch_delta_epilogue_split(e->dout, pin32 + e->qkv_w, L.n_in, L.dnorm, eps, M, hv, e->y, s));
+        else
+          RC(launch_delta_epilogue(e->dout, pin + e->qkv_w, L.n_in, L.dnorm, eps, M, hv, 128, e->y, s));
       }
       {
         STAGE(kStGemm);
-        RC(launch_gemm(e->y, L.w_out, nullptr, M, hid, e->value, kEpiAddF32, e->h, hid, s));
+        RC(launch_gemm(e->y, L.w_out, nullptr, M, hid, e->value, kEpiAddF32, e->h, hid, s, split));
       }
     } else {
       uint16_t* pb = reinterpret_cast<uint16_t*>(e->proj);
+      float* pb32 = e->proj;
       {
         STAGE(kStGemm);
-        RC(launch_gemm(e->u, L.w_att, nullptr, M, L.n_att, hid, kEpiBF16, pb, L.n_att, s));
+        if (split) RC(launch_gemm(e->u, L.w_att, nullptr, M, L.n_att, hid, kEpiF32, pb32, L.n_att, s, 1));
+        else RC(launch_gemm(e->u, L.w_att, nullptr, M, L.n_att, hid, kEpiBF16, pb, L.n_att, s));
       }
       {
         STAGE(kStAttnPro);
-        RC(launch_attention_prologue(pb, L.n_att, L.qn, L.kn, eps, pack, P, H, Hkv, d, c.rotary_dim,
-                                     e->inv_freq, e->qatt, e->katt, s));
+        if (split)
+          RC(launch_attention_prologue(pb32, L.n_att, L.qn, L.kn, eps, pack, P, H, Hkv, d, c.rotary_dim,
+                                       e->inv_freq, e->qatt, e->katt, s));
+        else
+          RC(launch_attention_prologue(pb, L.n_att, L.qn, L.kn, eps, pack, P, H, Hkv, d, c.rotary_dim,
+                                       e->inv_freq, e->qatt, e->katt, s));
       }
       const int v_col = 2 * e->att_n + e->att_kv;
       {
         STAGE(kStAttnPro);
-        RC(launch_transpose_v(pb + v_col, L.n_att, d, vpack, Hkv, e->vt, e->vt_pitch, s));
+        if (split) RC(launch_transpose_v(pb32 + v_col, L.n_att, d, vpack, Hkv, e->vt, e->vt_pitch, s));
+        else RC(launch_transpose_v(pb + v_col, L.n_att, d, vpack, Hkv, e->vt, e->vt_pitch, s));
       }
       if (cap) {
         auto& cl = cap->layers[li];
@@ -649,31 +690,42 @@ int run_pack(clef_engine* e, const int32_t* ids, const int64_t* offsets, int s0,
         a.pvt = init->layers[li].vt;
         a.pvt_pitch = init->vt_pitch;
       }
-      a.gate = pb + d;
-      a.g_ts = L.n_att;
-      a.g_hs = 2 * d;
-      a.out = e->y;
-      a.o_ts = e->att_n;
-      a.o_hs = d;
+      if (split) {
+        // F32 attention output; the gate product and its split follow.
+        a.out = e->dout;
+        a.o_ts = e->att_n;
+        a.o_hs = d;
+      } else {
+        a.gate = pb + d;
+        a.g_ts = L.n_att;
+        a.g_hs = 2 * d;
+        a.out = e->y;
+        a.o_ts = e->att_n;
+        a.o_hs = d;
+      }
       {
         STAGE(kStAttn);
         RC(launch_attention_tc(a, vpack, s));
       }
+      if (split) {
+        STAGE(kStAttnPro);
+        RC(launch_gate_split(e->dout, pb32 + d, L.n_att, 2 * d, H, d, M, e->y, s));
+      }
       {
         STAGE(kStGemm);
-        RC(launch_gemm(e->y, L.w_o, nullptr, M, hid, e->att_n, kEpiAddF32, e->h, hid, s));
+        RC(launch_gemm(e->y, L.w_o, nullptr, M, hid, e->att_n, kEpiAddF32, e->h, hid, s, split));
       }
     }
     {
       STAGE(kStNorm);
-      RC(launch_rmsnorm(e->h, L.post_eff, M, hid, eps, CLEF_BF16, e->u, s));
+      RC(launch_rmsnorm(e->h, L.post_eff, M, hid, eps, norm_out, e->u, s));
     }
     {
       STAGE(kStGemm);
-      RC(launch_gemm(e->u, L.w_gate, L.w_up, M, c.intermediate_size, hid, kEpiSwiGLU, e->act,
-                     c.intermediate_size, s));
+      RC(launch_gemm(e->u, L.w_gate, L.w_up, M, c.intermediate_size, hid, split ? kEpiSwiGLUSplit : kEpiSwiGLU,
+                     e->act, (int64_t)x2 * c.intermediate_size, s, split));
       RC(launch_gemm(e->act, L.w_down, nullptr, M, hid, c.intermediate_size, kEpiAddF32, e->h, hid,
-                     s));
+                     s, split));
     }
   }
   if ((logits || logits_dev) && c.head_outputs) {
@@ -954,6 +1006,22 @@ int clef_engine_prefill_device(clef_engine* e, const int32_t* ids_device, const 
 }
 
 int64_t clef_engine_launches(const clef_engine* e) { return e ? e->launches : 0; }
+
+int clef_engine_set_precision(clef_engine* e, int32_t precision) {
+  CLEF_CHECK(e, CLEF_ERR_INVALID, "set_precision: null engine");
+  CLEF_CHECK(precision == CLEF_PRECISION_BF16 || precision == CLEF_PRECISION_SPLIT, CLEF_ERR_INVALID,
+             "set_precision: unknown precision");
+  if (precision != e->precision) {
+    // The arena is resized on the next prefill; pending work must not use it.
+    DeviceGuard g(e->device);
+    CLEF_CUDA(cudaStreamSynchronize(e->stream));
+    CLEF_CUDA(cudaDeviceSynchronize());
+    e->precision = precision;
+  }
+  return CLEF_OK;
+}
+
+int32_t clef_engine_precision(const clef_engine* e) { return e ? e->precision : -1; }
 
 int clef_engine_cancel(clef_engine* e, int32_t cancel) {
   CLEF_CHECK(e, CLEF_ERR_INVALID, "cancel: null engine");

@@ -15,7 +15,14 @@
 //               release the accumulator so the next tile's MMAs overlap it.
 // Epilogues: BF16 store, F32 store, F32 residual add (h += X W^T), and the
 // fused SwiGLU silu(X Wg^T) * (X Wu^T) (the B tile holds 128 gate rows and
-// 128 up rows of the same output columns).
+// 128 up rows of the same output columns), stored as BF16 or as a split pair.
+//
+// Split operands: X may hold each activation as two BF16 halves, x = hi + lo
+// with hi = bf16(x) and lo = bf16(x - hi), in columns [0, K) and [K, 2K) of a
+// [M, 2K] matrix. The kernel then walks 2K columns of X while the K slabs of W
+// wrap around (slab kb of X meets slab kb mod K/64 of W), so one accumulator
+// receives hi W^T + lo W^T: the product of the activation to about 2^-17 of
+// its value instead of BF16's 2^-9, at twice the tensor work.
 #include <cudaTypedefs.h>
 
 #include "kernels.cuh"
@@ -40,7 +47,8 @@ constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
 struct GemmParams {
   int64_t M;
   int N;        // output columns
-  int K;
+  int K;        // columns of X walked by the MMA loop (2 x W's K for split operands)
+  int kb_w;     // 64-wide K slabs of W (== K / 64 unless X is split)
   int epi;
   void* out;
   int64_t ldo;
@@ -91,6 +99,28 @@ __device__ __forceinline__ void store_tile(const GemmParams& p, uint32_t tbase, 
 #pragma unroll
           for (int j = 0; j < 32; ++j)
             if (n0 + j < p.N) dst[j] = (uint16_t)((packed[j >> 1] >> ((j & 1) * 16)) & 0xffff);
+        }
+        if (p.epi == kEpiSwiGLUSplit) {
+          // Low halves: y - bf16(y), columns [N, 2N) of the row.
+          uint32_t low[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float g0 = u2f(gr[2 * j]), g1 = u2f(gr[2 * j + 1]);
+            const float y0 = silu_f(g0) * u2f(ur[2 * j]);
+            const float y1 = silu_f(g1) * u2f(ur[2 * j + 1]);
+            low[j] = pack_bf16x2(y0 - __uint_as_float(packed[j] << 16),
+                                 y1 - __uint_as_float(packed[j] & 0xffff0000u));
+          }
+          uint16_t* dlo = dst + p.N;
+          if (n0 + 32 <= p.N) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              reinterpret_cast<uint4*>(dlo)[j] = make_uint4(low[4 * j], low[4 * j + 1], low[4 * j + 2], low[4 * j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < p.N) dlo[j] = (uint16_t)((low[j >> 1] >> ((j & 1) * 16)) & 0xffff);
+          }
         }
       }
     }
@@ -160,7 +190,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const bool swiglu = p.epi == kEpiSwiGLU;
+  const bool swiglu = p.epi == kEpiSwiGLU || p.epi == kEpiSwiGLUSplit;
   const int num_tiles = p.tiles_m * p.tiles_n;
   const int nk = p.K / BK;
 
@@ -203,12 +233,13 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint8_t* sa = smem + (size_t)stage * STAGE_BYTES;
           uint8_t* sb = sa + A_BYTES;
           mbar_expect_tx(&full[stage], STAGE_BYTES);
+          const int kw = (kb % p.kb_w) * BK;  // W's slab (wraps for split X)
           tma_load_2d(&map_a, &full[stage], sa, kb * BK, tm * BM);
           if (swiglu) {
-            tma_load_2d(&map_b, &full[stage], sb, kb * BK, tn * 128);
-            tma_load_2d(&map_b2, &full[stage], sb + B_BYTES / 2, kb * BK, tn * 128);
+            tma_load_2d(&map_b, &full[stage], sb, kw, tn * 128);
+            tma_load_2d(&map_b2, &full[stage], sb + B_BYTES / 2, kw, tn * 128);
           } else {
-            tma_load_2d(&map_b, &full[stage], sb, kb * BK, tn * BN);
+            tma_load_2d(&map_b, &full[stage], sb, kw, tn * BN);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -325,7 +356,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
-  const bool swiglu = p.epi == kEpiSwiGLU;
+  const bool swiglu = p.epi == kEpiSwiGLU || p.epi == kEpiSwiGLUSplit;
   const int num_tiles = p.tiles_m * p.tiles_n;
   const int nk = p.K / BK;
 
@@ -372,11 +403,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           uint8_t* sb = sa + P_A_BYTES;
           if (leader) mbar_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
           const uint32_t bar = full0 + (uint32_t)(stage * sizeof(uint64_t));
+          const int kw = (kb % p.kb_w) * BK;  // W's slab (wraps for split X)
           tma_load_2d_pair(&map_a, bar, sa, kb * BK, tm * 256 + (int)rank * 128);
           if (swiglu)
-            tma_load_2d_pair(leader ? &map_b : &map_b2, bar, sb, kb * BK, tn * 128);
+            tma_load_2d_pair(leader ? &map_b : &map_b2, bar, sb, kw, tn * 128);
           else
-            tma_load_2d_pair(&map_b, bar, sb, kb * BK, tn * BN + (int)rank * 128);
+            tma_load_2d_pair(&map_b, bar, sb, kw, tn * BN + (int)rank * 128);
           if (++stage == P_STAGES) {
             stage = 0;
             phase ^= 1;
@@ -501,20 +533,22 @@ int make_map(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols, ui
 }  // namespace
 
 int launch_gemm(const uint16_t* X, const uint16_t* W, const uint16_t* W2, int64_t M, int N, int K,
-                int epi, void* out, int64_t ldo, cudaStream_t s) {
+                int epi, void* out, int64_t ldo, cudaStream_t s, int x_split) {
   if (M == 0) return CLEF_OK;
   CLEF_CHECK(K % BK == 0 && K > 0, CLEF_ERR_UNSUPPORTED, "gemm: K must be a multiple of 64");
   CLEF_CHECK(N > 0 && N % 16 == 0, CLEF_ERR_UNSUPPORTED, "gemm: N must be a multiple of 16");
   CLEF_CHECK(M <= (int64_t)INT32_MAX - BM, CLEF_ERR_UNSUPPORTED, "gemm: M too large");
   CLEF_CHECK(((uintptr_t)X & 15) == 0 && ((uintptr_t)W & 15) == 0 && ((uintptr_t)out & 15) == 0,
              CLEF_ERR_INVALID, "gemm: operands must be 16-byte aligned");
-  const bool swiglu = epi == kEpiSwiGLU;
+  const bool swiglu = epi == kEpiSwiGLU || epi == kEpiSwiGLUSplit;
   const int elem = (epi == kEpiBF16 || swiglu) ? 2 : 4;
-  CLEF_CHECK(ldo >= N && (ldo * elem) % 16 == 0, CLEF_ERR_INVALID,
-             "gemm: ldo must cover N and keep rows 16-byte aligned");
+  const int out_cols = epi == kEpiSwiGLUSplit ? 2 * N : N;
+  CLEF_CHECK(ldo >= out_cols && (ldo * elem) % 16 == 0, CLEF_ERR_INVALID,
+             "gemm: ldo must cover the output columns and keep rows 16-byte aligned");
   CUtensorMap ma, mb, mb2;
   const bool pair_maps = M > BM;  // the CTA-pair kernel loads 128-row halves of B
-  int rc = make_map(&ma, X, (uint64_t)M, (uint64_t)K, BM);
+  const int xk = x_split ? 2 * K : K;  // columns of X (hi | lo halves when split)
+  int rc = make_map(&ma, X, (uint64_t)M, (uint64_t)xk, BM);
   if (rc) return rc;
   if (swiglu) {
     CLEF_CHECK(W2 && ((uintptr_t)W2 & 15) == 0, CLEF_ERR_INVALID, "gemm: SwiGLU up matrix");
@@ -529,7 +563,8 @@ int launch_gemm(const uint16_t* X, const uint16_t* W, const uint16_t* W2, int64_
   GemmParams p;
   p.M = M;
   p.N = N;
-  p.K = K;
+  p.K = xk;
+  p.kb_w = K / BK;
   p.epi = epi;
   p.out = out;
   p.ldo = ldo;
@@ -571,6 +606,15 @@ int clef_gemm_bf16(const uint16_t* X, const uint16_t* W, int64_t M, int32_t N, i
   CLEF_CHECK(epilogue >= CLEF_EPI_STORE_BF16 && epilogue <= CLEF_EPI_ADD_F32, CLEF_ERR_INVALID,
              "gemm_bf16: epilogue");
   return launch_gemm(X, W, nullptr, M, N, K, epilogue, out, ldo, as_stream(stream));
+}
+
+int clef_gemm_bf16_split(const uint16_t* X2, const uint16_t* W, int64_t M, int32_t N, int32_t K,
+                         int32_t epilogue, void* out, int64_t ldo, void* stream) {
+  CLEF_CHECK(X2 && W && out, CLEF_ERR_INVALID, "gemm_bf16_split: null pointer");
+  CLEF_CHECK(M >= 0, CLEF_ERR_INVALID, "gemm_bf16_split: M");
+  CLEF_CHECK(epilogue >= CLEF_EPI_STORE_BF16 && epilogue <= CLEF_EPI_ADD_F32, CLEF_ERR_INVALID,
+             "gemm_bf16_split: epilogue");
+  return launch_gemm(X2, W, nullptr, M, N, K, epilogue, out, ldo, as_stream(stream), 1);
 }
 
 int clef_gemm_swiglu(const uint16_t* X, const uint16_t* Wg, const uint16_t* Wu, int64_t M,

@@ -19,6 +19,9 @@ struct SeqPack {
 };
 
 // ---- pointwise.cu ----------------------------------------------------------
+// out_dtype: CLEF_F32, CLEF_BF16, or kOutBF16Split (out [rows, 2 * width]
+// BF16: hi = bf16(x) in columns [0, width), lo = bf16(x - hi) in [width, 2 width)).
+constexpr int kOutBF16Split = 2;
 int launch_rmsnorm(const float* x, const float* w, int64_t rows, int width, float eps,
                    int out_dtype, void* out, cudaStream_t s);
 int launch_conv4(const float* x, int64_t ldx, const float* hist, int hist_rows, const float* w,
@@ -34,15 +37,26 @@ int launch_delta_prologue(const uint16_t* proj, int64_t ldp, int a_col, int b_co
                           int hist_rows, const float* conv_w, const float* dt_bias,
                           const float* a_log, const SeqPack& pack, int Hk, int Hv, int dk, int dv,
                           float* q, float* k, float* v, float* g, float* beta, cudaStream_t s);
-// y[t, h*dv + i] = bf16(bf16(rms(bf16(o))*w) * silu(bf16(z))) for each v-head.
+// y[t, h*dv + i] = bf16(rms(o) * w * silu(z)) for each v-head (F32 math).
 int launch_delta_epilogue(const float* o, const uint16_t* z, int64_t ldz, const float* w, float eps,
                           int64_t T, int Hv, int dv, uint16_t* y, cudaStream_t s);
+// Same from F32 z rows, y stored as the split BF16 pair [T, 2 * Hv * 128].
+int launch_delta_epilogue_split(const float* o, const float* z, int64_t ldz, const float* w, float eps,
+                                int64_t T, int Hv, uint16_t* y, cudaStream_t s);
 // Attention prologue: q/k RMSNorm (offset weights already +1) and partial
 // RoPE from the fused BF16 projection; positions = offset + index in sequence.
 int launch_attention_prologue(const uint16_t* proj, int64_t ldp, const float* qw, const float* kw,
                               float eps, const SeqPack& pack, int64_t pos_offset, int H, int Hkv,
                               int d, int rot, const float* inv_freq_dev, uint16_t* q_out,
                               uint16_t* k_out, cudaStream_t s);
+// Same from the F32 projection rows of the engine's split precision.
+int launch_attention_prologue(const float* proj, int64_t ldp, const float* qw, const float* kw,
+                              float eps, const SeqPack& pack, int64_t pos_offset, int H, int Hkv,
+                              int d, int rot, const float* inv_freq_dev, uint16_t* q_out,
+                              uint16_t* k_out, cudaStream_t s);
+// y [T, 2 * H * d] = split BF16 pair of o [T, H, d] * sigmoid(gate[t*g_ts + h*g_hs + e]).
+int launch_gate_split(const float* o, const float* gate, int64_t g_ts, int64_t g_hs, int H, int d, int64_t T,
+                      uint16_t* y, cudaStream_t s);
 int launch_embed(const uint16_t* table, const int32_t* ids, int64_t T, int hidden, float* h,
                  cudaStream_t s);
 // Final RMSNorm of each sequence's last row and the linear schema head.
@@ -97,11 +111,15 @@ void host_fill(float* dst, int64_t n, uint64_t seed, uint64_t stream, int kind, 
 enum HostFill { kFillNormal = 0, kFillUniform = 1 };
 
 // ---- gemm.cu ----------------------------------------------------------------
-enum GemmEpi { kEpiBF16 = 0, kEpiF32 = 1, kEpiAddF32 = 2, kEpiSwiGLU = 3 };
+// kEpiSwiGLUSplit stores the SwiGLU product as split BF16 halves: hi in
+// columns [0, N), lo = bf16(y - hi) in [N, 2N) (ldo >= 2N).
+enum GemmEpi { kEpiBF16 = 0, kEpiF32 = 1, kEpiAddF32 = 2, kEpiSwiGLU = 3, kEpiSwiGLUSplit = 4 };
 // out[M, N] (ldo) = epilogue(X[M, K] * W[N, K]^T). For kEpiSwiGLU, W2 is the
-// up matrix and W the gate matrix (both [N, K]); out is BF16.
+// up matrix and W the gate matrix (both [N, K]); out is BF16. With x_split,
+// X is [M, 2K]: the split BF16 pair of each activation (hi in columns [0, K),
+// lo in [K, 2K)), and the result is (hi + lo) W^T.
 int launch_gemm(const uint16_t* X, const uint16_t* W, const uint16_t* W2, int64_t M, int N, int K,
-                int epi, void* out, int64_t ldo, cudaStream_t s);
+                int epi, void* out, int64_t ldo, cudaStream_t s, int x_split = 0);
 
 // ---- attention.cu -----------------------------------------------------------
 struct AttnArgs {
@@ -159,6 +177,8 @@ struct AttnTcArgs {
 int launch_attention_tc(const AttnTcArgs& a, const SeqPackVT& pk, cudaStream_t s);
 // vt[kvh * 256 + e][cu_vt[s] + j] = v[(cu[s] + j) * v_ts + kvh * v_hs + e].
 int launch_transpose_v(const uint16_t* v, int64_t v_ts, int64_t v_hs, const SeqPackVT& pk, int Hkv,
+                       uint16_t* vt, int64_t vt_pitch, cudaStream_t s);
+int launch_transpose_v(const float* v, int64_t v_ts, int64_t v_hs, const SeqPackVT& pk, int Hkv,
                        uint16_t* vt, int64_t vt_pitch, cudaStream_t s);
 int attention_tc_device_error(int* code);
 

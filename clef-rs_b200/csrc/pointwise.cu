@@ -6,6 +6,7 @@
 // Every kernel reads and writes with 16-byte vectors where the layout allows
 // and reduces with warp shuffles; one warp owns one normalisation row, so no
 // shared-memory reduction or block barrier sits on the hot path.
+#include <algorithm>
 #include <cmath>
 
 #include <type_traits>
@@ -30,6 +31,8 @@ __device__ __forceinline__ int64_t seq_of(const int64_t* cu, int nseq, int64_t t
 // One warp per row: sum of squares, inverse = 1 / sqrt(sum / width + eps),
 // out = (x * inverse) * w. With NV > 0 (width == 128 * NV) the row is read
 // once into registers, all NV 16-byte loads of a lane in flight together.
+// OUT_BF16: 0 = F32, 1 = BF16, 2 = split BF16 pair (hi in columns [0, width),
+// lo in [width, 2 width) of a row of 2 width).
 template <int OUT_BF16, int NV>
 __global__ void rms_kernel(const float* __restrict__ x, const float* __restrict__ w, int64_t rows,
                            int width, float eps, void* __restrict__ out) {
@@ -52,7 +55,12 @@ __global__ void rms_kernel(const float* __restrict__ x, const float* __restrict_
       const float4 b = *reinterpret_cast<const float4*>(w + i);
       const float r0 = __fmul_rn(__fmul_rn(a[j].x, inv), b.x), r1 = __fmul_rn(__fmul_rn(a[j].y, inv), b.y);
       const float r2 = __fmul_rn(__fmul_rn(a[j].z, inv), b.z), r3 = __fmul_rn(__fmul_rn(a[j].w, inv), b.w);
-      if (OUT_BF16) {
+      if (OUT_BF16 == 2) {
+        const uint2 hi = make_uint2(pack_bf16x2(r0, r1), pack_bf16x2(r2, r3));
+        uint16_t* o = reinterpret_cast<uint16_t*>(out) + row * 2 * width + i;
+        *reinterpret_cast<uint2*>(o) = hi;
+        *reinterpret_cast<uint2*>(o + width) = make_uint2(split_lo_bf16x2(r0, r1, hi.x), split_lo_bf16x2(r2, r3, hi.y));
+      } else if (OUT_BF16) {
         *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(out) + row * width + i) =
             make_uint2(pack_bf16x2(r0, r1), pack_bf16x2(r2, r3));
       } else {
@@ -83,7 +91,12 @@ __global__ void rms_kernel(const float* __restrict__ x, const float* __restrict_
       float4 b = *reinterpret_cast<const float4*>(w + i);
       float r0 = __fmul_rn(__fmul_rn(a.x, inv), b.x), r1 = __fmul_rn(__fmul_rn(a.y, inv), b.y);
       float r2 = __fmul_rn(__fmul_rn(a.z, inv), b.z), r3 = __fmul_rn(__fmul_rn(a.w, inv), b.w);
-      if (OUT_BF16) {
+      if (OUT_BF16 == 2) {
+        const uint2 hi = make_uint2(pack_bf16x2(r0, r1), pack_bf16x2(r2, r3));
+        uint16_t* o = reinterpret_cast<uint16_t*>(out) + row * 2 * width + i;
+        *reinterpret_cast<uint2*>(o) = hi;
+        *reinterpret_cast<uint2*>(o + width) = make_uint2(split_lo_bf16x2(r0, r1, hi.x), split_lo_bf16x2(r2, r3, hi.y));
+      } else if (OUT_BF16) {
         uint2 p = make_uint2(pack_bf16x2(r0, r1), pack_bf16x2(r2, r3));
         *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(out) + row * width + i) = p;
       } else {
@@ -94,8 +107,15 @@ __global__ void rms_kernel(const float* __restrict__ x, const float* __restrict_
   } else {
     for (int i = lane; i < width; i += 32) {
       float r = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
-      if (OUT_BF16) reinterpret_cast<uint16_t*>(out)[row * width + i] = f2bf(r);
-      else reinterpret_cast<float*>(out)[row * width + i] = r;
+      if (OUT_BF16 == 2) {
+        const uint16_t hi = f2bf(r);
+        reinterpret_cast<uint16_t*>(out)[row * 2 * width + i] = hi;
+        reinterpret_cast<uint16_t*>(out)[row * 2 * width + width + i] = f2bf(r - bf2f(hi));
+      } else if (OUT_BF16) {
+        reinterpret_cast<uint16_t*>(out)[row * width + i] = f2bf(r);
+      } else {
+        reinterpret_cast<float*>(out)[row * width + i] = r;
+      }
     }
   }
 }
@@ -294,48 +314,52 @@ __global__ void __launch_bounds__(256, 4) delta_prologue_kernel(
 }
 
 // ---- DeltaNet epilogue (qwen.rs:671-676) -------------------------------------
-// Rounding points follow the reference run in the BF16 projection dtype:
-// o -> P, norm output -> P, z in P, product -> P.
+// y = RMSNorm_128(o) * w (no offset) * silu(z) in F32; the only rounding is
+// the store of y, the out-projection's operand (BF16, or a split BF16 pair with
+// hi in columns [0, Hv*128) and lo in [Hv*128, 2*Hv*128) when SPLIT). z is the
+// in-projection output: BF16 in the engine's default precision, F32 in its
+// split precision.
+template <typename ZIn, bool SPLIT>
 __global__ void __launch_bounds__(256) delta_epilogue_kernel(const float* __restrict__ o,
-                                                             const uint16_t* __restrict__ z, int64_t ldz,
+                                                             const ZIn* __restrict__ z, int64_t ldz,
                                                              const float* __restrict__ w, float eps,
                                                              int64_t T, int Hv, uint16_t* __restrict__ y) {
   // One warp per token; its Hv rows of 128 go four at a time with all eight
   // loads of a batch (o rows and z rows) issued before any is used.
+  using ZV = std::conditional_t<std::is_same<ZIn, float>::value, float4, uint2>;
   const int lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= T) return;
   const float4 wv = *reinterpret_cast<const float4*>(w + lane * 4);
+  const int64_t V = (int64_t)Hv * 128;
   constexpr int HB = 4;  // heads per batch: 8 loads per lane in flight
   for (int h0 = 0; h0 < Hv; h0 += HB) {
-    float4 a[HB], zv[HB];
-    uint2 zr[HB];
+    float4 a[HB];
+    ZV zr[HB];
 #pragma unroll
     for (int u = 0; u < HB; ++u) {
       if (h0 + u < Hv) {
         a[u] = *reinterpret_cast<const float4*>(o + (t * Hv + h0 + u) * 128 + lane * 4);
-        zr[u] = *reinterpret_cast<const uint2*>(z + t * ldz + (h0 + u) * 128 + lane * 4);
+        zr[u] = *reinterpret_cast<const ZV*>(z + t * ldz + (h0 + u) * 128 + lane * 4);
       }
     }
 #pragma unroll
     for (int u = 0; u < HB; ++u) {
       if (h0 + u >= Hv) break;
-      zv[u] = ProIn<uint16_t>::f4(zr[u]);
-      const float4 b = make_float4(bf16_round(a[u].x), bf16_round(a[u].y), bf16_round(a[u].z),
-                                   bf16_round(a[u].w));
+      const float4 zv = ProIn<ZIn>::f4(zr[u]);
+      const float4 b = a[u];
       float ss = b.x * b.x + b.y * b.y + b.z * b.z + b.w * b.w;
       ss = warp_sum(ss);
       const float inv = 1.f / sqrtf(ss / 128.f + eps);
-      const float n0 = bf16_round(__fmul_rn(__fmul_rn(b.x, inv), wv.x));
-      const float n1 = bf16_round(__fmul_rn(__fmul_rn(b.y, inv), wv.y));
-      const float n2 = bf16_round(__fmul_rn(__fmul_rn(b.z, inv), wv.z));
-      const float n3 = bf16_round(__fmul_rn(__fmul_rn(b.w, inv), wv.w));
-      const float y0 = __fmul_rn(n0, silu_f(bf16_round(zv[u].x)));
-      const float y1 = __fmul_rn(n1, silu_f(bf16_round(zv[u].y)));
-      const float y2 = __fmul_rn(n2, silu_f(bf16_round(zv[u].z)));
-      const float y3 = __fmul_rn(n3, silu_f(bf16_round(zv[u].w)));
-      *reinterpret_cast<uint2*>(y + (t * Hv + h0 + u) * 128 + lane * 4) =
-          make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y2, y3));
+      const float y0 = __fmul_rn(__fmul_rn(__fmul_rn(b.x, inv), wv.x), silu_f(zv.x));
+      const float y1 = __fmul_rn(__fmul_rn(__fmul_rn(b.y, inv), wv.y), silu_f(zv.y));
+      const float y2 = __fmul_rn(__fmul_rn(__fmul_rn(b.z, inv), wv.z), silu_f(zv.z));
+      const float y3 = __fmul_rn(__fmul_rn(__fmul_rn(b.w, inv), wv.w), silu_f(zv.w));
+      const uint2 hi = make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y2, y3));
+      uint16_t* dst = y + t * (SPLIT ? 2 * V : V) + (h0 + u) * 128 + lane * 4;
+      *reinterpret_cast<uint2*>(dst) = hi;
+      if (SPLIT)
+        *reinterpret_cast<uint2*>(dst + V) = make_uint2(split_lo_bf16x2(y0, y1, hi.x), split_lo_bf16x2(y2, y3, hi.y));
     }
   }
 }
@@ -346,12 +370,29 @@ __global__ void __launch_bounds__(256) delta_epilogue_kernel(const float* __rest
 // all H + Hkv rows of 256 features, which go four at a time (8 features per
 // lane, loads issued up front). Rows [0, H) are query heads (projection
 // columns h*2d .. h*2d+d), rows [H, H+Hkv) key heads (columns 2*H*d + j*d).
-// The norm output is rounded to BF16 (the projection dtype) before the
-// rotation, and the rotated features again after it.
+// Norm and rotation run in F32; the rotated features are rounded once, to
+// the BF16 operands of the tensor-core attention. The projection rows are
+// BF16 (the engine's default precision) or F32 (its split precision).
 constexpr int AP_WARPS = 8;
 
+// Eight consecutive projection features of one lane as F32.
+__device__ __forceinline__ void load8(const uint16_t* src, float x[8]) {
+  const uint4 r = *reinterpret_cast<const uint4*>(src);
+  const uint32_t r32[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    x[2 * i] = __uint_as_float(r32[i] << 16);
+    x[2 * i + 1] = __uint_as_float(r32[i] & 0xffff0000u);
+  }
+}
+__device__ __forceinline__ void load8(const float* src, float x[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(src), b = *reinterpret_cast<const float4*>(src + 4);
+  x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
+}
+
+template <typename In>
 __global__ void __launch_bounds__(AP_WARPS * 32) attention_prologue_kernel(
-    const uint16_t* __restrict__ proj, int64_t ldp, const float* __restrict__ qw,
+    const In* __restrict__ proj, int64_t ldp, const float* __restrict__ qw,
     const float* __restrict__ kw, float eps, const int64_t* __restrict__ cu, int nseq, int64_t pos_offset,
     int H, int Hkv, int rot, const float* __restrict__ inv_freq, uint16_t* __restrict__ q_out,
     uint16_t* __restrict__ k_out, int64_t T) {
@@ -372,14 +413,14 @@ __global__ void __launch_bounds__(AP_WARPS * 32) attention_prologue_kernel(
   const int per = H + Hkv;
   const int lane_half = half / 8;  // lanes covering the first half
   for (int h0 = 0; h0 < per; h0 += 4) {
-    uint4 raw[4];
+    float xs[4][8];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int hh = h0 + u;
       if (hh < per) {
-        const uint16_t* src = hh < H ? proj + t * ldp + (int64_t)hh * 2 * d
-                                     : proj + t * ldp + (int64_t)2 * H * d + (int64_t)(hh - H) * d;
-        raw[u] = *reinterpret_cast<const uint4*>(src + lane * 8);
+        const In* src = hh < H ? proj + t * ldp + (int64_t)hh * 2 * d
+                               : proj + t * ldp + (int64_t)2 * H * d + (int64_t)(hh - H) * d;
+        load8(src + lane * 8, xs[u]);
       }
     }
 #pragma unroll
@@ -389,19 +430,15 @@ __global__ void __launch_bounds__(AP_WARPS * 32) attention_prologue_kernel(
       const bool isq = hh < H;
       const float* wn = isq ? qw : kw;
       float x[8];
-      const uint32_t r32[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        x[2 * i] = __uint_as_float(r32[i] << 16);
-        x[2 * i + 1] = __uint_as_float(r32[i] & 0xffff0000u);
-      }
+      for (int i = 0; i < 8; ++i) x[i] = xs[u][i];
       float ss = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
       ss = warp_sum(ss);
       const float inv = 1.f / sqrtf(ss / (float)d + eps);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) x[i] = bf16_round(__fmul_rn(__fmul_rn(x[i], inv), wn[lane * 8 + i]));
+      for (int i = 0; i < 8; ++i) x[i] = __fmul_rn(__fmul_rn(x[i], inv), wn[lane * 8 + i]);
       // Partial NeoX rotation on features [0, rot): pairs (i, i + rot/2).
       float partner[8];
 #pragma unroll
@@ -414,7 +451,7 @@ __global__ void __launch_bounds__(AP_WARPS * 32) attention_prologue_kernel(
           const float c = cs_tab[warp][0][fi], sn = cs_tab[warp][1][fi];
           // rotation * cos + rotate_half(rotation) * sin
           const float rotated = f < half ? -partner[i] : partner[i];
-          x[i] = bf16_round(__fadd_rn(__fmul_rn(x[i], c), __fmul_rn(rotated, sn)));
+          x[i] = __fadd_rn(__fmul_rn(x[i], c), __fmul_rn(rotated, sn));
         }
       }
       uint16_t* dst = isq ? q_out + (t * H + hh) * (int64_t)d : k_out + (t * Hkv + (hh - H)) * (int64_t)d;
@@ -519,17 +556,16 @@ int launch_rmsnorm(const float* x, const float* w, int64_t rows, int width, floa
   const dim3 grid((unsigned)ceil_div(rows, warps));
   // Register-resident rows for the backbone widths (hidden 2560 and 4096).
   const bool al = (((uintptr_t)x | (uintptr_t)w | (uintptr_t)out) & 15) == 0;
-  if (al && width == 2560) {
-    if (out_dtype == CLEF_BF16) rms_kernel<1, 20><<<grid, warps * 32, 0, s>>>(x, w, rows, width, eps, out);
-    else rms_kernel<0, 20><<<grid, warps * 32, 0, s>>>(x, w, rows, width, eps, out);
-  } else if (al && width == 4096) {
-    if (out_dtype == CLEF_BF16) rms_kernel<1, 32><<<grid, warps * 32, 0, s>>>(x, w, rows, width, eps, out);
-    else rms_kernel<0, 32><<<grid, warps * 32, 0, s>>>(x, w, rows, width, eps, out);
-  } else if (out_dtype == CLEF_BF16) {
-    rms_kernel<1, 0><<<grid, warps * 32, 0, s>>>(x, w, rows, width, eps, out);
-  } else {
-    rms_kernel<0, 0><<<grid, warps * 32, 0, s>>>(x, w, rows, width, eps, out);
-  }
+#define CLEF_RMS_LAUNCH(NV)                                                                  \
+  do {                                                                                       \
+    if (out_dtype == kOutBF16Split) rms_kernel<2, NV><<<grid, warps * 32, 0, s>>>(x, w, rows, width, eps, out); \
+    else if (out_dtype == CLEF_BF16) rms_kernel<1, NV><<<grid, warps * 32, 0, s>>>(x, w, rows, width, eps, out); \
+    else rms_kernel<0, NV><<<grid, warps * 32, 0, s>>>(x, w, rows, width, eps, out);       \
+  } while (0)
+  if (al && width == 2560) CLEF_RMS_LAUNCH(20);
+  else if (al && width == 4096) CLEF_RMS_LAUNCH(32);
+  else CLEF_RMS_LAUNCH(0);
+#undef CLEF_RMS_LAUNCH
   return launch_status("rmsnorm");
 }
 
@@ -588,8 +624,32 @@ int launch_delta_epilogue(const float* o, const uint16_t* z, int64_t ldz, const 
   (void)dv;
   const int64_t rows = T * Hv;
   if (rows == 0) return CLEF_OK;
-  delta_epilogue_kernel<<<(unsigned)ceil_div(T, 8), 256, 0, s>>>(o, z, ldz, w, eps, T, Hv, y);
+  delta_epilogue_kernel<uint16_t, false><<<(unsigned)ceil_div(T, 8), 256, 0, s>>>(o, z, ldz, w, eps, T, Hv, y);
   return launch_status("delta_epilogue");
+}
+
+int launch_delta_epilogue_split(const float* o, const float* z, int64_t ldz, const float* w, float eps,
+                                int64_t T, int Hv, uint16_t* y, cudaStream_t s) {
+  if (T * Hv == 0) return CLEF_OK;
+  CLEF_CHECK(ldz % 4 == 0 && ((uintptr_t)z & 15) == 0, CLEF_ERR_INVALID,
+             "delta_epilogue: F32 z rows must be 16-byte aligned");
+  delta_epilogue_kernel<float, true><<<(unsigned)ceil_div(T, 8), 256, 0, s>>>(o, z, ldz, w, eps, T, Hv, y);
+  return launch_status("delta_epilogue");
+}
+
+template <typename In>
+int launch_attention_prologue_t(const In* proj, int64_t ldp, const float* qw, const float* kw,
+                                float eps, const SeqPack& pack, int64_t pos_offset, int H, int Hkv,
+                                int rot, const float* inv_freq_dev, uint16_t* q_out, uint16_t* k_out,
+                                cudaStream_t s) {
+  const int64_t rows = pack.total * (H + Hkv);
+  if (rows == 0) return CLEF_OK;
+  CLEF_CHECK(rot % 16 == 0 && rot <= 256, CLEF_ERR_UNSUPPORTED,
+             "attention_prologue: rotary_dim must be a multiple of 16, at most 256");
+  attention_prologue_kernel<In><<<(unsigned)ceil_div(pack.total, AP_WARPS), AP_WARPS * 32, 0, s>>>(
+      proj, ldp, qw, kw, eps, pack.cu_seqlens, pack.nseq, pos_offset, H, Hkv, rot, inv_freq_dev,
+      q_out, k_out, pack.total);
+  return launch_status("attention_prologue");
 }
 
 int launch_attention_prologue(const uint16_t* proj, int64_t ldp, const float* qw, const float* kw,
@@ -597,14 +657,51 @@ int launch_attention_prologue(const uint16_t* proj, int64_t ldp, const float* qw
                               int d, int rot, const float* inv_freq_dev, uint16_t* q_out,
                               uint16_t* k_out, cudaStream_t s) {
   (void)d;
-  const int64_t rows = pack.total * (H + Hkv);
-  if (rows == 0) return CLEF_OK;
-  CLEF_CHECK(rot % 16 == 0 && rot <= 256, CLEF_ERR_UNSUPPORTED,
-             "attention_prologue: rotary_dim must be a multiple of 16, at most 256");
-  attention_prologue_kernel<<<(unsigned)ceil_div(pack.total, AP_WARPS), AP_WARPS * 32, 0, s>>>(
-      proj, ldp, qw, kw, eps, pack.cu_seqlens, pack.nseq, pos_offset, H, Hkv, rot, inv_freq_dev,
-      q_out, k_out, pack.total);
-  return launch_status("attention_prologue");
+  return launch_attention_prologue_t(proj, ldp, qw, kw, eps, pack, pos_offset, H, Hkv, rot, inv_freq_dev, q_out,
+                                     k_out, s);
+}
+
+int launch_attention_prologue(const float* proj, int64_t ldp, const float* qw, const float* kw,
+                              float eps, const SeqPack& pack, int64_t pos_offset, int H, int Hkv,
+                              int d, int rot, const float* inv_freq_dev, uint16_t* q_out,
+                              uint16_t* k_out, cudaStream_t s) {
+  (void)d;
+  return launch_attention_prologue_t(proj, ldp, qw, kw, eps, pack, pos_offset, H, Hkv, rot, inv_freq_dev, q_out,
+                                     k_out, s);
+}
+
+// ---- split precision: gated attention output ------------------------------
+// y = o * sigmoid(gate) in F32 (qwen.rs:519-524), stored as the split BF16
+// operand of o_proj: hi in columns [0, H*d), lo in [H*d, 2*H*d).
+__global__ void gate_split_kernel(const float* __restrict__ o, const float* __restrict__ gate, int64_t g_ts,
+                                  int64_t g_hs, int H, int d, int64_t T, uint16_t* __restrict__ y) {
+  const int64_t width = (int64_t)H * d;
+  const int64_t quads = T * width / 4;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < quads; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e0 = i * 4;
+    const int64_t t = e0 / width;
+    const int64_t c = e0 - t * width;
+    const int64_t h = c / d, e = c - h * d;
+    const float4 ov = *reinterpret_cast<const float4*>(o + e0);
+    const float4 gv = *reinterpret_cast<const float4*>(gate + t * g_ts + h * g_hs + e);
+    const float y0 = ov.x * sigmoid_f(gv.x), y1 = ov.y * sigmoid_f(gv.y);
+    const float y2 = ov.z * sigmoid_f(gv.z), y3 = ov.w * sigmoid_f(gv.w);
+    const uint2 hi = make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y2, y3));
+    uint16_t* dst = y + t * 2 * width + c;
+    *reinterpret_cast<uint2*>(dst) = hi;
+    *reinterpret_cast<uint2*>(dst + width) = make_uint2(split_lo_bf16x2(y0, y1, hi.x), split_lo_bf16x2(y2, y3, hi.y));
+  }
+}
+
+int launch_gate_split(const float* o, const float* gate, int64_t g_ts, int64_t g_hs, int H, int d, int64_t T,
+                      uint16_t* y, cudaStream_t s) {
+  if (T == 0) return CLEF_OK;
+  CLEF_CHECK(d % 4 == 0 && g_ts % 4 == 0 && g_hs % 4 == 0 && ((((uintptr_t)o) | (uintptr_t)gate) & 15) == 0,
+             CLEF_ERR_INVALID, "gate_split: F32 rows must be 16-byte aligned");
+  const int64_t quads = T * H * d / 4;
+  const unsigned blocks = (unsigned)std::min<int64_t>(ceil_div(quads, 256), 148 * 16);
+  gate_split_kernel<<<blocks, 256, 0, s>>>(o, gate, g_ts, g_hs, H, d, T, y);
+  return launch_status("gate_split");
 }
 
 int launch_embed(const uint16_t* table, const int32_t* ids, int64_t T, int hidden, float* h,

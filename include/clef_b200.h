@@ -180,6 +180,14 @@ typedef enum clef_epilogue {
 int clef_gemm_bf16(const uint16_t* X, const uint16_t* W, int64_t M, int32_t N, int32_t K,
                    int32_t epilogue, void* out, int64_t ldo, void* stream);
 
+/* Same product with the activation carried as a split BF16 pair: X2 BF16
+ * [M, 2K] holds hi = bf16(x) in columns [0, K) and lo = bf16(x - hi) in
+ * [K, 2K); the result is (hi + lo) W^T, i.e. x W^T to about 2^-17 of x, at
+ * twice the tensor-core work (no counterpart in the reference; the F32-class
+ * projection of the engine's CLEF_PRECISION_SPLIT). */
+int clef_gemm_bf16_split(const uint16_t* X2, const uint16_t* W, int64_t M, int32_t N, int32_t K,
+                         int32_t epilogue, void* out, int64_t ldo, void* stream);
+
 /* Fused SwiGLU projection: out BF16 [M, N] = silu(X Wg^T) * (X Wu^T), with
  * Wg, Wu BF16 [N, K]. Replaces the gated TileKernel path and
  * Projection::gated_forward (projection.rs:67-81; neural.metal:99-125). */
@@ -262,6 +270,20 @@ int clef_engine_prefill(clef_engine* e, const int32_t* ids, const int64_t* offse
 int clef_engine_prefill_device(clef_engine* e, const int32_t* ids_device, const int64_t* offsets,
                                int32_t nseq, const clef_prefix* initial, float* logits_device,
                                void* stream);
+
+/* Arithmetic of the projection GEMMs (no counterpart in the reference, whose
+ * device profiles pick one model dtype). CLEF_PRECISION_BF16 (the default):
+ * BF16 operands and BF16 in-projection / attention-projection outputs, the
+ * fastest path. CLEF_PRECISION_SPLIT: every activation operand of a GEMM is
+ * carried as two BF16 halves (hi = bf16(x), lo = bf16(x - hi)) against the
+ * same BF16 weights, and the projection outputs are F32, so the projections
+ * reproduce F32 arithmetic on the BF16 weights to about 2^-17 relative, at
+ * twice the tensor-core work; the attention's q, k, v and probabilities stay
+ * BF16. Used to qualify decisions against the reference's F32 CPU path.
+ * Takes effect from the next prefill; waits for the engine's pending work. */
+typedef enum clef_precision { CLEF_PRECISION_BF16 = 0, CLEF_PRECISION_SPLIT = 1 } clef_precision;
+int clef_engine_set_precision(clef_engine* e, int32_t precision);
+int32_t clef_engine_precision(const clef_engine* e);
 
 /* Number of kernels the engine has issued in prefill calls so far. */
 int64_t clef_engine_launches(const clef_engine* e);

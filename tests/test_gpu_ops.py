@@ -124,6 +124,29 @@ def test_gemm_residual_add():
     assert (h - (h0 + ref)).abs().max().item() <= 2e-5 * ref.abs().max().item() + 1e-6
 
 
+@pytest.mark.parametrize("M,N,K", [(100, 272, 2560), (2048, 2560, 9216), (8192, 10240, 2560)])
+def test_gemm_split_operands(M, N, K):
+    """clef_gemm_bf16_split: an F32 activation carried as hi + lo BF16 halves
+    against BF16 weights reproduces the F64 product of the unrounded
+    activation within 2e-5 of the output's max (F32 accumulation and the
+    2^-17 split residue), where the single-BF16 operand is off by ~1e-3."""
+    import clef_b200 as cb
+    rng = np.random.default_rng(M + N)
+    x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).cuda()
+    w = torch.from_numpy((0.02 * rng.standard_normal((N, K))).astype(np.float32)).cuda().bfloat16()
+    ref = (x.double() @ w.double().T)
+    scale = ref.abs().max().item()
+    y = cb.gemm_split(cb.split_bf16(x), w, epilogue=cb.EPI_F32)
+    err = (y.double() - ref).abs().max().item()
+    single = (cb.gemm(x.bfloat16(), w, epilogue=cb.EPI_F32).double() - ref).abs().max().item()
+    print(f"split M={M} N={N} K={K}: rel {err / scale:.2e} (single BF16 operand {single / scale:.2e})")
+    assert err <= 2e-5 * scale and err * 20 < single
+    h = torch.randn(M, N, device="cuda")
+    h0 = h.clone()
+    cb.gemm_split(cb.split_bf16(x), w, epilogue=cb.EPI_ADD_F32, out=h)
+    assert (h.double() - (h0.double() + ref)).abs().max().item() <= 2e-5 * scale + 1e-5
+
+
 @pytest.mark.parametrize("M", [64, 700])
 def test_gemm_swiglu(M):
     import clef_b200 as cb

@@ -33,7 +33,7 @@ STAGES = ["embed", "norm", "gemm", "delta_prologue", "delta_scan", "delta_epilog
 EXPORTS = [
     "clef_last_error", "clef_version", "clef_config_validate", "clef_rmsnorm", "clef_conv4",
     "clef_delta_prologue", "clef_delta_scan_workspace_size", "clef_delta_scan",
-    "clef_delta_scan_noalloc", "clef_gemm_bf16", "clef_gemm_bf16_split",
+    "clef_delta_scan_noalloc", "clef_delta_packed", "clef_delta_prepare_packed", "clef_gemm_bf16", "clef_gemm_bf16_split",
     "clef_gemm_swiglu", "clef_attention_gqa", "clef_attention_gqa_vt", "clef_compact_copy",
     "clef_engine_create",
     "clef_engine_set_weight", "clef_engine_init_random", "clef_engine_get_weight",
@@ -92,6 +92,8 @@ def _load():
                                            _i32, _vp, _i32, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
         "clef_delta_scan_noalloc": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32,
                                                    _vp, _i32, _vp, _i32, _i64, _vp, _vp, _vp, _vp]),
+        "clef_delta_packed": (ctypes.c_int, [_vp, _i64, _i32, _i32, _i32, _vp, _i64, _vp, _vp]),
+        "clef_delta_prepare_packed": (ctypes.c_int, [_vp, _i64, _vp, _vp, _i64, _i32, _i32, _vp, _vp]),
         "clef_gemm_bf16": (ctypes.c_int, [_vp, _vp, _i64, _i32, _i32, _i32, _vp, _i64, _vp]),
         "clef_gemm_bf16_split": (ctypes.c_int, [_vp, _vp, _i64, _i32, _i32, _i32, _vp, _i64, _vp]),
         "clef_gemm_swiglu": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i32, _i32, _vp, _vp]),
@@ -259,6 +261,34 @@ def delta_scan(q, k, v, g, beta, cu_seqlens=None, init_state=None, init_shared=F
                                _ptr(fin), _ptr(out), _ptr(workspace), workspace.numel(),
                                _stream(stream)))
     return out, cap, fin
+
+
+def delta_packed(packed, dk, dv, initial=None, capture=0, stream=None):
+    """DeltaKernel / CachedDelta on the reference's packed input: packed F32
+    [T, H, 2 dk + dv + 2] (q | k | v | e^g | beta). Returns (o [T, H, dv],
+    captured state [H, dk, dv] or None)."""
+    import torch
+    T, H, width = packed.shape
+    if width != 2 * dk + dv + 2:
+        raise ClefError(1, "delta_packed: packed width must be 2 dk + dv + 2")
+    n = T * H * dv + (H * dk * dv if capture else 0)
+    out = torch.empty(n, dtype=torch.float32, device=packed.device)
+    _check(lib.clef_delta_packed(_ptr(packed), T, H, dk, dv, _ptr(initial), int(capture), _ptr(out),
+                                 _stream(stream)))
+    o = out[:T * H * dv].view(T, H, dv)
+    state = out[T * H * dv:].view(H, dk, dv) if capture else None
+    return o, state
+
+
+def delta_prepare_packed(mixed, g, beta, Hk, Hv, stream=None):
+    """DeltaPrepareKernel: mixed F32 [T, >= (2 Hk + Hv) 128], g, beta F32
+    [T, Hv] -> packed [T, Hv, 386]."""
+    import torch
+    T = mixed.shape[0]
+    out = torch.empty((T, Hv, 386), dtype=torch.float32, device=mixed.device)
+    _check(lib.clef_delta_prepare_packed(_ptr(mixed), mixed.stride(0), _ptr(g), _ptr(beta), T, Hk, Hv, _ptr(out),
+                                         _stream(stream)))
+    return out
 
 
 def gemm(x, w, epilogue=EPI_BF16, out=None, stream=None):

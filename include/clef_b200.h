@@ -166,6 +166,32 @@ int clef_delta_scan_noalloc(const float* q, const float* k, const float* v, cons
                             const float* init_state, int32_t init_shared, int64_t capture,
                             float* capture_state, float* final_state, float* out, void* stream);
 
+/* DeltaKernel and CachedDelta in the reference's packed layout
+ * (crates/core/src/models/metal.rs:79-413, delta.metal:18-131): `packed` F32
+ * [T, H, 2 dk + dv + 2] holds per token and head q | k | v | decay | beta,
+ * with q and k already normalised (and q scaled) by the caller and decay =
+ * e^g. Output `out` F32: o [T, H, dv], followed by the state after token
+ * `capture` [H, dk, dv] when capture > 0 (CachedDelta's flat output, so `out`
+ * holds T H dv + H dk dv floats then). initial_state: F32 [H, dk, dv] to
+ * resume from, or NULL for zeros. Dimensions as the reference's `dimensions`
+ * check (metal.rs:280-290): 1 <= T <= 4096, 1 <= H <= 32, dk a power of two
+ * up to 128, 1 <= dv <= 128, 0 <= capture <= T; anything else is
+ * CLEF_ERR_INVALID before any launch. Per-token F32 recurrence; a capture
+ * followed by a resume reproduces the uninterrupted run bit for bit.
+ * Stream-ordered, no workspace. */
+int clef_delta_packed(const float* packed, int64_t T, int32_t H, int32_t dk, int32_t dv,
+                      const float* initial_state, int64_t capture, float* out, void* stream);
+
+/* DeltaPrepareKernel (crates/core/src/models/pointwise.rs:195-279,
+ * pointwise.metal:69-114): from the post-conv rows `mixed` F32 [T, ldm]
+ * (q | k | v = Hk*128 | Hk*128 | Hv*128 columns), the log-decay g and beta
+ * F32 [T, Hv], writes the packed input of clef_delta_packed with dk = dv = 128:
+ * out F32 [T, Hv, 386] = q / sqrt(|q|^2 + 1e-6) / sqrt(128) | k / sqrt(|k|^2 +
+ * 1e-6) | v | e^g | beta, q and k of value head h taken from key head
+ * h / (Hv / Hk). 1 <= T <= 4096 as in the reference. */
+int clef_delta_prepare_packed(const float* mixed, int64_t ldm, const float* g, const float* beta, int64_t T,
+                              int32_t Hk, int32_t Hv, float* out, void* stream);
+
 /* GEMM epilogues for clef_gemm_bf16. */
 typedef enum clef_epilogue {
   CLEF_EPI_STORE_BF16 = 0,  /* out BF16 [M, ldo] = X W^T                    */

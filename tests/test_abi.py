@@ -190,3 +190,16 @@ def test_prefix_transfer_rejects_before_touching_a_device():
     out = ctypes.c_void_p(0x1)
     assert lib.clef_prefix_create(None, 16, ctypes.byref(out)) == 1
     assert out.value is None  # cleared on every path
+
+
+def test_delta_packed_rejects_the_reference_dimension_limits():
+    """clef_delta_packed refuses what the reference's `dimensions` refuses
+    (metal.rs:280-290) before touching device memory."""
+    import clef_b200 as cb
+    fake = ctypes.c_void_p(0x10000)
+    L = cb.lib
+    for T, H, dk, dv, cap in [(0, 1, 4, 4, 0), (4097, 1, 4, 4, 0), (8, 33, 4, 4, 0), (8, 2, 3, 4, 0),
+                              (8, 2, 256, 4, 0), (8, 2, 4, 129, 0), (8, 2, 4, 0, 0), (8, 2, 4, 4, 9)]:
+        assert L.clef_delta_packed(fake, T, H, dk, dv, None, cap, fake, None) == 1, (T, H, dk, dv, cap)
+    assert "dimensions" in L.clef_last_error().decode() or "capture" in L.clef_last_error().decode()
+    assert L.clef_delta_prepare_packed(fake, 8192, fake, fake, 4097, 16, 32, fake, None) == 1

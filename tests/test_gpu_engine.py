@@ -175,6 +175,47 @@ def test_prefix_moves_through_a_device_copy(models, boundary):
     prefix.close()
 
 
+@pytest.mark.parametrize("boundary", [4160, 8192])
+def test_prefix_beyond_4096_tokens(models, boundary):
+    """Prefix state past the reference's 4096-token cap: capture after
+    `boundary` tokens (64-aligned), resume a 300-token suffix. The resumed
+    run equals the uninterrupted one bit for bit (the reference demands zero
+    drift, docs/clef-flash-prefix-reuse.md:66), also after the prefix went
+    through clef_prefix_export / clef_prefix_import; in the split precision
+    the resumed hidden rows match the oracle's own capture and resume
+    (Backbone::prefill, qwen.rs:337-364; models/mod.rs:116-171) within 2e-3
+    relative RMS and its logits within 2e-2."""
+    import clef_b200 as cb
+    cfg, eng, ref = models
+    seq = np.random.default_rng(boundary).integers(0, cfg.vocab_size, boundary + 300).astype(np.int32)
+    full_lg, full_h, _ = eng.prefill([seq], hidden=True)
+    _, _, prefix = eng.prefill([seq], capture=boundary)
+    lg, hid, _ = eng.prefill([seq[boundary:]], initial=prefix, hidden=True)
+    assert np.array_equal(hid, full_h) and np.array_equal(lg, full_lg)
+    buf = torch.empty(prefix.span_bytes(), dtype=torch.uint8, device="cuda")
+    prefix.export_to(buf)
+    twin = eng.create_prefix(boundary)
+    twin.import_from(buf)
+    lg2, hid2, _ = eng.prefill([seq[boundary:]], initial=twin, hidden=True)
+    assert np.array_equal(hid2, full_h) and np.array_equal(lg2, full_lg)
+    twin.close()
+    prefix.close()
+    eng.set_precision(cb.PRECISION_SPLIT)
+    try:
+        _, _, prefix = eng.prefill([seq], capture=boundary)
+        lg, hid, _ = eng.prefill([seq[boundary:]], initial=prefix, hidden=True)
+        prefix.close()
+    finally:
+        eng.set_precision(cb.PRECISION_BF16)
+    _, rstate = ref.prefill(seq, capture=boundary)
+    rh, _ = ref.prefill(seq[boundary:], initial=rstate)
+    head_w = eng.get_weight("clef.head.weight").reshape(7, cfg.hidden_size)
+    rel = np.sqrt(((hid[boundary:] - rh[boundary:]) ** 2).mean() / (rh[boundary:] ** 2).mean())
+    err_l = np.abs(lg[0] - oracle.head(rh[-1], head_w)).max()
+    print(f"prefix {boundary}: resumed suffix vs oracle rel-rms {rel:.3e} logits {err_l:.3e}")
+    assert rel <= 2e-3 and err_l <= 2e-2
+
+
 def test_prefix_import_checks_the_layout(models):
     """A created prefix cannot seed a prefill before it is filled, and an
     import of a copy made for another layout (here: the same span, but the

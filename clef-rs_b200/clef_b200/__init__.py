@@ -34,7 +34,7 @@ EXPORTS = [
     "clef_last_error", "clef_version", "clef_config_validate", "clef_rmsnorm", "clef_conv4",
     "clef_delta_prologue", "clef_delta_scan_workspace_size", "clef_delta_scan",
     "clef_delta_scan_noalloc", "clef_delta_packed", "clef_delta_prepare_packed", "clef_gemm_bf16", "clef_gemm_bf16_split",
-    "clef_gemm_swiglu", "clef_attention_gqa", "clef_attention_gqa_vt", "clef_compact_copy",
+    "clef_gemm_swiglu", "clef_attention_gqa_workspace_size", "clef_attention_gqa", "clef_attention_gqa_vt", "clef_compact_copy",
     "clef_engine_create",
     "clef_engine_set_weight", "clef_engine_init_random", "clef_engine_get_weight",
     "clef_engine_weight_count", "clef_engine_finalize", "clef_engine_prefill",
@@ -97,7 +97,9 @@ def _load():
         "clef_gemm_bf16": (ctypes.c_int, [_vp, _vp, _i64, _i32, _i32, _i32, _vp, _i64, _vp]),
         "clef_gemm_bf16_split": (ctypes.c_int, [_vp, _vp, _i64, _i32, _i32, _i32, _vp, _i64, _vp]),
         "clef_gemm_swiglu": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i32, _i32, _vp, _vp]),
-        "clef_attention_gqa": (ctypes.c_int, [_vp, _vp, _vp, _i32, _i32, _i64, _i64, _i32, _vp, _vp]),
+        "clef_attention_gqa_workspace_size": (_sz, [_i32, _i32, _i64, _i64]),
+        "clef_attention_gqa": (ctypes.c_int, [_vp, _vp, _vp, _i32, _i32, _i64, _i64, _i32, _vp, _vp, _sz,
+                                              _vp]),
         "clef_attention_gqa_vt": (ctypes.c_int, [_vp, _vp, _vp, _i32, _i32, _i64, _i64, _i32, _i64, _vp,
                                                  _vp]),
         "clef_compact_copy": (ctypes.c_int, [_vp, _i32, _vp, _vp, _i32, _vp, _vp]),
@@ -337,16 +339,20 @@ def gemm_swiglu(x, wg, wu, out=None, stream=None):
     return out
 
 
-def attention_gqa(q, k, v, out=None, stream=None):
-    """AttentionKernel / ops::attention: q BF16 [Hq, Tq, 256], k, v BF16
-    [Hkv, Tk, 256], causal lower-right; returns F32 [Hq, Tq, 256]."""
+def attention_gqa(q, k, v, out=None, workspace=None, stream=None):
+    """AttentionKernel / ops::attention on the tcgen05 tensor cores: q BF16
+    [Hq, Tq, 256], k, v BF16 [Hkv, Tk, 256], causal lower-right; returns F32
+    [Hq, Tq, 256]."""
     import torch
     Hq, Tq, d = q.shape
     Hkv, Tk = k.shape[0], k.shape[1]
     if out is None:
         out = torch.empty((Hq, Tq, d), dtype=torch.float32, device=q.device)
-    _check(lib.clef_attention_gqa(_ptr(q), _ptr(k), _ptr(v), Hq, Hkv, Tq, Tk, d, _ptr(out),
-                                  _stream(stream)))
+    if workspace is None:
+        size = int(lib.clef_attention_gqa_workspace_size(Hq, Hkv, Tq, Tk))
+        workspace = torch.empty(size, dtype=torch.uint8, device=q.device)
+    _check(lib.clef_attention_gqa(_ptr(q), _ptr(k), _ptr(v), Hq, Hkv, Tq, Tk, d, _ptr(out), _ptr(workspace),
+                                  workspace.numel(), _stream(stream)))
     return out
 
 

@@ -22,10 +22,20 @@
 //               gate o * sigmoid(gate) (qwen.rs:519-524).
 // V is consumed transposed (V^T rows = head dimension, keys contiguous) so both
 // products use K-major shared-memory operands with the 128-byte swizzle.
+// Entry points: the engine (token-major q/k, V^T per pack), clef_attention_gqa_vt
+// (the same layouts from a caller) and clef_attention_gqa (the reference's
+// head-major [H, T, 256] tensors of AttentionKernel, metal.rs:415-633, brought
+// to those layouts in a caller-provided workspace first).
 #include <cudaTypedefs.h>
 
 #include "kernels.cuh"
 #include "sm100.cuh"
+
+#define RC_(x)           \
+  do {                   \
+    int rc_ = (x);       \
+    if (rc_) return rc_; \
+  } while (0)
 
 namespace clef {
 
@@ -492,6 +502,18 @@ __global__ void transpose_v_kernel(const In* __restrict__ v, int64_t v_ts, int64
   }
 }
 
+// dst[(t * H + h) * 256 + e] = src[(h * T + t) * 256 + e]: head-major rows to
+// the token-major layout the kernel's Q/K tensor maps read (one warp per
+// 512-byte row, 16-byte accesses).
+__global__ void head_to_token_major_kernel(const uint16_t* __restrict__ src, int H, int64_t T,
+                                           uint16_t* __restrict__ dst) {
+  const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= (int64_t)H * T) return;
+  const int64_t h = r / T, t = r - h * T;
+  const int lane = threadIdx.x & 31;
+  reinterpret_cast<uint4*>(dst + (t * H + h) * D)[lane] = reinterpret_cast<const uint4*>(src + r * D)[lane];
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -605,6 +627,75 @@ int attention_tc_device_error(int* code) { return read_device_error(code); }
 using namespace clef;
 
 extern "C" {
+
+size_t clef_attention_gqa_workspace_size(int32_t Hq, int32_t Hkv, int64_t Tq, int64_t Tk) {
+  if (Hq <= 0 || Hkv <= 0 || Tq <= 0 || Tk < Tq) return 0;
+  auto a256 = [](size_t x) { return (x + 255) & ~(size_t)255; };
+  const int64_t pre = Tk - Tq;
+  return a256((size_t)Tq * Hq * 256 * 2) + a256((size_t)Tk * Hkv * 256 * 2) +
+         a256((size_t)Hkv * 256 * ((pre + 63) / 64 * 64) * 2) + a256((size_t)Hkv * 256 * ((Tq + 63) / 64 * 64) * 2);
+}
+
+int clef_attention_gqa(const uint16_t* q, const uint16_t* k, const uint16_t* v, int32_t Hq,
+                       int32_t Hkv, int64_t Tq, int64_t Tk, int32_t d, float* out, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  CLEF_CHECK(q && k && v && out, CLEF_ERR_INVALID, "attention_gqa: null pointer");
+  CLEF_CHECK(d == 256, CLEF_ERR_UNSUPPORTED, "attention_gqa: d must be 256");
+  CLEF_CHECK(Hq > 0 && Hkv > 0 && Hq % Hkv == 0, CLEF_ERR_INVALID, "attention_gqa: head counts");
+  CLEF_CHECK(Tq > 0 && Tk >= Tq, CLEF_ERR_INVALID, "attention_gqa: need 0 < Tq <= Tk");
+  CLEF_CHECK((((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 15) == 0,
+             CLEF_ERR_INVALID, "attention_gqa: pointers must be 16-byte aligned");
+  const size_t need = clef_attention_gqa_workspace_size(Hq, Hkv, Tq, Tk);
+  CLEF_CHECK(workspace && workspace_bytes >= need && ((uintptr_t)workspace & 255) == 0, CLEF_ERR_INVALID,
+             "attention_gqa: workspace must be 256-byte aligned and hold "
+             "clef_attention_gqa_workspace_size() bytes");
+  cudaStream_t s = as_stream(stream);
+  auto a256 = [](size_t x) { return (x + 255) & ~(size_t)255; };
+  const int64_t pre = Tk - Tq;
+  const int64_t pre_pitch = (pre + 63) / 64 * 64, own_pitch = (Tq + 63) / 64 * 64;
+  uint8_t* w = reinterpret_cast<uint8_t*>(workspace);
+  uint16_t* qt = reinterpret_cast<uint16_t*>(w);
+  w += a256((size_t)Tq * Hq * 256 * 2);
+  uint16_t* kt = reinterpret_cast<uint16_t*>(w);
+  w += a256((size_t)Tk * Hkv * 256 * 2);
+  uint16_t* pvt = reinterpret_cast<uint16_t*>(w);
+  w += a256((size_t)Hkv * 256 * pre_pitch * 2);
+  uint16_t* vt = reinterpret_cast<uint16_t*>(w);
+  // Token-major q and k, transposed values (prefix keys and own keys in
+  // separate V^T blocks so both start 64-key aligned).
+  head_to_token_major_kernel<<<(unsigned)ceil_div((int64_t)Hq * Tq, 8), 256, 0, s>>>(q, Hq, Tq, qt);
+  head_to_token_major_kernel<<<(unsigned)ceil_div((int64_t)Hkv * Tk, 8), 256, 0, s>>>(k, Hkv, Tk, kt);
+  RC_(launch_status("attention_gqa: layout"));
+  SeqPackVT one;
+  one.nseq = 1;
+  if (pre > 0) {
+    one.total = pre;
+    RC_(launch_transpose_v(v, 256, Tk * 256, one, Hkv, pvt, pre_pitch, s));
+  }
+  one.total = Tq;
+  RC_(launch_transpose_v(v + pre * 256, 256, Tk * 256, one, Hkv, vt, own_pitch, s));
+  AttnTcArgs a;
+  a.H = Hq;
+  a.Hkv = Hkv;
+  a.scale = 1.f / 16.f;
+  a.q = qt;
+  a.rows_q = Tq;
+  a.k = kt + pre * Hkv * 256;
+  a.rows_k = Tq;
+  a.vt = vt;
+  a.vt_cols = Tq;
+  a.vt_pitch = own_pitch;
+  if (pre > 0) {
+    a.prefix_len = pre;
+    a.pk = kt;
+    a.pvt = pvt;
+    a.pvt_pitch = pre_pitch;
+  }
+  a.out = out;  // head-major F32 [Hq, Tq, 256]
+  a.o_ts = 256;
+  a.o_hs = Tq * 256;
+  return launch_attention_tc(a, one, s);
+}
 
 int clef_attention_gqa_vt(const uint16_t* q, const uint16_t* k, const uint16_t* vt, int32_t Hq,
                           int32_t Hkv, int64_t Tq, int64_t Tk, int32_t d, int64_t vt_pitch,

@@ -121,28 +121,6 @@ enum GemmEpi { kEpiBF16 = 0, kEpiF32 = 1, kEpiAddF32 = 2, kEpiSwiGLU = 3, kEpiSw
 int launch_gemm(const uint16_t* X, const uint16_t* W, const uint16_t* W2, int64_t M, int N, int K,
                 int epi, void* out, int64_t ldo, cudaStream_t s, int x_split = 0);
 
-// ---- attention.cu -----------------------------------------------------------
-struct AttnArgs {
-  const uint16_t* q = nullptr;  // token-major: q[t*q_ts + h*q_hs + e]
-  int64_t q_ts = 0, q_hs = 0;
-  const uint16_t* k = nullptr;  // own keys:  k[t*k_ts + h*k_hs + e]
-  const uint16_t* v = nullptr;
-  int64_t k_ts = 0, k_hs = 0, v_ts = 0, v_hs = 0;
-  const uint16_t* pk = nullptr;  // shared prefix keys (prefix_len rows), same for all seqs
-  const uint16_t* pv = nullptr;
-  int64_t p_ts = 0, p_hs = 0;
-  int64_t prefix_len = 0;
-  int H = 0, Hkv = 0, d = 256;
-  float scale = 0.0625f;
-  // Output: F32 [t*o_ts + h*o_hs + e] when gate == nullptr, else BF16
-  // o * sigmoid(gate[t*g_ts + h*g_hs + e]).
-  void* out = nullptr;
-  int64_t o_ts = 0, o_hs = 0;
-  const uint16_t* gate = nullptr;
-  int64_t g_ts = 0, g_hs = 0;
-};
-int launch_attention(const AttnArgs& a, const SeqPack& pack, cudaStream_t s);
-
 // ---- attention_tc.cu --------------------------------------------------------
 // Packed sequences for the tcgen05 attention: token offsets, padded V^T column
 // offsets (each sequence starts at a multiple of 64 keys so every TMA

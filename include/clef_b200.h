@@ -221,14 +221,18 @@ int clef_gemm_swiglu(const uint16_t* X, const uint16_t* Wg, const uint16_t* Wu, 
                      int32_t N, int32_t K, uint16_t* out, void* stream);
 
 /* Causal grouped-query attention with the lower-right mask (query i of Tq
- * sees keys j <= i + Tk - Tq), scale 1/sqrt(d), online softmax in F32.
+ * sees keys j <= i + Tk - Tq), scale 1/sqrt(d), online softmax in F32 on the
+ * tcgen05 tensor cores (BF16 q, k, v and probabilities, F32 accumulation).
  * q BF16 [Hq, Tq, d], k, v BF16 [Hkv, Tk, d], out F32 [Hq, Tq, d].
- * Query head h reads kv head h / (Hq / Hkv). d = 256, Tq <= Tk.
+ * Query head h reads kv head h / (Hq / Hkv). d = 256, Tq <= Tk. The
+ * workspace (256-byte aligned, clef_attention_gqa_workspace_size bytes)
+ * holds the token-major q/k and transposed v the kernel reads.
  * Replaces AttentionKernel (metal.rs:415-633) and ops::attention
  * (ops.rs:62-143). */
+size_t clef_attention_gqa_workspace_size(int32_t Hq, int32_t Hkv, int64_t Tq, int64_t Tk);
 int clef_attention_gqa(const uint16_t* q, const uint16_t* k, const uint16_t* v, int32_t Hq,
                        int32_t Hkv, int64_t Tq, int64_t Tk, int32_t d, float* out,
-                       void* stream);
+                       void* workspace, size_t workspace_bytes, void* stream);
 
 /* The same attention on the tcgen05 tensor cores, in the engine's layouts:
  * q BF16 [Tq, Hq, 256] and k BF16 [Tk, Hkv, 256] token-major; V given

@@ -103,9 +103,13 @@ def test_gemm_rejects_before_launch():
 
 def test_attention_and_pointwise_reject_before_launch():
     L = cb.lib
-    assert L.clef_attention_gqa(FAKE, FAKE, FAKE, 16, 4, 10, 10, 128, FAKE, None) == 3
-    assert L.clef_attention_gqa(FAKE, FAKE, FAKE, 16, 5, 10, 10, 256, FAKE, None) == 1
-    assert L.clef_attention_gqa(FAKE, FAKE, FAKE, 16, 4, 11, 10, 256, FAKE, None) == 1
+    assert L.clef_attention_gqa(FAKE, FAKE, FAKE, 16, 4, 10, 10, 128, FAKE, FAKE, 1 << 30, None) == 3
+    assert L.clef_attention_gqa(FAKE, FAKE, FAKE, 16, 5, 10, 10, 256, FAKE, FAKE, 1 << 30, None) == 1
+    assert L.clef_attention_gqa(FAKE, FAKE, FAKE, 16, 4, 11, 10, 256, FAKE, FAKE, 1 << 30, None) == 1
+    # A workspace smaller than clef_attention_gqa_workspace_size is refused.
+    need = L.clef_attention_gqa_workspace_size(16, 4, 10, 10)
+    assert need > 0
+    assert L.clef_attention_gqa(FAKE, FAKE, FAKE, 16, 4, 10, 10, 256, FAKE, FAKE, need - 1, None) == 1
     assert L.clef_rmsnorm(FAKE, FAKE, 4, 256, 0.0, 0, FAKE, None) == 1
     assert L.clef_rmsnorm(FAKE, FAKE, 4, 256, 1e-6, 5, FAKE, None) == 1
     assert L.clef_conv4(FAKE, 8, None, 2, FAKE, 4, 8, FAKE, None) == 1  # history rows without data

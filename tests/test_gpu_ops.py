@@ -128,8 +128,9 @@ def test_gemm_residual_add():
 def test_gemm_split_operands(M, N, K):
     """clef_gemm_bf16_split: an F32 activation carried as hi + lo BF16 halves
     against BF16 weights reproduces the F64 product of the unrounded
-    activation within 2e-5 of the output's max (F32 accumulation and the
-    2^-17 split residue), where the single-BF16 operand is off by ~1e-3."""
+    activation within 2e-5 * sqrt(K / 2560) of the output's max (F32
+    accumulation over K terms and the 2^-17 split residue), where the
+    single-BF16 operand is off by ~1.6e-3."""
     import clef_b200 as cb
     rng = np.random.default_rng(M + N)
     x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).cuda()
@@ -140,11 +141,11 @@ def test_gemm_split_operands(M, N, K):
     err = (y.double() - ref).abs().max().item()
     single = (cb.gemm(x.bfloat16(), w, epilogue=cb.EPI_F32).double() - ref).abs().max().item()
     print(f"split M={M} N={N} K={K}: rel {err / scale:.2e} (single BF16 operand {single / scale:.2e})")
-    assert err <= 2e-5 * scale and err * 20 < single
+    assert err <= 2e-5 * np.sqrt(K / 2560) * scale and err * 20 < single
     h = torch.randn(M, N, device="cuda")
     h0 = h.clone()
     cb.gemm_split(cb.split_bf16(x), w, epilogue=cb.EPI_ADD_F32, out=h)
-    assert (h.double() - (h0.double() + ref)).abs().max().item() <= 2e-5 * scale + 1e-5
+    assert (h.double() - (h0.double() + ref)).abs().max().item() <= 2e-5 * np.sqrt(K / 2560) * scale + 1e-5
 
 
 @pytest.mark.parametrize("M", [64, 700])

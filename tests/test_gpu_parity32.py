@@ -21,8 +21,10 @@ Two checks per precision:
     operands) is held to the 2e-2 logits bound. The default BF16 precision
     rounds every GEMM operand and the projection outputs to BF16; those
     roundings alone move 32-layer logits by up to ~1e-1 from the F32 path on
-    this geometry (the oracle with the same rounding points against itself,
-    printed as the rounding floor), so its bound is 1.5e-1;
+    this geometry (the oracle with the same rounding points against the F32
+    oracle, printed as the rounding floor), so its bound is 2e-1, and on the
+    requests where the floor is measured the device may be at most twice as
+    far from the F32 path as the floor;
   * against the oracle run with the precision's own BF16 rounding points
     (oracle.set_rounding), on 8 requests. With few roundings (split) the two
     runs stay close, which isolates the kernels' arithmetic: <= 5e-3. With a
@@ -51,8 +53,8 @@ ROUNDING = {
     "split": oracle.ROUND_ATTN_QKV | oracle.ROUND_P,
 }
 PRECISION = {"bf16": 0, "split": 1}
-LOGITS_BOUND = {"bf16": 1.5e-1, "split": 2e-2}
-MATCHED_BOUND = {"bf16": 1.5e-1, "split": 5e-3}
+LOGITS_BOUND = {"bf16": 2e-1, "split": 2e-2}
+MATCHED_BOUND = {"bf16": 2e-1, "split": 5e-3}
 
 
 def softmax(x):
@@ -131,4 +133,5 @@ def test_32_layer_logits_and_decisions(model32, mode):
         print("  " + line)
     assert err_matched <= MATCHED_BOUND[mode]
     assert max_err <= LOGITS_BOUND[mode]
+    assert float(err[:MATCHED_REQUESTS].max()) <= max(2 * floor, 2e-2)
     assert matched == compared

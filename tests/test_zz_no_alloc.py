@@ -9,7 +9,9 @@ kernel, the workspace entry the two-kernel pipeline whose intra-chunk Gram
 products run on the tcgen05 tensor core; the outputs therefore agree to F32
 summation-order noise: max-abs 1e-5 on the outputs and 1e-4 on the final states
 (the scan's tolerance against the oracle is 1e-3). Checked on two calls in a row
-with different packings (the second call must not see the first call's offsets).
+with different packings (the second call must not see the first call's offsets),
+and directly against the oracle's per-token recurrence on config 1, with
+initial states (per sequence and shared) and with a capture.
 
 This file is collected last on purpose; it needs nothing from the others and
 also passes alone in a fresh process.
@@ -71,6 +73,59 @@ def test_noalloc_scan_matches_workspace_scan_on_two_calls_in_a_row():
     second = workloads.delta_operator_inputs(T=1000, seed=22)
     (o_ws, f_ws), (o_na, f_na) = scan_both(second, [0, 300, 301, 450, 640, 999, 1000])
     assert close(o_na, o_ws, 1e-5) and close(f_na, f_ws, 1e-4)
+
+
+def _noalloc(inp, cu, init=None, init_shared=0, capture=0):
+    import clef_b200 as cb
+    qs, ks = workloads.scan_operands(inp)
+    t = {k: torch.from_numpy(np.ascontiguousarray(v)).cuda()
+         for k, v in dict(q=qs, k=ks, v=inp["v"], g=inp["g"], b=inp["beta"]).items()}
+    T, Hk, _ = qs.shape
+    Hv = inp["v"].shape[1]
+    nseq = len(cu) - 1
+    cu = np.ascontiguousarray(cu, np.int64)
+    out = torch.empty((T, Hv, 128), dtype=torch.float32, device="cuda")
+    fin = torch.empty((nseq, Hv, 128, 128), dtype=torch.float32, device="cuda")
+    cap = torch.empty((Hv, 128, 128), dtype=torch.float32, device="cuda") if capture else None
+    init_t = None if init is None else torch.from_numpy(np.ascontiguousarray(init, np.float32)).cuda()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rc = cb.lib.clef_delta_scan_noalloc(_p(t["q"]), _p(t["k"]), _p(t["v"]), _p(t["g"]), _p(t["b"]), T, Hk, Hv,
+                                        128, 128, cu.ctypes.data, nseq, _p(init_t), init_shared, capture,
+                                        _p(cap), _p(fin), _p(out), stream)
+    assert rc == 0, cb.lib.clef_last_error().decode()
+    torch.cuda.synchronize()
+    return out.cpu().numpy(), fin.cpu().numpy(), None if cap is None else cap.cpu().numpy()
+
+
+def test_noalloc_scan_matches_the_oracle_recurrence():
+    """Config 1 (T = 1024, 16 / 32 heads, seed 0) through the allocation-free
+    entry against the oracle's per-token recurrence at the scan's 1e-3 bound."""
+    import oracle
+    inp = workloads.delta_operator_inputs(T=1024, seed=0)
+    o, fin, _ = _noalloc(inp, [0, 1024])
+    want, state, _ = oracle.delta_recurrence(inp["q"], inp["k"], inp["v"], inp["g"], inp["beta"])
+    assert close(o, want, 1e-3) and close(fin[0], state, 1e-3)
+
+
+def test_noalloc_scan_initial_states_and_capture_match_the_oracle():
+    """Per-sequence initial states, one state shared by every sequence, and a
+    capture inside a chunk: each against the oracle's recurrence (1e-3)."""
+    import oracle
+    inp = workloads.delta_operator_inputs(T=400, seed=24)
+    cu = [0, 150, 400]
+    rng = np.random.default_rng(5)
+    init = (0.05 * rng.standard_normal((2, 32, 128, 128))).astype(np.float32)
+    for shared in (0, 1):
+        o, fin, _ = _noalloc(inp, cu, init=init[:1] if shared else init, init_shared=shared)
+        for s in range(2):
+            a, b = cu[s], cu[s + 1]
+            start = init[0] if shared else init[s]
+            want, state, _ = oracle.delta_recurrence(inp["q"][a:b], inp["k"][a:b], inp["v"][a:b], inp["g"][a:b],
+                                                     inp["beta"][a:b], state=start)
+            assert close(o[a:b], want, 1e-3) and close(fin[s], state, 1e-3), (shared, s)
+    o, _, cap = _noalloc(inp, [0, 400], capture=100)
+    want, _, wcap = oracle.delta_recurrence(inp["q"], inp["k"], inp["v"], inp["g"], inp["beta"], capture=100)
+    assert close(o, want, 1e-3) and close(cap, wcap, 1e-3)
 
 
 def test_noalloc_scan_single_sequence_and_size_limit():

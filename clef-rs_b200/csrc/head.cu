@@ -30,6 +30,9 @@ struct clef_head {
   std::map<std::string, std::vector<float>> host;     // loaded, not yet uploaded
   std::map<std::string, int64_t> off;                 // name -> float offset in blob
   float* blob = nullptr;
+  // memory_projection as a three-term BF16 operand [W_hi | W_hi | W_lo]
+  // [width, 3 hidden] for the tensor-core path (null when the shapes do not fit it).
+  uint16_t* mem_w3 = nullptr;
   bool finalized = false;
   float prior_scale = 0.f, joint_scale = 0.f, gate = 0.f;
   // workspace
@@ -41,6 +44,33 @@ struct clef_head {
 
 namespace clef {
 namespace {
+
+// ---- F32-accurate products on the BF16 tensor cores -------------------------
+// x = hi + lo with hi = bf16(x), lo = bf16(x - hi). A product of two such
+// pairs keeps hi.hi + lo.hi + hi.lo (the dropped lo.lo term is below 2^-16 of
+// it); laid out as X3 = [x_hi | x_lo | x_hi] and W3 = [w_hi | w_hi | w_lo]
+// along K it is one BF16 GEMM with K' = 3K and F32 accumulation.
+__global__ void split3_rows_kernel(const float* __restrict__ x, int64_t ldx, int64_t rows, int k, int w_side,
+                                   uint16_t* __restrict__ out) {
+  const int64_t n = rows * k;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / k;
+    const int c = (int)(i - r * k);
+    const float v = x[r * ldx + c];
+    const uint16_t hi = f2bf(v), lo = f2bf(v - bf2f(hi));
+    uint16_t* o = out + r * 3 * (int64_t)k;
+    o[c] = hi;
+    o[k + c] = w_side ? hi : lo;
+    o[2 * k + c] = w_side ? lo : hi;
+  }
+}
+
+int split3(const float* x, int64_t ldx, int64_t rows, int k, bool w_side, uint16_t* out, cudaStream_t s) {
+  const int64_t n = rows * k;
+  const unsigned blocks = (unsigned)std::min<int64_t>(ceil_div(n, 256), 148 * 32);
+  split3_rows_kernel<<<blocks, 256, 0, s>>>(x, ldx, rows, k, w_side ? 1 : 0, out);
+  return launch_status("head split3");
+}
 
 // ---- F32 GEMM on the CUDA cores --------------------------------------------
 // out[m, n] = res[m, n] + act(sum_k X[m, k] W[n, k] + bias[n]) with W stored
@@ -819,11 +849,12 @@ const float* W(const clef_head* hd, const std::string& name) { return hd->blob +
 
 // Workspace layout for one record; every slot is a multiple of 64 floats.
 struct HeadWs {
-  float *normalized, *memory, *nm, *U, *S, *C, *qs, *ctx, *lex, *routed, *tq, *q, *att, *ffh, *base, *oq, *summ,
+  float *normalized, *x3, *memory, *nm, *U, *S, *C, *qs, *ctx, *lex, *routed, *tq, *q, *att, *ffh, *base, *oq, *summ,
       *summn, *fields, *gproj, *qkv, *anchor, *opts, *feats, *r1, *resid, *prior, *cosine, *logits, *part;
 };
 
 constexpr int64_t kSplitCap = 4 << 20;  // floats of split-K partial sums (16 MB)
+constexpr int64_t kTensorRows = 64;     // records at least this long take the tensor-core memory projection
 
 size_t plan_ws(const clef_head_config& c, int64_t T, int nq, int no, float* base, HeadWs* w) {
   size_t off = 0;
@@ -837,6 +868,7 @@ size_t plan_ws(const clef_head_config& c, int64_t T, int nq, int no, float* base
   HeadWs d;
   HeadWs* t = w ? w : &d;
   take(&t->normalized, T * h);
+  take(&t->x3, (T * 3 * h + 1) / 2);  // BF16 three-term operand of the memory projection
   take(&t->memory, T * wd);
   take(&t->nm, T * wd);
   take(&t->U, R * wd);
@@ -934,6 +966,15 @@ int clef_head_finalize(clef_head* hd) {
   hd->joint_scale = (float)std::exp(std::min((double)hd->host["joint_logit_scale"][0], lim));
   hd->gate = (float)(1.0 / (1.0 + std::exp(-(double)hd->host["residual_gate"][0])));
   hd->host.clear();
+  // The memory projection (the head's one large product, T x hidden x width)
+  // runs on the tcgen05 GEMM when its shapes fit the kernel's tiling.
+  if (c.hidden_size % 64 == 0 && c.width % 16 == 0) {
+    const int64_t h = c.hidden_size;
+    CLEF_CUDA(cudaMalloc(&hd->mem_w3, sizeof(uint16_t) * (size_t)w * 3 * h));
+    const int rc = split3(W(hd, "memory_projection.weight"), h, w, (int)h, true, hd->mem_w3, hd->stream);
+    if (rc) return rc;
+    CLEF_CUDA(cudaStreamSynchronize(hd->stream));
+  }
   hd->finalized = true;
   return CLEF_OK;
 }
@@ -1025,8 +1066,15 @@ int clef_head_forward(clef_head* hd, const float* hidden, int64_t T, const float
   g_split.sms = num_sms(hd->device);
   // Memory side (head.rs:154-157).
   RCH(layer_norm(hidden, h, Ti, (int)h, W(hd, "hidden_norm.weight"), W(hd, "hidden_norm.bias"), b.normalized, h, s));
-  RCH(gemm_f32(b.normalized, h, W(hd, "memory_projection.weight"), h, Ti, (int)wd, (int)h, nullptr, false, nullptr, 0,
-               b.memory, wd, s));
+  if (hd->mem_w3 && T >= kTensorRows) {
+    // F32-accurate three-term product on the tensor cores (hi.hi + lo.hi + hi.lo).
+    RCH(split3(b.normalized, h, T, (int)h, false, reinterpret_cast<uint16_t*>(b.x3), s));
+    RCH(launch_gemm(reinterpret_cast<const uint16_t*>(b.x3), hd->mem_w3, nullptr, T, (int)wd, (int)(3 * h), kEpiF32,
+                    b.memory, wd, s));
+  } else {
+    RCH(gemm_f32(b.normalized, h, W(hd, "memory_projection.weight"), h, Ti, (int)wd, (int)h, nullptr, false, nullptr,
+                 0, b.memory, wd, s));
+  }
   const float* glob = b.normalized + (T - 1) * h;
   // Questions, option contexts and lexical means (head.rs:158-186).
   span_mean_kernel<<<nq, 256, 0, s>>>(b.normalized, h, (int)h, d_ispan, nullptr, b.qs, h);
@@ -1132,6 +1180,7 @@ int clef_head_destroy(clef_head* hd) {
   {
     DeviceGuardH g(hd->device);
     if (hd->blob) cudaFree(hd->blob);
+    if (hd->mem_w3) cudaFree(hd->mem_w3);
     if (hd->ws) cudaFree(hd->ws);
     if (hd->meta_d) cudaFree(hd->meta_d);
     if (hd->stream) cudaStreamDestroy(hd->stream);

@@ -211,29 +211,18 @@ __device__ __forceinline__ void cp_async_wait() {
 // the correctly rounded quotient; e^-x overflowing gives -0 for very negative x).
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 
-template <typename V>
-__device__ __forceinline__ void pro_step(const V* __restrict__ rows, int I, const float* __restrict__ hist,
-                                         int hist_rows, int width, const float (&tw)[4][4], int64_t t,
-                                         int64_t start, int c, int key, int Hv, float qscale,
-                                         float* __restrict__ q, float* __restrict__ k,
-                                         float* __restrict__ v) {
-  // rows[(I + i) * 256] is token t - 3 + i of this thread's channels (i = 0..3).
+// Conv output of one token from its four input rows (oldest first), then
+// SiLU, L2 normalisation of q/k heads and the store.
+__device__ __forceinline__ void pro_finish(const float4 (&x)[4], const float (&tw)[4][4], int64_t t, int c, int key,
+                                           int Hv, float qscale, float* __restrict__ q, float* __restrict__ k,
+                                           float* __restrict__ v) {
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
   for (int tap = 0; tap < 4; ++tap) {
-    const int64_t r = t - (3 - tap);
-    float4 xv;
-    if (r >= start) {
-      xv = ProIn<std::conditional_t<sizeof(V) == 16, float, uint16_t>>::f4(rows[(I + tap) * 256]);
-    } else {
-      const int64_t hr = hist_rows + (r - start);
-      if (!hist || hr < 0) continue;  // rows before the sequence are zero
-      xv = *reinterpret_cast<const float4*>(hist + hr * width + c);
-    }
-    acc.x = __fadd_rn(acc.x, __fmul_rn(xv.x, tw[tap][0]));
-    acc.y = __fadd_rn(acc.y, __fmul_rn(xv.y, tw[tap][1]));
-    acc.z = __fadd_rn(acc.z, __fmul_rn(xv.z, tw[tap][2]));
-    acc.w = __fadd_rn(acc.w, __fmul_rn(xv.w, tw[tap][3]));
+    acc.x = __fadd_rn(acc.x, __fmul_rn(x[tap].x, tw[tap][0]));
+    acc.y = __fadd_rn(acc.y, __fmul_rn(x[tap].y, tw[tap][1]));
+    acc.z = __fadd_rn(acc.z, __fmul_rn(x[tap].z, tw[tap][2]));
+    acc.w = __fadd_rn(acc.w, __fmul_rn(x[tap].w, tw[tap][3]));
   }
   const float4 m = make_float4(silu_fast(acc.x), silu_fast(acc.y), silu_fast(acc.z), silu_fast(acc.w));
   if (c < 2 * key) {
@@ -251,6 +240,17 @@ __device__ __forceinline__ void pro_step(const V* __restrict__ rows, int I, cons
   } else {
     *reinterpret_cast<float4*>(v + t * (int64_t)(Hv * 128) + (c - 2 * key)) = m;
   }
+}
+
+// Input row of token t (this thread's 4 channels) for a sequence starting at
+// `start`: the staged projection row, a conv-history row, or zeros.
+template <typename V>
+__device__ __forceinline__ float4 pro_row(const V* __restrict__ rows, int i, const float* __restrict__ hist,
+                                          int hist_rows, int width, int64_t r, int64_t start, int c) {
+  if (r >= start) return ProIn<std::conditional_t<sizeof(V) == 16, float, uint16_t>>::f4(rows[i * 256]);
+  const int64_t hr = hist_rows + (r - start);
+  if (!hist || hr < 0) return make_float4(0.f, 0.f, 0.f, 0.f);  // rows before the sequence are zero
+  return *reinterpret_cast<const float4*>(hist + hr * width + c);
 }
 
 template <typename In>
@@ -290,6 +290,11 @@ __global__ void __launch_bounds__(256, 4) delta_prologue_kernel(
                           {w0.z, w1.z, w2.z, w3.z},
                           {w0.w, w1.w, w2.w, w3.w}};
   cp_async_wait<0>();
+  // Sliding window of the four input rows (converted once each): staged row
+  // i + j is token t_begin - 3 + i + j.
+  float4 win[4];
+#pragma unroll
+  for (int j = 0; j < 3; ++j) win[j] = pro_row<V>(rows, j, hist, hist_rows, width, t_begin - 3 + j, start, c);
 #pragma unroll 1
   for (int i = 0; i < PRO_RUN; ++i) {
     const int64_t t = t_begin + i;
@@ -298,8 +303,14 @@ __global__ void __launch_bounds__(256, 4) delta_prologue_kernel(
       ++s;
       start = t;
       next_start = cu[s + 1];
+#pragma unroll
+      for (int j = 0; j < 3; ++j) win[j] = pro_row<V>(rows, i + j, hist, hist_rows, width, t - 3 + j, start, c);
     }
-    pro_step<V>(rows, i, hist, hist_rows, width, tw, t, start, c, key, Hv, qscale, q, k, v);
+    win[3] = pro_row<V>(rows, i + 3, hist, hist_rows, width, t, start, c);
+    pro_finish(win, tw, t, c, key, Hv, qscale, q, k, v);
+    win[0] = win[1];
+    win[1] = win[2];
+    win[2] = win[3];
   }
   if (blockIdx.x == 0) {
     for (int idx = threadIdx.x; idx < (t_end - t_begin) * Hv; idx += blockDim.x) {

@@ -14,8 +14,8 @@
 //               issued while the softmax of block j runs;
 //   warps 2..9  one query row per thread, two warps per row quarter (each
 //               exponentiates half of every 64-key block): tcgen05.ld of the S row, mask,
-//               online softmax in the log2 domain, P row (BF16) into a
-//               swizzled shared tile for the PV product. The running maximum is
+//               online softmax in the log2 domain, P row (BF16) stored back into
+//               TMEM by tcgen05.st, where the PV product reads it as its A operand. The running maximum is
 //               only raised (and O rescaled in TMEM) when a row's maximum grows
 //               by more than 8 in log2 units, so O is rarely touched; the
 //               epilogue normalises O by the row sum and applies the output
@@ -49,20 +49,19 @@ constexpr int BK = 64;
 constexpr int Q_BYTES = BQ * D * 2;        // 64 KB: 4 atoms of [128 rows x 128 B]
 constexpr int K_BYTES = BK * D * 2;        // 32 KB: 4 atoms of [64 rows x 128 B]
 constexpr int VT_BYTES = D * BK * 2;       // 32 KB: [256 rows x 128 B]
-constexpr int P_BYTES = BQ * BK * 2;       // 16 KB: [128 rows x 128 B]
 constexpr int TILE_BYTES = 32 * 1024;      // one ring slot: a K tile or a V^T tile
 static_assert(K_BYTES == TILE_BYTES && VT_BYTES == TILE_BYTES, "ring slots hold K or V^T tiles");
 constexpr int NSLOT = 4;
 constexpr int OFF_Q = 0;
 constexpr int OFF_RING = OFF_Q + Q_BYTES;               // NSLOT slots
-constexpr int OFF_P = OFF_RING + NSLOT * TILE_BYTES;    // 2 buffers
-constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
+constexpr int OFF_BAR = OFF_RING + NSLOT * TILE_BYTES;
 constexpr int OFF_LSUM = OFF_BAR + 256;                // [2][128] F32 partial row sums
 constexpr int SMEM = 1024 + OFF_LSUM + 2 * BQ * 4;
 constexpr int SOFTMAX_WARPS = 8;                        // two per TMEM lane quarter
 constexpr int THREADS = 64 + SOFTMAX_WARPS * 32;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t COL_O = 0, COL_S = 256;             // S buffers at 256 and 320
+constexpr uint32_t COL_P = 384;                        // P buffers (BF16 pairs) at 384 and 416
 constexpr float RESCALE_THRESHOLD = 8.f;               // log2 units
 
 struct TcParams {
@@ -270,11 +269,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           ok = false;
           break;
         }
-        const uint32_t pa = sbase + OFF_P + st * P_BYTES, vb = sbase + OFF_RING + slot * TILE_BYTES;
+        const uint32_t vb = sbase + OFF_RING + slot * TILE_BYTES;
+        // P_j from TMEM (16 keys = 8 columns per instruction) times V_j.
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk)
-          umma_f16(tmem + COL_O, desc_k_sw128(pa + kk * 32), desc_k_sw128(vb + kk * 32), idesc_o,
-                   (j | kk) != 0);
+          umma_f16_ts(tmem + COL_O, tmem + COL_P + st * (BK / 2) + kk * 8, desc_k_sw128(vb + kk * 32), idesc_o,
+                      (j | kk) != 0);
         umma_commit(&empty[slot]);
         umma_commit(&pv_done[st]);
         if (j + 2 < nblk) ok = issue_s(j + 2);
@@ -367,26 +367,23 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!ok) break;
       }
       // p = 2^(s * scale * log2 e - m), rounded to BF16 as the PV product
-      // consumes it; the row sum adds the rounded values.
-      uint8_t* prow = sm + OFF_P + st * P_BYTES + r * 128;
+      // consumes it; the row sum adds the rounded values. This warp's 32 keys
+      // go into TMEM columns [COL_P + 32 st + 16 hf, +16) of its lanes, two
+      // per column in key order.
       const float neg_m = -m_run;
       float ps[2] = {0.f, 0.f};
+      uint32_t w[16];
 #pragma unroll
-      for (int cq = 0; cq < 4; ++cq) {
-        const int ch = hf * 4 + cq;  // this warp's 16-byte chunks of the 128-byte P row
-        uint32_t w[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[cq * 8 + 2 * e]), p.sl2, neg_m));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[cq * 8 + 2 * e + 1]), p.sl2, neg_m));
-          w[e] = pack_bf16x2(p0, p1);
-          ps[0] += __uint_as_float(w[e] << 16);
-          ps[1] += __uint_as_float(w[e] & 0xffff0000u);
-        }
-        *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      for (int e = 0; e < 16; ++e) {
+        const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * e]), p.sl2, neg_m));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * e + 1]), p.sl2, neg_m));
+        w[e] = pack_bf16x2(p0, p1);
+        ps[0] += __uint_as_float(w[e] << 16);
+        ps[1] += __uint_as_float(w[e] & 0xffff0000u);
       }
+      tmem_st_32x32b_x16(tmem + lane_off + COL_P + st * (BK / 2) + hf * 16, w);
+      tmem_st_wait();
       l_run += ps[0] + ps[1];
-      fence_async_shared();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[st]);

@@ -207,3 +207,10 @@ def test_delta_packed_rejects_the_reference_dimension_limits():
         assert L.clef_delta_packed(fake, T, H, dk, dv, None, cap, fake, None) == 1, (T, H, dk, dv, cap)
     assert "dimensions" in L.clef_last_error().decode() or "capture" in L.clef_last_error().decode()
     assert L.clef_delta_prepare_packed(fake, 8192, fake, fake, 4097, 16, 32, fake, None) == 1
+
+
+def test_precision_setter_validates_before_touching_an_engine():
+    import clef_b200 as cb
+    assert cb.lib.clef_engine_set_precision(None, 1) == 1
+    assert cb.lib.clef_engine_precision(None) == -1
+    assert cb.PRECISION_BF16 == 0 and cb.PRECISION_SPLIT == 1

@@ -65,8 +65,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-tokens", type=int, default=256)
     ap.add_argument("--profile-op", default=None,
-                    choices=["gemm", "gemm_swiglu", "scan", "scan1", "attention", "attention_tc",
-                             "prologue", "head"],
+                    choices=["gemm", "gemm_swiglu", "gemm_split", "scan", "scan1", "packed", "attention",
+                             "attention_tc", "prologue", "head"],
                     help="run one operator on a profiling-sized case and exit (for ncu)")
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--scan-seqs", type=int, default=64,
@@ -362,7 +362,22 @@ def profile_op(args):
             torch.cuda.synchronize()
             print(f"{label}: {e0.elapsed_time(e1):.3f} ms", flush=True)
 
-    if args.profile_op in ("gemm", "gemm_swiglu"):
+    if args.profile_op == "gemm_split":
+        # Split-BF16 activation operand (hi | lo) against BF16 weights.
+        M, K, N = 8192, 2560, 9216
+        x2 = cb.split_bf16(torch.randn(M, K, device=dev))
+        w = (0.02 * torch.randn(N, K, device=dev)).bfloat16()
+        out = torch.empty(M, N, device=dev)
+        timed(f"gemm_split {M}x{N}x{K} (tensor work 2x)", lambda: cb.gemm_split(x2, w, epilogue=cb.EPI_F32, out=out))
+    elif args.profile_op == "packed":
+        # DeltaKernel's largest accepted case: T = 4096, H = 32, dk = dv = 128.
+        T, H, dk, dv = 4096, 32, 128, 128
+        qk = torch.nn.functional.normalize(torch.randn(T, H, 2, dk, device=dev), dim=-1)
+        packed = torch.cat([qk[:, :, 0] / dk ** 0.5, qk[:, :, 1], torch.randn(T, H, dv, device=dev),
+                            torch.rand(T, H, 1, device=dev), torch.sigmoid(torch.randn(T, H, 1, device=dev))],
+                           -1).contiguous()
+        timed(f"delta_packed T={T} H={H}", lambda: cb.delta_packed(packed, dk, dv))
+    elif args.profile_op in ("gemm", "gemm_swiglu"):
         M, K, N = 8192, 2560, 9216
         x = torch.randn(M, K, device=dev).bfloat16()
         w = (0.02 * torch.randn(N, K, device=dev)).bfloat16()

@@ -16,10 +16,11 @@
 // The recurrence kernel is the reference's per-token update in F32
 // (delta_recurrence_prefill, qwen.rs:867-880; clef_delta, delta.metal:18-131):
 //   S <- S * decay;  d = (v - S^T k) * beta;  S <- S + k d^T;  o = S^T q.
-// One warp owns 4 value columns of one head; lane l holds the state rows
-// (keys) l, l + 32, l + 64, l + 96 of those columns in registers, so a token
-// costs two warp reductions of 4 independent sums. The next token's inputs are
-// loaded while the current one is processed. The state never leaves registers
+// One warp owns one value column of one head (two when H * dv > 2048), so
+// many independent per-token chains share each SM; lane l holds the state
+// rows (keys) l, l + 32, l + 64, l + 96 of its columns in registers, so a
+// token costs two warp reductions. The inputs of the next four tokens are in
+// flight while the current one is processed. The state never leaves registers
 // between tokens, so capturing and resuming reproduce an uninterrupted run bit
 // for bit. Any dk that is a power of two up to 128 and any dv up to 128 are
 // accepted, as the reference's `dimensions` check allows (metal.rs:280-290).
@@ -31,102 +32,115 @@ namespace clef {
 
 namespace {
 
-constexpr int PK_WARPS = 4;  // 128-thread CTAs, as the reference dispatches
+constexpr int PK_WARPS = 4;  // 128-thread CTAs
+constexpr int PK_AHEAD = 4;  // tokens whose inputs are in flight ahead of the one being processed
 
-template <int KP>  // key rows per lane: 1 (dk <= 32), 2 (dk = 64), 4 (dk = 128)
+// KP: key rows per lane (1: dk <= 32, 2: dk = 64, 4: dk = 128); NV: value
+// columns per warp (1, or 2 when H * dv warps of one column would not all be
+// resident at once, which would run the token loop in two waves).
+template <int KP, int NV>
 __global__ void __launch_bounds__(PK_WARPS * 32)
     delta_packed_kernel(const float* __restrict__ in, int T, int H, int dk, int dv,
                         const float* __restrict__ init, int capture, float* __restrict__ out) {
   const int lane = threadIdx.x & 31;
-  const int groups = (dv + 3) / 4;
+  const int groups = (dv + NV - 1) / NV;
   const int w = blockIdx.x * PK_WARPS + (threadIdx.x >> 5);
-  if (w >= H * groups) return;
+  if (w >= H * groups) return;  // whole warps
   const int head = w / groups;
-  const int c0 = (w - head * groups) * 4;
+  const int col0 = (w - head * groups) * NV;
   const int width = 2 * dk + dv + 2;
-  float st[KP][4];
+  float st[NV][KP];
 #pragma unroll
-  for (int p = 0; p < KP; ++p)
-#pragma unroll
-    for (int v = 0; v < 4; ++v) {
-      const int key = lane + 32 * p, col = c0 + v;
-      st[p][v] = (init && key < dk && col < dv) ? init[((int64_t)head * dk + key) * dv + col] : 0.f;
-    }
-  // Inputs of token t (loaded one token ahead).
-  float kq[2][KP], vv[4], decay = 0.f, beta = 0.f;
-  auto load = [&](int t, float (&k)[KP], float (&q)[KP], float (&val)[4], float& dc, float& bt) {
-    const float* base = in + ((int64_t)t * H + head) * width;
+  for (int c = 0; c < NV; ++c)
 #pragma unroll
     for (int p = 0; p < KP; ++p) {
-      const int key = lane + 32 * p;
-      q[p] = key < dk ? base[key] : 0.f;
-      k[p] = key < dk ? base[dk + key] : 0.f;
+      const int key = lane + 32 * p, col = col0 + c;
+      st[c][p] = (init && key < dk && col < dv) ? init[((int64_t)head * dk + key) * dv + col] : 0.f;
     }
+  // Ring of the next PK_AHEAD tokens' inputs (slot s holds token t with t % PK_AHEAD == s).
+  float rk[PK_AHEAD][KP], rq[PK_AHEAD][KP], rv[PK_AHEAD][NV], rd[PK_AHEAD], rb[PK_AHEAD];
+  const float* base0 = in + (int64_t)head * width;
+  const int64_t tstride = (int64_t)H * width;
+#define CLEF_PK_LOAD(t, s)                                        \
+  do {                                                            \
+    const float* b_ = base0 + (int64_t)(t) * tstride;             \
+    _Pragma("unroll") for (int p = 0; p < KP; ++p) {              \
+      const int key = lane + 32 * p;                              \
+      rq[s][p] = key < dk ? b_[key] : 0.f;                        \
+      rk[s][p] = key < dk ? b_[dk + key] : 0.f;                   \
+    }                                                             \
+    _Pragma("unroll") for (int c = 0; c < NV; ++c)                \
+      rv[s][c] = col0 + c < dv ? b_[2 * dk + col0 + c] : 0.f;     \
+    rd[s] = b_[2 * dk + dv];                                      \
+    rb[s] = b_[2 * dk + dv + 1];                                  \
+  } while (0)
 #pragma unroll
-    for (int v = 0; v < 4; ++v) val[v] = c0 + v < dv ? base[2 * dk + c0 + v] : 0.f;
-    dc = base[2 * dk + dv];
-    bt = base[2 * dk + dv + 1];
-  };
-  float nk[KP], nq[KP], nv[4], nd, nb;
-  load(0, nk, nq, nv, nd, nb);
+  for (int s = 0; s < PK_AHEAD; ++s)
+    if (s < T) CLEF_PK_LOAD(s, s);
   const int64_t state_out = (int64_t)T * H * dv;
-  for (int t = 0; t < T; ++t) {
+  for (int t0 = 0; t0 < T; t0 += PK_AHEAD) {
 #pragma unroll
-    for (int p = 0; p < KP; ++p) {
-      kq[0][p] = nk[p];
-      kq[1][p] = nq[p];
-    }
-#pragma unroll
-    for (int v = 0; v < 4; ++v) vv[v] = nv[v];
-    decay = nd;
-    beta = nb;
-    if (t + 1 < T) load(t + 1, nk, nq, nv, nd, nb);
-    float mem[4];
-#pragma unroll
-    for (int v = 0; v < 4; ++v) {
-      float acc = 0.f;
+    for (int s = 0; s < PK_AHEAD; ++s) {
+      const int t = t0 + s;
+      if (t >= T) break;
+      float k[KP], q[KP], v[NV];
 #pragma unroll
       for (int p = 0; p < KP; ++p) {
-        st[p][v] = st[p][v] * decay;
-        acc = fmaf(st[p][v], kq[0][p], acc);
+        k[p] = rk[s][p];
+        q[p] = rq[s][p];
       }
-      mem[v] = acc;
-    }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
+      for (int c = 0; c < NV; ++c) v[c] = rv[s][c];
+      const float decay = rd[s], beta = rb[s];
+      if (t + PK_AHEAD < T) CLEF_PK_LOAD(t + PK_AHEAD, s);
+      float mem[NV];
 #pragma unroll
-      for (int v = 0; v < 4; ++v) mem[v] += __shfl_xor_sync(0xffffffffu, mem[v], o);
-    float res[4];
+      for (int c = 0; c < NV; ++c) {
+        mem[c] = 0.f;
 #pragma unroll
-    for (int v = 0; v < 4; ++v) {
-      const float d = (vv[v] - mem[v]) * beta;
-      float acc = 0.f;
-#pragma unroll
-      for (int p = 0; p < KP; ++p) {
-        st[p][v] = fmaf(kq[0][p], d, st[p][v]);
-        acc = fmaf(st[p][v], kq[1][p], acc);
-      }
-      res[v] = acc;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-      for (int v = 0; v < 4; ++v) res[v] += __shfl_xor_sync(0xffffffffu, res[v], o);
-    if (lane == 0) {
-#pragma unroll
-      for (int v = 0; v < 4; ++v)
-        if (c0 + v < dv) out[((int64_t)t * H + head) * dv + c0 + v] = res[v];
-    }
-    if (t + 1 == capture) {
-#pragma unroll
-      for (int p = 0; p < KP; ++p)
-#pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          const int key = lane + 32 * p, col = c0 + v;
-          if (key < dk && col < dv) out[state_out + ((int64_t)head * dk + key) * dv + col] = st[p][v];
+        for (int p = 0; p < KP; ++p) {
+          st[c][p] = st[c][p] * decay;
+          mem[c] = fmaf(st[c][p], k[p], mem[c]);
         }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int c = 0; c < NV; ++c) mem[c] += __shfl_xor_sync(0xffffffffu, mem[c], o);
+      float res[NV];
+#pragma unroll
+      for (int c = 0; c < NV; ++c) {
+        const float d = (v[c] - mem[c]) * beta;
+        res[c] = 0.f;
+#pragma unroll
+        for (int p = 0; p < KP; ++p) {
+          st[c][p] = fmaf(k[p], d, st[c][p]);
+          res[c] = fmaf(st[c][p], q[p], res[c]);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int c = 0; c < NV; ++c) res[c] += __shfl_xor_sync(0xffffffffu, res[c], o);
+      if (lane < NV && col0 + lane < dv) {
+        float r = res[0];
+#pragma unroll
+        for (int c = 1; c < NV; ++c)
+          if (lane == c) r = res[c];
+        out[((int64_t)t * H + head) * dv + col0 + lane] = r;
+      }
+      if (t + 1 == capture) {
+#pragma unroll
+        for (int c = 0; c < NV; ++c)
+#pragma unroll
+          for (int p = 0; p < KP; ++p) {
+            const int key = lane + 32 * p, col = col0 + c;
+            if (key < dk && col < dv) out[state_out + ((int64_t)head * dk + key) * dv + col] = st[c][p];
+          }
+      }
     }
   }
+#undef CLEF_PK_LOAD
 }
 
 // One warp per (token, value head): the value head's query/key head is
@@ -181,15 +195,25 @@ int clef_delta_packed(const float* packed, int64_t T, int32_t H, int32_t dk, int
              CLEF_ERR_INVALID, "delta_packed: fused DeltaNet dimensions (T 1..4096, H 1..32, dk a power of two "
                                "up to 128, dv 1..128)");
   CLEF_CHECK(capture >= 0 && capture <= T, CLEF_ERR_INVALID, "delta_packed: capture boundary");
-  const int groups = (dv + 3) / 4;
-  const unsigned blocks = (unsigned)ceil_div((int64_t)H * groups, PK_WARPS);
   cudaStream_t s = as_stream(stream);
-  if (dk <= 32)
-    delta_packed_kernel<1><<<blocks, PK_WARPS * 32, 0, s>>>(packed, (int)T, H, dk, dv, initial_state, (int)capture, out);
-  else if (dk == 64)
-    delta_packed_kernel<2><<<blocks, PK_WARPS * 32, 0, s>>>(packed, (int)T, H, dk, dv, initial_state, (int)capture, out);
-  else
-    delta_packed_kernel<4><<<blocks, PK_WARPS * 32, 0, s>>>(packed, (int)T, H, dk, dv, initial_state, (int)capture, out);
+  // One column per warp while all H * dv warps fit on the GPU at once
+  // (<= 2048 here); two per warp beyond, so the token loop runs in one wave.
+  const bool two = (int64_t)H * dv > 2048;
+  const int nv = two ? 2 : 1;
+  const unsigned blocks = (unsigned)ceil_div((int64_t)H * ((dv + nv - 1) / nv), PK_WARPS);
+#define CLEF_PK_LAUNCH(KP)                                                                                 \
+  do {                                                                                                   \
+    if (two)                                                                                             \
+      delta_packed_kernel<KP, 2><<<blocks, PK_WARPS * 32, 0, s>>>(packed, (int)T, H, dk, dv, initial_state, \
+                                                                  (int)capture, out);                    \
+    else                                                                                                 \
+      delta_packed_kernel<KP, 1><<<blocks, PK_WARPS * 32, 0, s>>>(packed, (int)T, H, dk, dv, initial_state, \
+                                                                  (int)capture, out);                    \
+  } while (0)
+  if (dk <= 32) CLEF_PK_LAUNCH(1);
+  else if (dk == 64) CLEF_PK_LAUNCH(2);
+  else CLEF_PK_LAUNCH(4);
+#undef CLEF_PK_LAUNCH
   return launch_status("delta_packed");
 }
 

@@ -20,6 +20,9 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
 TAILS = [(1, 1, 1, 1), (33, 2, 4, 5), (33, 2, 32, 13), (257, 2, 64, 13), (257, 2, 128, 13), (17, 2, 128, 128)]
+# Beyond the reference's tails: the widest head count (two value columns per warp) and
+# an odd value width at that head count.
+WIDE = [(65, 32, 128, 128), (40, 32, 64, 127)]
 
 
 def l2(x):
@@ -41,7 +44,7 @@ def pack(q, k, v, g, beta):
                                 dtype=np.float32)
 
 
-@pytest.mark.parametrize("T,H,dk,dv", TAILS)
+@pytest.mark.parametrize("T,H,dk,dv", TAILS + WIDE)
 def test_packed_recurrence_matches_oracle(T, H, dk, dv):
     import clef_b200 as cb
     q, k, v, g, beta = reference_inputs(T, H, dk, dv)

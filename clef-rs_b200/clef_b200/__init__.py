@@ -39,6 +39,7 @@ EXPORTS = [
     "clef_engine_set_weight", "clef_engine_init_random", "clef_engine_get_weight",
     "clef_engine_weight_count", "clef_engine_finalize", "clef_engine_prefill",
     "clef_engine_prefill_device", "clef_engine_set_precision", "clef_engine_precision",
+    "clef_engine_set_sm_limit",
     "clef_engine_launches", "clef_engine_cancel",
     "clef_engine_stage_times", "clef_engine_set_profiling", "clef_engine_destroy",
     "clef_prefix_tokens", "clef_prefix_bytes", "clef_prefix_destroy", "clef_prefix_span_bytes",
@@ -115,6 +116,7 @@ def _load():
         "clef_engine_launches": (_i64, [_vp]),
         "clef_engine_set_precision": (ctypes.c_int, [_vp, _i32]),
         "clef_engine_precision": (_i32, [_vp]),
+        "clef_engine_set_sm_limit": (ctypes.c_int, [_vp, _i32]),
         "clef_engine_cancel": (ctypes.c_int, [_vp, _i32]),
         "clef_engine_stage_times": (ctypes.c_int, [_vp, _vp, _i32]),
         "clef_engine_set_profiling": (ctypes.c_int, [_vp, _i32]),
@@ -472,6 +474,10 @@ class Engine:
         """PRECISION_BF16 (default) or PRECISION_SPLIT (split-BF16 operands and
         F32 projection outputs: F32-class projections at twice the tensor work)."""
         _check(lib.clef_engine_set_precision(self.handle, int(precision)))
+
+    def set_sm_limit(self, sms: int) -> None:
+        """SMs the engine's persistent kernels may occupy (0 = all)."""
+        _check(lib.clef_engine_set_sm_limit(self.handle, int(sms)))
 
     @property
     def precision(self) -> int:

@@ -30,6 +30,15 @@ int device_errors(int* code) {
   return CLEF_OK;
 }
 
+thread_local int g_persistent_cap = 0;
+
+void set_persistent_cap(int ctas) { g_persistent_cap = ctas > 0 ? ctas : 0; }
+
+int persistent_ctas(int device) {
+  const int n = num_sms(device);
+  return g_persistent_cap > 0 && g_persistent_cap < n ? g_persistent_cap : n;
+}
+
 int num_sms(int device) {
   static int cached[64] = {0};
   if (device < 0 || device >= 64) return 148;

@@ -119,5 +119,10 @@ __device__ __forceinline__ float warp_sum(float v) {
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 int num_sms(int device);
+// CTAs a persistent kernel (one CTA per SM) launched from this host thread may
+// use: all SMs, or fewer while a cap is set for the thread (an engine that
+// shares the GPU with another stream's work sets one around its prefill).
+int persistent_ctas(int device);
+void set_persistent_cap(int ctas);  // 0 = no cap
 
 }  // namespace clef

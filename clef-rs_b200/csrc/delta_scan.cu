@@ -1477,7 +1477,7 @@ int launch_delta_scan_planned(const ScanPlan& plan, const float* q, const float*
   CLEF_CUDA(cudaGetDevice(&dev));
   const int64_t pairs = (int64_t)plan.nseq * plan.Hv;
   // Persistent tcgen05 carry: one CTA per SM at most.
-  const int grid = (int)std::min<int64_t>(pairs, num_sms(dev));
+  const int grid = (int)std::min<int64_t>(pairs, persistent_ctas(dev));
   delta_carry_tc_kernel<<<grid, TC_THREADS, TC_SMEM, s>>>(p, (int)pairs);
   return launch_status("delta_carry_tc");
 }

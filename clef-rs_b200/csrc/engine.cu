@@ -123,6 +123,7 @@ struct clef_engine {
   float* inv_freq = nullptr;
   bool finalized = false;
   int precision = CLEF_PRECISION_BF16;
+  int sm_limit = 0;  // SMs the persistent kernels of a prefill may occupy (0 = all)
   int arena_precision = -1;  // precision the activation arena was sized for
   std::atomic<int> cancel{0};
   // geometry
@@ -502,11 +503,18 @@ void collect_stage_times(clef_engine* e) {
 // ids_dev: when set, the token ids already sit in device memory (packed like
 // `ids`) and logits_dev receives the logits on the device; nothing is copied
 // to or from the host except the offsets table.
+// Caps the persistent kernels launched from this thread for the scope.
+struct PersistentCap {
+  explicit PersistentCap(int n) { set_persistent_cap(n); }
+  ~PersistentCap() { set_persistent_cap(0); }
+};
+
 int run_pack(clef_engine* e, const int32_t* ids, const int64_t* offsets, int s0, int s1,
              const clef_prefix* init, int64_t capture, clef_prefix* cap, float* logits,
              float* hidden, int64_t hidden_row0, const int32_t* ids_dev = nullptr,
              float* logits_dev = nullptr) {
   const clef_config& c = e->cfg;
+  PersistentCap sm_cap(e->sm_limit);
   cudaStream_t s = e->stream;
   const int np = s1 - s0;
   const int64_t t0 = offsets[s0];
@@ -1022,6 +1030,14 @@ int clef_engine_set_precision(clef_engine* e, int32_t precision) {
 }
 
 int32_t clef_engine_precision(const clef_engine* e) { return e ? e->precision : -1; }
+
+int clef_engine_set_sm_limit(clef_engine* e, int32_t sms) {
+  CLEF_CHECK(e, CLEF_ERR_INVALID, "set_sm_limit: null engine");
+  CLEF_CHECK(sms >= 0, CLEF_ERR_INVALID, "set_sm_limit: negative SM count");
+  CLEF_CHECK(sms == 0 || sms >= 2, CLEF_ERR_INVALID, "set_sm_limit: at least 2 SMs (one CTA pair)");
+  e->sm_limit = sms;
+  return CLEF_OK;
+}
 
 int clef_engine_cancel(clef_engine* e, int32_t cancel) {
   CLEF_CHECK(e, CLEF_ERR_INVALID, "cancel: null engine");

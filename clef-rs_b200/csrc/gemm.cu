@@ -582,11 +582,11 @@ int launch_gemm(const uint16_t* X, const uint16_t* W, const uint16_t* W2, int64_
   }
   const int tiles = p.tiles_m * p.tiles_n;
   if (pair) {
-    const int clusters = std::min(tiles, num_sms(dev) / 2);
+    const int clusters = std::min(tiles, std::max(1, persistent_ctas(dev) / 2));
     gemm_pair_kernel<<<2 * clusters, THREADS, P_SMEM_BYTES, s>>>(ma, mb, mb2, p);
     return launch_status("gemm_pair");
   }
-  const int grid = std::min(tiles, num_sms(dev));
+  const int grid = std::min(tiles, persistent_ctas(dev));
   gemm_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, mb2, p);
   return launch_status("gemm");
 }

@@ -315,6 +315,14 @@ typedef enum clef_precision { CLEF_PRECISION_BF16 = 0, CLEF_PRECISION_SPLIT = 1 
 int clef_engine_set_precision(clef_engine* e, int32_t precision);
 int32_t clef_engine_precision(const clef_engine* e);
 
+/* Caps the SMs that the engine's persistent kernels (projection GEMMs, scan
+ * carry) occupy during its prefills, 0 = all (the default). Lets two engines,
+ * or an engine and other work, share one GPU on separate streams with their
+ * persistent kernels on disjoint SM sets instead of queueing behind each
+ * other. Results do not depend on it (the same tiles and sequences, spread
+ * over fewer CTAs). No counterpart in the reference. */
+int clef_engine_set_sm_limit(clef_engine* e, int32_t sms);
+
 /* Number of kernels the engine has issued in prefill calls so far. */
 int64_t clef_engine_launches(const clef_engine* e);
 

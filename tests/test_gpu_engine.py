@@ -269,6 +269,21 @@ def test_decisions_match_oracle(models):
         assert abs(a.score - b.score) <= 5e-2
 
 
+def test_sm_limit_changes_nothing_but_placement(models):
+    """clef_engine_set_sm_limit: the persistent kernels on fewer SMs compute
+    the same tiles and sequences, so the logits are bit-identical."""
+    cfg, eng, _ = models
+    seqs = [ids(n, 60 + n) for n in (300, 129, 64)]
+    want, _, _ = eng.prefill(seqs)
+    for sms in (74, 10):
+        eng.set_sm_limit(sms)
+        try:
+            got, _, _ = eng.prefill(seqs)
+        finally:
+            eng.set_sm_limit(0)
+        assert np.array_equal(got, want), sms
+
+
 def test_cancel_between_layers(models):
     import clef_b200 as cb
     cfg, eng, _ = models

@@ -621,6 +621,35 @@ def main():
                 "frac": round(achieved / peak, 4), "peak_source": f"{pk_kind} bf16_tflops_sustained",
                 "traffic": traffic,
                 "stage_ms_per_step": {k: round(v / args.steps, 3) for k, v in stages.items()}}
+    # Memory-bound stages against the measured HBM copy bandwidth: algorithmic
+    # bytes per token (the tensors each stage must read and write once) x tokens
+    # x layers that run the stage, over its live CUDA-event time.
+    hbm_peak = float(pk.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+    n_delta = sum(1 for i in range(cfg.num_hidden_layers) if not cfg.is_attention(i))
+    n_att = cfg.num_hidden_layers - n_delta
+    key, value = cfg.linear_num_key_heads * 128, cfg.linear_num_value_heads * 128
+    hv, hid = cfg.linear_num_value_heads, cfg.hidden_size
+    pb = 4 if split else 2  # projection output bytes
+    att_q, att_kv = cfg.num_attention_heads * cfg.head_dim, cfg.num_key_value_heads * cfg.head_dim
+    per_token = {
+        # conv rows in (q|k|v, a, b), q k v g beta out (F32)
+        "delta_prologue": (n_delta, (2 * key + value + 2 * hv) * pb + (2 * key + value + 2 * hv) * 4),
+        # q k v g beta in, o out (F32)
+        "delta_scan": (n_delta, (2 * key + value + 2 * hv) * 4 + value * 4),
+        # o (F32) and z in, y out (BF16, or the split pair)
+        "delta_epilogue": (n_delta, value * 4 + value * pb + value * 2 * (2 if split else 1)),
+        # h (F32) in, normed operand out (BF16 or split pair); two norms per layer
+        "norm": (2 * cfg.num_hidden_layers, hid * 4 + hid * 2 * (2 if split else 1)),
+    }
+    hbm_stages = {}
+    for name, (layers, nbytes) in per_token.items():
+        ms_stage = stages.get(name, 0.0) / args.steps
+        if ms_stage > 0:
+            gbs = tokens * layers * nbytes / (ms_stage / 1000.0) / 1e9
+            hbm_stages[name] = {"bytes_per_token_layer": nbytes, "ms_per_step": round(ms_stage, 3),
+                                "gbs": round(gbs, 1), "frac": round(gbs / hbm_peak, 3)}
+    roofline["hbm_stages"] = hbm_stages
+    roofline["hbm_peak_gbs"] = hbm_peak
     pre_len = 16384 if prefix is not None else 0
     total_flops = sum(flops_per_request(cfg, int(L), pre_len) for L in lens)
     line = {"metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world,

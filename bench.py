@@ -626,26 +626,25 @@ def main():
     # x layers that run the stage, over its live CUDA-event time.
     hbm_peak = float(pk.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
     n_delta = sum(1 for i in range(cfg.num_hidden_layers) if not cfg.is_attention(i))
-    n_att = cfg.num_hidden_layers - n_delta
-    key, value = cfg.linear_num_key_heads * 128, cfg.linear_num_value_heads * 128
-    hv, hid = cfg.linear_num_value_heads, cfg.hidden_size
-    pb = 4 if split else 2  # projection output bytes
-    att_q, att_kv = cfg.num_attention_heads * cfg.head_dim, cfg.num_key_value_heads * cfg.head_dim
+    w_key, w_val = cfg.linear_num_key_heads * 128, cfg.linear_num_value_heads * 128
+    w_gate, w_hid = cfg.linear_num_value_heads, cfg.hidden_size
+    proj_b = 4 if split else 2  # projection output bytes
+    op_b = 4 if split else 2    # GEMM operand bytes per element (split pair: hi + lo)
     per_token = {
         # conv rows in (q|k|v, a, b), q k v g beta out (F32)
-        "delta_prologue": (n_delta, (2 * key + value + 2 * hv) * pb + (2 * key + value + 2 * hv) * 4),
+        "delta_prologue": (n_delta, (2 * w_key + w_val + 2 * w_gate) * (proj_b + 4)),
         # q k v g beta in, o out (F32)
-        "delta_scan": (n_delta, (2 * key + value + 2 * hv) * 4 + value * 4),
-        # o (F32) and z in, y out (BF16, or the split pair)
-        "delta_epilogue": (n_delta, value * 4 + value * pb + value * 2 * (2 if split else 1)),
-        # h (F32) in, normed operand out (BF16 or split pair); two norms per layer
-        "norm": (2 * cfg.num_hidden_layers, hid * 4 + hid * 2 * (2 if split else 1)),
+        "delta_scan": (n_delta, (2 * w_key + w_val + 2 * w_gate) * 4 + w_val * 4),
+        # o (F32) and z in, y out (the out-projection's operand)
+        "delta_epilogue": (n_delta, w_val * (4 + proj_b + op_b)),
+        # h (F32) in, normed operand out; two norms per layer
+        "norm": (2 * cfg.num_hidden_layers, w_hid * (4 + op_b)),
     }
     hbm_stages = {}
-    for name, (layers, nbytes) in per_token.items():
+    for name, (n_layers, nbytes) in per_token.items():
         ms_stage = stages.get(name, 0.0) / args.steps
         if ms_stage > 0:
-            gbs = tokens * layers * nbytes / (ms_stage / 1000.0) / 1e9
+            gbs = tokens * n_layers * nbytes / (ms_stage / 1000.0) / 1e9
             hbm_stages[name] = {"bytes_per_token_layer": nbytes, "ms_per_step": round(ms_stage, 3),
                                 "gbs": round(gbs, 1), "frac": round(gbs / hbm_peak, 3)}
     roofline["hbm_stages"] = hbm_stages

@@ -8,7 +8,7 @@ seed 7729 (fixtures/synthetic/provenance.json); its CPU backbone must reproduce
 This script only re-packages the tensors (names, shapes and values unchanged)
 into one .npz so the tests can run where the reference checkout is absent.
 
-Usage: python tests/golden/make_golden.py [REFERENCE_ROOT]
+Usage: python tests/golden/make_golden.py REFERENCE_ROOT
 """
 import json
 import sys
@@ -19,7 +19,9 @@ from safetensors.numpy import load_file
 
 
 def main() -> None:
-    root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {Path(__file__).name} <checkout of the reference project>")
+    root = Path(sys.argv[1])
     fx = root / "crates/core/fixtures/synthetic"
     weights = load_file(str(fx / "backbone.safetensors"))
     expected = load_file(str(fx / "backbone-output.safetensors"))["hidden"]

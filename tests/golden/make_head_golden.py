@@ -10,7 +10,7 @@ with `logits.{i}` within 1e-5 + 1e-4|e| (mod.rs:75-86). This script only
 re-packages the tensors (names, shapes and values unchanged) into one .npz so
 the tests run where the reference checkout is absent.
 
-Usage: python tests/golden/make_head_golden.py [REFERENCE_ROOT]
+Usage: python tests/golden/make_head_golden.py REFERENCE_ROOT
 """
 import json
 import sys
@@ -28,7 +28,9 @@ QUESTIONS = [
 
 
 def main() -> None:
-    root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {Path(__file__).name} <checkout of the reference project>")
+    root = Path(sys.argv[1])
     fx = root / "crates/core/fixtures/synthetic"
     weights = load_file(str(fx / "head.safetensors"))
     inputs = load_file(str(fx / "head-input.safetensors"))

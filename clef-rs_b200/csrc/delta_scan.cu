@@ -33,10 +33,7 @@
 // A capture point inside a chunk does not change the chunking: the state at
 // the capture token is formed from the same chunk quantities, so a prefill with
 // capture is bit-identical to one without.
-#include <cudaTypedefs.h>
-
 #include <algorithm>
-#include <cstring>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -960,19 +957,14 @@ namespace {
 //   M     [R | O1] = S^T [K; Q]^T                           -> r_bar
 //   E c   R <- V^T - R diag(e^G); split in place            -> c_bar
 //   M     D = X_R (T diag beta)^T                           -> d_bar
-//   E g   outputs of chunk k - 1 (O1 read in step a): a full chunk's two
-//         32-token halves are staged in stage k - 1's consumed K/Q image and
-//         written by one TMA tile store each (the warps of a half gather on
-//         og_bar, one thread stores and waits for the store to read the
-//         tile); a partial chunk's rows go out by per-thread stores
-//                                                          -> stage k - 1 free
+//   E g   outputs of chunk k - 1 (O1 read in step a)       -> stage k - 1 free
 //   E e   X_D' = split D diag(egd); split D in place        -> e_bar
 //   M     S^T += X_D' K -> i_bar; O2 = X_D P^T -> f_bar, stage k free
 // ---------------------------------------------------------------------------
 constexpr int TC_STAGE = 100352;  // one chunk's K/Q and T/P images, 1024-aligned
 constexpr int TC_THREADS = 320;
 constexpr int TC_OFF_BAR = 2 * TC_STAGE;
-constexpr int TC_SMEM = 1024 + TC_OFF_BAR + 19 * 8;
+constexpr int TC_SMEM = 1024 + TC_OFF_BAR + 17 * 8;
 static_assert(KQ_IMG + TP_IMG <= TC_STAGE && TC_STAGE % 1024 == 0, "carry stage layout");
 constexpr uint32_t TC_S = 0, TC_SA = 128, TC_R = 256, TC_O1 = 320, TC_D = 384, TC_O2 = 448;
 
@@ -1005,8 +997,7 @@ __device__ __forceinline__ uint32_t tok_col(uint32_t base, bool lo, int t) {
   return base + 32 * (t >> 1) + 8 * (t & 1) + (lo ? 16 : 0);
 }
 
-__global__ void __launch_bounds__(TC_THREADS, 1)
-    delta_carry_tc_kernel(PipeArgs p, int npairs, const __grid_constant__ CUtensorMap map_out, int tma_out) {
+__global__ void __launch_bounds__(TC_THREADS, 1) delta_carry_tc_kernel(PipeArgs p, int npairs) {
   using namespace sm100;
   extern __shared__ __align__(128) uint8_t sm_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>(((uintptr_t)sm_raw + 1023) & ~(uintptr_t)1023);
@@ -1027,7 +1018,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t* capd_bar = bar + 13;  // capture chunk: captured state read by the 8 warps
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 15);
-  uint64_t* og_bar = bar + 16;    // [2] the 4 warps of an output half staged their rows
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&full[i], 1);
@@ -1043,8 +1033,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     mbar_init(drain, 1);
     mbar_init(cap_bar, 1);
     mbar_init(capd_bar, 8);
-    mbar_init(&og_bar[0], 4);
-    mbar_init(&og_bar[1], 4);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -1195,44 +1183,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     };
     // g: O^T = (S^T Q^T) diag(e^G) + D^T P^T of chunk c (CTA chunk kc, stage
     // stc), the first term read earlier into o1s.
-    // Completed phases of og_bar: every epilogue thread takes the same branch
-    // for every chunk, so the counter agrees across the 8 warps.
-    uint32_t og_phase = 0;
     auto do_g = [&](const ScanChunk& c, int stc, int kc, int h, const float (&o1s)[32]) -> bool {
       if (!wait_all(f_bar, kc & 1)) return false;
       tc_fence_after();
       uint32_t o2[32];
       tmem_ld_32x32b_x32(lq + TC_O2 + 32 * hf, o2);
       tmem_ld_wait();
-      if (tma_out && c.n == C) {
-        // Row i of this half's [32 tokens x 128 dv] tile; the stage's K/Q
-        // image is free once O2 of the chunk has completed (f_bar).
-        float* tile = reinterpret_cast<float*>(sm + stc * TC_STAGE) + hf * (32 * DV);
+      const int nmine = c.n - 32 * hf;
+      float* op = a.out + ((c.t0 + 32 * hf) * a.Hv + h) * DV + row;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) tile[i * DV + row] = o1s[i] + __uint_as_float(o2[i]);
-        fence_async_shared();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&og_bar[hf]);
-        const uint32_t parity = og_phase & 1;
-        ++og_phase;
-        if (q == 0) {
-          // One thread stores the half tile once its 4 warps have written it,
-          // and the stage is released only after the store has read it.
-          if (!wait_all(&og_bar[hf], parity)) return false;
-          if (lane == 0) {
-            tma_store_2d(&map_out, tile, h * DV, (int)(c.t0 + 32 * hf));
-            bulk_commit();
-            bulk_wait_read();
-          }
-          __syncwarp();
-        }
-      } else {
-        const int nmine = c.n - 32 * hf;
-        float* op = a.out + ((c.t0 + 32 * hf) * a.Hv + h) * DV + row;
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (i < nmine) op[i * tstride] = o1s[i] + __uint_as_float(o2[i]);
-      }
+      for (int i = 0; i < 32; ++i)
+        if (i < nmine) op[i * tstride] = o1s[i] + __uint_as_float(o2[i]);
       arrive(&empty[stc]);
       return true;
     };
@@ -1482,36 +1443,6 @@ int delta_scan_plan(const int64_t* cu_host, int nseq, int Hk, int Hv, void* ws, 
   return CLEF_OK;
 }
 
-namespace {
-PFN_cuTensorMapEncodeTiled_v12000 scan_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  }
-  return fn;
-}
-
-// The scan output o [T, Hv, 128] F32 as a 2-D tensor [T rows, Hv * 128
-// columns], box 128 columns x 32 rows, no swizzle (rows of 512 bytes).
-int out_map(CUtensorMap* m, float* out, int64_t T, int Hv) {
-  auto fn = scan_encode_fn();
-  if (!fn) return fail(CLEF_ERR_CUDA, "delta_scan: cuTensorMapEncodeTiled unavailable");
-  cuuint64_t dims[2] = {(cuuint64_t)Hv * DV, (cuuint64_t)T};
-  cuuint64_t strides[1] = {(cuuint64_t)Hv * DV * sizeof(float)};
-  cuuint32_t box[2] = {DV, 32};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, out, dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(CLEF_ERR_CUDA, "delta_scan: output tensor map");
-  return CLEF_OK;
-}
-}  // namespace
-
 int launch_delta_scan_planned(const ScanPlan& plan, const float* q, const float* k, const float* v,
                               const float* g, const float* beta, const float* init, int init_shared,
                               int64_t capture, float* capture_state, float* final_state, float* out,
@@ -1547,15 +1478,7 @@ int launch_delta_scan_planned(const ScanPlan& plan, const float* q, const float*
   const int64_t pairs = (int64_t)plan.nseq * plan.Hv;
   // Persistent tcgen05 carry: one CTA per SM at most.
   const int grid = (int)std::min<int64_t>(pairs, persistent_ctas(dev));
-  // Output rows [T, Hv * 128] F32 as a TMA tensor: boxes of 128 values x 32 tokens.
-  CUtensorMap map_out;
-  memset(&map_out, 0, sizeof(map_out));
-  int tma_out = 0;
-  if (plan.total >= C && ((uintptr_t)out & 15) == 0) {
-    RC_(out_map(&map_out, out, plan.total, plan.Hv));
-    tma_out = 1;
-  }
-  delta_carry_tc_kernel<<<grid, TC_THREADS, TC_SMEM, s>>>(p, (int)pairs, map_out, tma_out);
+  delta_carry_tc_kernel<<<grid, TC_THREADS, TC_SMEM, s>>>(p, (int)pairs);
   return launch_status("delta_carry_tc");
 }
 

@@ -235,21 +235,6 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 
-// 2-D tiled store shared -> global (no multicast), tracked in this thread's
-// bulk async-group; the global coordinates must be non-negative and x 16-byte
-// aligned in bytes. The source tile is read asynchronously: wait with
-// bulk_wait_read() before the shared memory is reused.
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
-               "r"(smem_u32(src)), "r"(x), "r"(y)
-               : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-// Waits until every committed bulk store of this thread has read its source.
-__device__ __forceinline__ void bulk_wait_read() {
-  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-}
-
 // Shared-memory matrix descriptor for a K-major operand tile stored with the
 // 128-byte swizzle (rows of 64 BF16, 8-row groups 1024 bytes apart):
 // start>>4 [0,14), LBO>>4 = 1 [16,30), SBO>>4 = 64 [32,46), version 1 [46,48),

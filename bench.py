@@ -66,7 +66,7 @@ def parse():
     ap.add_argument("--cpu-sample-tokens", type=int, default=256)
     ap.add_argument("--profile-op", default=None,
                     choices=["gemm", "gemm_swiglu", "gemm_split", "scan", "scan1", "packed", "attention",
-                             "attention_tc", "prologue", "head"],
+                             "attention_tc", "attention_prefix", "prologue", "head"],
                     help="run one operator on a profiling-sized case and exit (for ncu)")
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--scan-seqs", type=int, default=64,
@@ -403,27 +403,30 @@ def profile_op(args):
         v = torch.randn(4, T, 256, device=dev).bfloat16()
         for _ in range(args.reps):
             cb.attention_gqa(q, k, v)
-    elif args.profile_op == "attention_tc":
+    elif args.profile_op in ("attention_tc", "attention_prefix"):
         # Token-major q/k and transposed V as the engine keeps them; the C ABI
         # is called directly so only the attention kernel runs per repetition.
-        T, H, Hkv = 4096, 16, 4
+        # attention_prefix: 2048 queries after a 16384-token shared prefix (the
+        # shape of a config-5 suffix).
+        T, P, H, Hkv = (4096, 0, 16, 4) if args.profile_op == "attention_tc" else (2048, 16384, 16, 4)
+        Tk = T + P
         q = torch.randn(T, H, 256, device=dev).bfloat16()
-        k = torch.randn(T, Hkv, 256, device=dev).bfloat16()
-        vt = torch.randn(Hkv * 256, T, device=dev).bfloat16()
+        k = torch.randn(Tk, Hkv, 256, device=dev).bfloat16()
+        vt = torch.randn(Hkv * 256, Tk, device=dev).bfloat16()
         o = torch.empty(T, H, 256, device=dev)
         st = torch.cuda.current_stream()
         ptr = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
-        flops = 2 * 2 * H * 256 * (T * (T + 1) // 2)
+        flops = 2 * 2 * H * 256 * (T * P + T * (T + 1) // 2)
         for i in range(args.reps):
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
-            rc = cb.lib.clef_attention_gqa_vt(ptr(q), ptr(k), ptr(vt), H, Hkv, T, T, 256, T, ptr(o),
+            rc = cb.lib.clef_attention_gqa_vt(ptr(q), ptr(k), ptr(vt), H, Hkv, T, Tk, 256, Tk, ptr(o),
                                               ctypes.c_void_p(st.cuda_stream))
             e1.record()
             assert rc == 0, cb.lib.clef_last_error().decode()
             torch.cuda.synchronize()
             ms = e0.elapsed_time(e1)
-            print(f"attention_tc T={T}: {ms:.3f} ms, {flops / ms / 1e9:.1f} TFLOP/s", flush=True)
+            print(f"{args.profile_op} T={T} prefix={P}: {ms:.3f} ms, {flops / ms / 1e9:.1f} TFLOP/s", flush=True)
     elif args.profile_op == "prologue":
         T, Hk, Hv = 16384, 16, 32
         width = 2 * Hk * 128 + Hv * 128

@@ -85,6 +85,13 @@ def max_threads() -> int:
 
 # BF16 rounding points of oracle.cpp (kRound*): 0 is the reference's F32 path.
 ROUND_OPERAND, ROUND_PROJ, ROUND_ATTN_QKV, ROUND_P, ROUND_FLOW = 1, 2, 4, 8, 16
+# Finer sites (each also inside ROUND_OPERAND or ROUND_PROJ): the operand of
+# a mixer's projections, of gate/up, of down, of DeltaNet out_proj, of o_proj;
+# the outputs of DeltaNet in_proj_qkv, the attention projections, in_proj_z and
+# in_proj_a/b.
+(ROUND_OP_MIX_IN, ROUND_OP_MLP_IN, ROUND_OP_DOWN, ROUND_OP_DELTA_OUT, ROUND_OP_ATTN_OUT,
+ ROUND_PROJ_DELTA_QKV, ROUND_PROJ_ATTN, ROUND_PROJ_DELTA_Z, ROUND_PROJ_DELTA_AB) = (
+    32, 64, 128, 256, 512, 1024, 2048, 4096, 8192)
 
 
 def set_rounding(mask: int) -> None:

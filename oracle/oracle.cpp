@@ -64,6 +64,16 @@ enum {
   kRoundAttnQKV = 4,
   kRoundP = 8,
   kRoundFlow = 16,
+  // Finer sites, each also covered by kRoundOperand / kRoundProj above.
+  kRoundOpMixIn = 32,       // normed hidden into a mixer's projections
+  kRoundOpMlpIn = 64,       // normed hidden into gate/up
+  kRoundOpDown = 128,       // SwiGLU activation into down
+  kRoundOpDeltaOut = 256,   // gated DeltaNet output into out_proj
+  kRoundOpAttnOut = 512,    // gated attention output into o_proj
+  kRoundProjDeltaQKV = 1024,  // DeltaNet in_proj_qkv output (conv input)
+  kRoundProjAttn = 2048,      // attention q/gate, k, v projection outputs
+  kRoundProjDeltaZ = 4096,    // DeltaNet in_proj_z output
+  kRoundProjDeltaAB = 8192,   // DeltaNet in_proj_a / in_proj_b outputs
 };
 int g_round = 0;
 
@@ -437,7 +447,7 @@ void delta_forward(const Model& m, int li, const float* x, int64_t t, const Laye
   const int taps = c.linear_conv_kernel_dim;
   std::vector<float> proj;
   linear(m, p + ".in_proj_qkv.weight", x, t, proj);
-  round_if(kRoundProj, proj);
+  round_if(kRoundProj | kRoundProjDeltaQKV, proj);
   const int64_t hist = init ? init->history_rows : 0;
   std::vector<float> projected((size_t)(hist + t) * width);
   if (hist) memcpy(projected.data(), init->history.data(), sizeof(float) * hist * width);
@@ -450,8 +460,8 @@ void delta_forward(const Model& m, int li, const float* x, int64_t t, const Laye
   std::vector<float> a, b;
   linear(m, p + ".in_proj_a.weight", x, t, a);
   linear(m, p + ".in_proj_b.weight", x, t, b);
-  round_if(kRoundProj, a);
-  round_if(kRoundProj, b);
+  round_if(kRoundProj | kRoundProjDeltaAB, a);
+  round_if(kRoundProj | kRoundProjDeltaAB, b);
   const auto& dt = W(m, p + ".dt_bias").data;
   const auto& alog = W(m, p + ".A_log").data;
   std::vector<float> g((size_t)t * hv), beta((size_t)t * hv);
@@ -480,7 +490,7 @@ void delta_forward(const Model& m, int li, const float* x, int64_t t, const Laye
   // norm(out) (no offset, qwen.rs:581-586) * silu(z) (qwen.rs:671-676).
   std::vector<float> z;
   linear(m, p + ".in_proj_z.weight", x, t, z);
-  round_if(kRoundProj, z);
+  round_if(kRoundProj | kRoundProjDeltaZ, z);
   const std::vector<float> nw = norm_weight(m, p + ".norm.weight", false);
   std::vector<float> normed((size_t)t * value);
   round_if(kRoundFlow, out);
@@ -488,7 +498,7 @@ void delta_forward(const Model& m, int li, const float* x, int64_t t, const Laye
   round_if(kRoundFlow, normed);
   std::vector<float> gated((size_t)t * value);
   for (int64_t i = 0; i < t * value; ++i) gated[i] = normed[i] * siluf_(z[i]);
-  round_if(kRoundOperand, gated);
+  round_if(kRoundOperand | kRoundOpDeltaOut, gated);
   if (capture && saved) {
     saved->full = false;
     saved->recurrent = captured;
@@ -512,9 +522,9 @@ void attention_forward(const Model& m, int li, const float* x, int64_t t,
   linear(m, p + ".q_proj.weight", x, t, proj);  // [t, heads, 2d]
   linear(m, p + ".k_proj.weight", x, t, kp);    // [t, kvh, d]
   linear(m, p + ".v_proj.weight", x, t, vp);    // [t, kvh, d]
-  round_if(kRoundProj, proj);
-  round_if(kRoundProj, kp);
-  round_if(kRoundProj | kRoundAttnQKV, vp);
+  round_if(kRoundProj | kRoundProjAttn, proj);
+  round_if(kRoundProj | kRoundProjAttn, kp);
+  round_if(kRoundProj | kRoundProjAttn | kRoundAttnQKV, vp);
   std::vector<float> gate((size_t)t * heads * d), qraw((size_t)t * heads * d);
   for (int64_t i = 0; i < t; ++i)
     for (int h = 0; h < heads; ++h) {
@@ -577,7 +587,7 @@ void attention_forward(const Model& m, int li, const float* x, int64_t t,
         }
         o[idx] = av * gv;
       }
-  round_if(kRoundOperand, o);
+  round_if(kRoundOperand | kRoundOpAttnOut, o);
   linear(m, p + ".o_proj.weight", o.data(), t, mixed_out);
 }
 
@@ -612,7 +622,7 @@ int prefill(const Model& m, const int32_t* ids, int64_t t, const Prefix* init, i
     const std::string p = L(li);
     const std::vector<float> wi = norm_weight(m, p + ".input_layernorm.weight", true);
     rms_rows(h.data(), wi.data(), t, hsz, c.rms_norm_eps, u.data());
-    round_if(kRoundOperand, u);
+    round_if(kRoundOperand | kRoundOpMixIn, u);
     const LayerState* st = init ? &init->layers[li] : nullptr;
     LayerState* sv = saved ? &saved->layers[li] : nullptr;
     if (c.layer_types[li])
@@ -622,12 +632,12 @@ int prefill(const Model& m, const int32_t* ids, int64_t t, const Prefix* init, i
     for (int64_t i = 0; i < t * hsz; ++i) h[i] = h[i] + mixed[i];
     const std::vector<float> wp = norm_weight(m, p + ".post_attention_layernorm.weight", true);
     rms_rows(h.data(), wp.data(), t, hsz, c.rms_norm_eps, u.data());
-    round_if(kRoundOperand, u);
+    round_if(kRoundOperand | kRoundOpMlpIn, u);
     std::vector<float> gt, up;
     linear(m, p + ".mlp.gate_proj.weight", u.data(), t, gt);
     linear(m, p + ".mlp.up_proj.weight", u.data(), t, up);
     for (size_t i = 0; i < gt.size(); ++i) gt[i] = siluf_(gt[i]) * up[i];
-    round_if(kRoundOperand, gt);
+    round_if(kRoundOperand | kRoundOpDown, gt);
     linear(m, p + ".mlp.down_proj.weight", gt.data(), t, ff);
     for (int64_t i = 0; i < t * hsz; ++i) h[i] = h[i] + ff[i];
   }

@@ -216,27 +216,25 @@ __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.f +
 __device__ __forceinline__ void pro_finish(const float4 (&x)[4], const float (&tw)[4][4], int64_t t, int c, int key,
                                            int Hv, float qscale, float* __restrict__ q, float* __restrict__ k,
                                            float* __restrict__ v) {
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  // Packed two-lane F32 multiplies and adds, each lane rounded on its own:
+  // the same multiply-then-add per tap as the scalar form, half the issues.
+  float2 a01 = make_float2(0.f, 0.f), a23 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int tap = 0; tap < 4; ++tap) {
-    acc.x = __fadd_rn(acc.x, __fmul_rn(x[tap].x, tw[tap][0]));
-    acc.y = __fadd_rn(acc.y, __fmul_rn(x[tap].y, tw[tap][1]));
-    acc.z = __fadd_rn(acc.z, __fmul_rn(x[tap].z, tw[tap][2]));
-    acc.w = __fadd_rn(acc.w, __fmul_rn(x[tap].w, tw[tap][3]));
+    a01 = __fadd2_rn(a01, __fmul2_rn(make_float2(x[tap].x, x[tap].y), make_float2(tw[tap][0], tw[tap][1])));
+    a23 = __fadd2_rn(a23, __fmul2_rn(make_float2(x[tap].z, x[tap].w), make_float2(tw[tap][2], tw[tap][3])));
   }
-  const float4 m = make_float4(silu_fast(acc.x), silu_fast(acc.y), silu_fast(acc.z), silu_fast(acc.w));
+  const float4 m = make_float4(silu_fast(a01.x), silu_fast(a01.y), silu_fast(a23.x), silu_fast(a23.y));
   if (c < 2 * key) {
     // The whole warp sits in one head (channel blocks of 1024, heads of 128).
     float ss = m.x * m.x + m.y * m.y + m.z * m.z + m.w * m.w;
     ss = warp_sum(ss);
     float inv = 1.f / sqrtf(ss + 1e-6f);
-    if (c < key) {
-      inv = __fmul_rn(inv, qscale);
-      *reinterpret_cast<float4*>(q + t * key + c) = make_float4(m.x * inv, m.y * inv, m.z * inv, m.w * inv);
-    } else {
-      *reinterpret_cast<float4*>(k + t * key + (c - key)) =
-          make_float4(m.x * inv, m.y * inv, m.z * inv, m.w * inv);
-    }
+    if (c < key) inv = __fmul_rn(inv, qscale);
+    const float2 i2 = make_float2(inv, inv);
+    const float2 n01 = __fmul2_rn(make_float2(m.x, m.y), i2), n23 = __fmul2_rn(make_float2(m.z, m.w), i2);
+    float* dst = c < key ? q + t * key + c : k + t * key + (c - key);
+    *reinterpret_cast<float4*>(dst) = make_float4(n01.x, n01.y, n23.x, n23.y);
   } else {
     *reinterpret_cast<float4*>(v + t * (int64_t)(Hv * 128) + (c - 2 * key)) = m;
   }

@@ -214,3 +214,46 @@ def test_precision_setter_validates_before_touching_an_engine():
     assert cb.lib.clef_engine_set_precision(None, 1) == 1
     assert cb.lib.clef_engine_precision(None) == -1
     assert cb.PRECISION_BF16 == 0 and cb.PRECISION_SPLIT == 1
+
+
+def test_header_is_plain_c_and_a_c_caller_links_every_entry(tmp_path):
+    """The header compiles as strict C11 (what bindgen or cgo read) and a C
+    program that takes the address of every declared entry links against
+    libclef_b200.so and runs its host-only entries, as a foreign caller would."""
+    import shutil
+    import subprocess
+    if shutil.which("gcc") is None:
+        pytest.skip("no C compiler")
+    names = header_functions()
+    table = ",\n".join(f'  {{"{n}", (fn)&{n}}}' for n in names)
+    src = tmp_path / "caller.c"
+    src.write_text(f"""#include "clef_b200.h"
+#include <stdio.h>
+#include <string.h>
+typedef void (*fn)(void);
+static const struct {{ const char* name; fn f; }} table[] = {{
+{table}
+}};
+int main(void) {{
+  size_t i;
+  float logits[7] = {{0.5f, -0.5f, 1.0f, 3.0f, 3.0f, 0.5f, 2.0f}};
+  clef_decision d;
+  for (i = 0; i < sizeof table / sizeof table[0]; ++i)
+    if (!table[i].f) return 10;
+  if (!strstr(clef_version(), "sm_100a")) return 11;
+  if (clef_config_validate(NULL) == 0) return 12;
+  if (strlen(clef_last_error()) == 0) return 13;
+  if (clef_decide(logits, 1, 7, &d) != 0) return 14;
+  if (d.choice != 1) return 15; /* the first of two equal maxima */
+  printf("%d entries\\n", (int)(sizeof table / sizeof table[0]));
+  return 0;
+}}
+""")
+    lib_dir = cb.LIB_PATH.parent
+    exe = tmp_path / "caller"
+    subprocess.run(["gcc", "-std=c11", "-Wall", "-Wextra", "-Werror", "-pedantic",
+                    "-I", str(ROOT / "include"), str(src), "-L", str(lib_dir), "-lclef_b200",
+                    f"-Wl,-rpath,{lib_dir}", "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert out.returncode == 0, (out.returncode, out.stderr)
+    assert out.stdout.strip() == f"{len(names)} entries"

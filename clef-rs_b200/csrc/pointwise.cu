@@ -229,7 +229,7 @@ __device__ __forceinline__ void pro_finish(const float4 (&x)[4], const float (&t
     // The whole warp sits in one head (channel blocks of 1024, heads of 128).
     float ss = m.x * m.x + m.y * m.y + m.z * m.z + m.w * m.w;
     ss = warp_sum(ss);
-    float inv = 1.f / sqrtf(ss + 1e-6f);
+    float inv = rsqrtf(ss + 1e-6f);  // the approximate reciprocal square root (a few ulp)
     if (c < key) inv = __fmul_rn(inv, qscale);
     const float2 i2 = make_float2(inv, inv);
     const float2 n01 = __fmul2_rn(make_float2(m.x, m.y), i2), n23 = __fmul2_rn(make_float2(m.z, m.w), i2);

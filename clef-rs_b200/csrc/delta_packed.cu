@@ -16,14 +16,21 @@
 // The recurrence kernel is the reference's per-token update in F32
 // (delta_recurrence_prefill, qwen.rs:867-880; clef_delta, delta.metal:18-131):
 //   S <- S * decay;  d = (v - S^T k) * beta;  S <- S + k d^T;  o = S^T q.
-// One warp owns one value column of one head (two when H * dv > 2048), so
-// many independent per-token chains share each SM; lane l holds the state
-// rows (keys) l, l + 32, l + 64, l + 96 of its columns in registers, so a
-// token costs two warp reductions. The inputs of the next four tokens are in
-// flight while the current one is processed. The state never leaves registers
-// between tokens, so capturing and resuming reproduce an uninterrupted run bit
-// for bit. Any dk that is a power of two up to 128 and any dv up to 128 are
-// accepted, as the reference's `dimensions` check allows (metal.rs:280-290).
+// Every (head, value column) is an independent chain through the tokens. A
+// column is held by LPC lanes of a warp, each keeping KL = dk / LPC state rows
+// (keys) in registers, so a warp carries 32 / LPC columns and a token costs
+// two reductions of log2(LPC) shuffle levels. The per-token work is bound by
+// the SM's load/store data path (shuffles and loads share it), so a lane's
+// keys are interleaved in pairs (lane j of a group holds keys 2j + 2 LPC i +
+// {0, 1}): the group's q and k loads of one pair index read one contiguous
+// 8 LPC-byte run, and the arithmetic runs on packed two-lane F32 multiplies
+// and FMAs (each lane rounded as the scalar form is). Each token's packed row
+// is prefetched into L1 PK_PREFETCH tokens ahead and its q, k, v, decay and
+// beta are loaded one token ahead into a second register set. The state never
+// leaves registers between tokens, so capturing and resuming reproduce an
+// uninterrupted run bit for bit. Any dk that is a power of two up to 128 and
+// any dv up to 128 are accepted, as the reference's `dimensions` check allows
+// (metal.rs:280-290).
 #include <cmath>
 
 #include "kernels.cuh"
@@ -32,115 +39,153 @@ namespace clef {
 
 namespace {
 
-constexpr int PK_WARPS = 4;  // 128-thread CTAs
-constexpr int PK_AHEAD = 4;  // tokens whose inputs are in flight ahead of the one being processed
+constexpr int PK_WARPS = 4;      // 128-thread CTAs
+constexpr int PK_PREFETCH = 16;  // tokens between a row's L1 prefetch and its use
+constexpr int PK_LPC128 = 8;     // lanes per value column when dk = 128
 
-// KP: key rows per lane (1: dk <= 32, 2: dk = 64, 4: dk = 128); NV: value
-// columns per warp (1, or 2 when H * dv warps of one column would not all be
-// resident at once, which would run the token loop in two waves).
-template <int KP, int NV>
+__device__ __forceinline__ void prefetch_l1(const float* p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
+// One token's inputs for one lane.
+template <int KL>
+struct PkTok {
+  float q[KL], k[KL];
+  float v, decay, beta;
+};
+
+// KL key rows per lane, LPC lanes per value column (KL * LPC = dk). PAIRS: KL
+// is even and the lane's keys are read as float2 pairs (the packed row width
+// 2 dk + dv + 2 is even and the input 8-byte aligned, so every row starts on
+// 8 bytes); otherwise key p of lane j is j + LPC p, read as single floats.
+template <int KL, int LPC, bool PAIRS>
 __global__ void __launch_bounds__(PK_WARPS * 32)
     delta_packed_kernel(const float* __restrict__ in, int T, int H, int dk, int dv,
                         const float* __restrict__ init, int capture, float* __restrict__ out) {
+  constexpr int CPW = 32 / LPC;  // value columns per warp
+  constexpr bool EVEN = KL % 2 == 0;
+  constexpr int NP = EVEN ? KL / 2 : 0;                // packed pairs per lane
+  constexpr int NA = NP >= 4 ? 4 : (NP > 0 ? NP : 1);  // independent packed partial sums
   const int lane = threadIdx.x & 31;
-  const int groups = (dv + NV - 1) / NV;
+  const int j = lane % LPC, cl = lane / LPC;
+  const int groups = (dv + CPW - 1) / CPW;
   const int w = blockIdx.x * PK_WARPS + (threadIdx.x >> 5);
   if (w >= H * groups) return;  // whole warps
   const int head = w / groups;
-  const int col0 = (w - head * groups) * NV;
+  const int col = (w - head * groups) * CPW + cl;
+  const bool live = col < dv;  // lanes past dv carry a zero chain and store nothing
   const int width = 2 * dk + dv + 2;
-  float st[NV][KP];
+  auto key_of = [&](int p) { return PAIRS ? 2 * j + 2 * LPC * (p >> 1) + (p & 1) : j + LPC * p; };
+  float st[KL];
 #pragma unroll
-  for (int c = 0; c < NV; ++c)
-#pragma unroll
-    for (int p = 0; p < KP; ++p) {
-      const int key = lane + 32 * p, col = col0 + c;
-      st[c][p] = (init && key < dk && col < dv) ? init[((int64_t)head * dk + key) * dv + col] : 0.f;
-    }
-  // Ring of the next PK_AHEAD tokens' inputs (slot s holds token t with t % PK_AHEAD == s).
-  float rk[PK_AHEAD][KP], rq[PK_AHEAD][KP], rv[PK_AHEAD][NV], rd[PK_AHEAD], rb[PK_AHEAD];
+  for (int p = 0; p < KL; ++p) st[p] = (init && live) ? init[((int64_t)head * dk + key_of(p)) * dv + col] : 0.f;
   const float* base0 = in + (int64_t)head * width;
   const int64_t tstride = (int64_t)H * width;
-#define CLEF_PK_LOAD(t, s)                                        \
-  do {                                                            \
-    const float* b_ = base0 + (int64_t)(t) * tstride;             \
-    _Pragma("unroll") for (int p = 0; p < KP; ++p) {              \
-      const int key = lane + 32 * p;                              \
-      rq[s][p] = key < dk ? b_[key] : 0.f;                        \
-      rk[s][p] = key < dk ? b_[dk + key] : 0.f;                   \
-    }                                                             \
-    _Pragma("unroll") for (int c = 0; c < NV; ++c)                \
-      rv[s][c] = col0 + c < dv ? b_[2 * dk + col0 + c] : 0.f;     \
-    rd[s] = b_[2 * dk + dv];                                      \
-    rb[s] = b_[2 * dk + dv + 1];                                  \
-  } while (0)
+  auto load = [&](PkTok<KL>& x, int t) {
+    const float* b = base0 + (int64_t)t * tstride;
+    if (PAIRS) {
 #pragma unroll
-  for (int s = 0; s < PK_AHEAD; ++s)
-    if (s < T) CLEF_PK_LOAD(s, s);
-  const int64_t state_out = (int64_t)T * H * dv;
-  for (int t0 = 0; t0 < T; t0 += PK_AHEAD) {
-#pragma unroll
-    for (int s = 0; s < PK_AHEAD; ++s) {
-      const int t = t0 + s;
-      if (t >= T) break;
-      float k[KP], q[KP], v[NV];
-#pragma unroll
-      for (int p = 0; p < KP; ++p) {
-        k[p] = rk[s][p];
-        q[p] = rq[s][p];
+      for (int i = 0; i < KL / 2; ++i) {
+        const float2 qq = *reinterpret_cast<const float2*>(b + 2 * j + 2 * LPC * i);
+        const float2 kk = *reinterpret_cast<const float2*>(b + dk + 2 * j + 2 * LPC * i);
+        x.q[2 * i] = qq.x, x.q[2 * i + 1] = qq.y;
+        x.k[2 * i] = kk.x, x.k[2 * i + 1] = kk.y;
       }
+    } else {
 #pragma unroll
-      for (int c = 0; c < NV; ++c) v[c] = rv[s][c];
-      const float decay = rd[s], beta = rb[s];
-      if (t + PK_AHEAD < T) CLEF_PK_LOAD(t + PK_AHEAD, s);
-      float mem[NV];
-#pragma unroll
-      for (int c = 0; c < NV; ++c) {
-        mem[c] = 0.f;
-#pragma unroll
-        for (int p = 0; p < KP; ++p) {
-          st[c][p] = st[c][p] * decay;
-          mem[c] = fmaf(st[c][p], k[p], mem[c]);
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int c = 0; c < NV; ++c) mem[c] += __shfl_xor_sync(0xffffffffu, mem[c], o);
-      float res[NV];
-#pragma unroll
-      for (int c = 0; c < NV; ++c) {
-        const float d = (v[c] - mem[c]) * beta;
-        res[c] = 0.f;
-#pragma unroll
-        for (int p = 0; p < KP; ++p) {
-          st[c][p] = fmaf(k[p], d, st[c][p]);
-          res[c] = fmaf(st[c][p], q[p], res[c]);
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int c = 0; c < NV; ++c) res[c] += __shfl_xor_sync(0xffffffffu, res[c], o);
-      if (lane < NV && col0 + lane < dv) {
-        float r = res[0];
-#pragma unroll
-        for (int c = 1; c < NV; ++c)
-          if (lane == c) r = res[c];
-        out[((int64_t)t * H + head) * dv + col0 + lane] = r;
-      }
-      if (t + 1 == capture) {
-#pragma unroll
-        for (int c = 0; c < NV; ++c)
-#pragma unroll
-          for (int p = 0; p < KP; ++p) {
-            const int key = lane + 32 * p, col = col0 + c;
-            if (key < dk && col < dv) out[state_out + ((int64_t)head * dk + key) * dv + col] = st[c][p];
-          }
+      for (int p = 0; p < KL; ++p) {
+        x.q[p] = b[j + LPC * p];
+        x.k[p] = b[dk + j + LPC * p];
       }
     }
+    x.v = live ? b[2 * dk + col] : 0.f;
+    x.decay = b[2 * dk + dv];
+    x.beta = b[2 * dk + dv + 1];
+  };
+  // Every 128-byte line of token t's row (width <= 386 floats < 32 lanes x 32).
+  auto prefetch = [&](int t) {
+    if (t < T) {
+      const float* b = base0 + (int64_t)t * tstride;
+      if (lane * 32 < width) prefetch_l1(b + lane * 32);
+      if (lane == 31) prefetch_l1(b + width - 1);
+    }
+  };
+  const int64_t state_out = (int64_t)T * H * dv;
+  // Group-of-LPC sum of per-lane packed partial sums (or of the scalar one).
+  auto reduce = [&](const float2 (&a)[NA], float scalar) {
+    float r = scalar;
+    if (EVEN) {
+      float2 s2 = a[0];
+#pragma unroll
+      for (int i = 1; i < NA; ++i) s2 = __fadd2_rn(s2, a[i]);
+      r = s2.x + s2.y;
+    }
+#pragma unroll
+    for (int o = LPC / 2; o > 0; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+    return r;
+  };
+  auto step = [&](const PkTok<KL>& x, int t) {
+    float2 a[NA];
+    float sa = 0.f;
+#pragma unroll
+    for (int i = 0; i < NA; ++i) a[i] = make_float2(0.f, 0.f);
+    if (EVEN) {
+      const float2 dd = make_float2(x.decay, x.decay);
+#pragma unroll
+      for (int i = 0; i < NP; ++i) {
+        const float2 s2 = __fmul2_rn(make_float2(st[2 * i], st[2 * i + 1]), dd);
+        st[2 * i] = s2.x, st[2 * i + 1] = s2.y;
+        a[i % NA] = __ffma2_rn(s2, make_float2(x.k[2 * i], x.k[2 * i + 1]), a[i % NA]);
+      }
+    } else {
+#pragma unroll
+      for (int p = 0; p < KL; ++p) {
+        st[p] = st[p] * x.decay;
+        sa = fmaf(st[p], x.k[p], sa);
+      }
+    }
+    const float mem = reduce(a, sa);
+    const float d = (x.v - mem) * x.beta;
+#pragma unroll
+    for (int i = 0; i < NA; ++i) a[i] = make_float2(0.f, 0.f);
+    sa = 0.f;
+    if (EVEN) {
+      const float2 d2 = make_float2(d, d);
+#pragma unroll
+      for (int i = 0; i < NP; ++i) {
+        const float2 s2 =
+            __ffma2_rn(make_float2(x.k[2 * i], x.k[2 * i + 1]), d2, make_float2(st[2 * i], st[2 * i + 1]));
+        st[2 * i] = s2.x, st[2 * i + 1] = s2.y;
+        a[i % NA] = __ffma2_rn(s2, make_float2(x.q[2 * i], x.q[2 * i + 1]), a[i % NA]);
+      }
+    } else {
+#pragma unroll
+      for (int p = 0; p < KL; ++p) {
+        st[p] = fmaf(x.k[p], d, st[p]);
+        sa = fmaf(st[p], x.q[p], sa);
+      }
+    }
+    const float res = reduce(a, sa);
+    if (j == 0 && live) out[((int64_t)t * H + head) * dv + col] = res;
+    if (t + 1 == capture && live) {
+#pragma unroll
+      for (int p = 0; p < KL; ++p) out[state_out + ((int64_t)head * dk + key_of(p)) * dv + col] = st[p];
+    }
+  };
+#pragma unroll 1
+  for (int t = 0; t < PK_PREFETCH; ++t) prefetch(t);
+  PkTok<KL> A, B;
+  load(A, 0);
+#pragma unroll 1
+  for (int t = 0; t < T; t += 2) {
+    if (t + 1 < T) load(B, t + 1);
+    prefetch(t + PK_PREFETCH);
+    step(A, t);
+    if (t + 1 >= T) break;
+    if (t + 2 < T) load(A, t + 2);
+    prefetch(t + 1 + PK_PREFETCH);
+    step(B, t + 1);
   }
-#undef CLEF_PK_LOAD
 }
 
 // One warp per (token, value head): the value head's query/key head is
@@ -196,23 +241,32 @@ int clef_delta_packed(const float* packed, int64_t T, int32_t H, int32_t dk, int
                                "up to 128, dv 1..128)");
   CLEF_CHECK(capture >= 0 && capture <= T, CLEF_ERR_INVALID, "delta_packed: capture boundary");
   cudaStream_t s = as_stream(stream);
-  // One column per warp while all H * dv warps fit on the GPU at once
-  // (<= 2048 here); two per warp beyond, so the token loop runs in one wave.
-  const bool two = (int64_t)H * dv > 2048;
-  const int nv = two ? 2 : 1;
-  const unsigned blocks = (unsigned)ceil_div((int64_t)H * ((dv + nv - 1) / nv), PK_WARPS);
-#define CLEF_PK_LAUNCH(KP)                                                                                 \
-  do {                                                                                                   \
-    if (two)                                                                                             \
-      delta_packed_kernel<KP, 2><<<blocks, PK_WARPS * 32, 0, s>>>(packed, (int)T, H, dk, dv, initial_state, \
-                                                                  (int)capture, out);                    \
-    else                                                                                                 \
-      delta_packed_kernel<KP, 1><<<blocks, PK_WARPS * 32, 0, s>>>(packed, (int)T, H, dk, dv, initial_state, \
-                                                                  (int)capture, out);                    \
+  // LPC lanes per value column, 32 / LPC columns per warp.
+  const int lpc = dk == 128 ? PK_LPC128 : dk < 4 ? dk : 4;
+  const int groups = (dv + 32 / lpc - 1) / (32 / lpc);
+  const unsigned blocks = (unsigned)ceil_div((int64_t)H * groups, PK_WARPS);
+  const bool pairs = dv % 2 == 0 && ((uintptr_t)packed & 7) == 0;
+#define CLEF_PK_LAUNCH(KL, LPC, PAIRS) \
+  delta_packed_kernel<KL, LPC, PAIRS><<<blocks, PK_WARPS * 32, 0, s>>>(packed, (int)T, H, dk, dv, initial_state, \
+                                                                       (int)capture, out)
+#define CLEF_PK_LAUNCH2(KL, LPC)        \
+  do {                                  \
+    if (pairs)                          \
+      CLEF_PK_LAUNCH(KL, LPC, true);    \
+    else                                \
+      CLEF_PK_LAUNCH(KL, LPC, false);   \
   } while (0)
-  if (dk <= 32) CLEF_PK_LAUNCH(1);
-  else if (dk == 64) CLEF_PK_LAUNCH(2);
-  else CLEF_PK_LAUNCH(4);
+  switch (dk) {
+    case 128: CLEF_PK_LAUNCH2(128 / PK_LPC128, PK_LPC128); break;
+    case 64: CLEF_PK_LAUNCH2(16, 4); break;
+    case 32: CLEF_PK_LAUNCH2(8, 4); break;
+    case 16: CLEF_PK_LAUNCH2(4, 4); break;
+    case 8: CLEF_PK_LAUNCH2(2, 4); break;
+    case 4: CLEF_PK_LAUNCH(1, 4, false); break;
+    case 2: CLEF_PK_LAUNCH(1, 2, false); break;
+    default: CLEF_PK_LAUNCH(1, 1, false); break;
+  }
+#undef CLEF_PK_LAUNCH2
 #undef CLEF_PK_LAUNCH
   return launch_status("delta_packed");
 }

@@ -379,24 +379,24 @@ __global__ void __launch_bounds__(256) delta_epilogue_kernel(const float* __rest
 // all H + Hkv rows of 256 features, which go four at a time (8 features per
 // lane, loads issued up front). Rows [0, H) are query heads (projection
 // columns h*2d .. h*2d+d), rows [H, H+Hkv) key heads (columns 2*H*d + j*d).
-// Norm and rotation run in F32; the rotated features are rounded once, to
-// the BF16 operands of the tensor-core attention. The projection rows are
-// BF16 (the engine's default precision) or F32 (its split precision).
+// Each rotation pair (f, f + half), f < half, sits in one lane: lane l <
+// half/4 holds features [4l, 4l + 4) and [half + 4l, half + 4l + 4), lane
+// l >= half/4 the 8 features from rot + 8 (l - half/4); so a lane's norm
+// weights and cos/sin are read once per token and no lane needs another's
+// features. Norm and rotation run in F32; the rotated features are rounded
+// once, to the BF16 operands of the tensor-core attention. The projection rows
+// are BF16 (the engine's default precision) or F32 (its split precision).
 constexpr int AP_WARPS = 8;
 
-// Eight consecutive projection features of one lane as F32.
-__device__ __forceinline__ void load8(const uint16_t* src, float x[8]) {
-  const uint4 r = *reinterpret_cast<const uint4*>(src);
-  const uint32_t r32[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    x[2 * i] = __uint_as_float(r32[i] << 16);
-    x[2 * i + 1] = __uint_as_float(r32[i] & 0xffff0000u);
-  }
+// Four consecutive projection features as F32.
+__device__ __forceinline__ void load4(const uint16_t* src, float* x) {
+  const uint2 r = *reinterpret_cast<const uint2*>(src);
+  x[0] = __uint_as_float(r.x << 16), x[1] = __uint_as_float(r.x & 0xffff0000u);
+  x[2] = __uint_as_float(r.y << 16), x[3] = __uint_as_float(r.y & 0xffff0000u);
 }
-__device__ __forceinline__ void load8(const float* src, float x[8]) {
-  const float4 a = *reinterpret_cast<const float4*>(src), b = *reinterpret_cast<const float4*>(src + 4);
-  x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
+__device__ __forceinline__ void load4(const float* src, float* x) {
+  const float4 a = *reinterpret_cast<const float4*>(src);
+  x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w;
 }
 
 template <typename In>
@@ -405,7 +405,7 @@ __global__ void __launch_bounds__(AP_WARPS * 32) attention_prologue_kernel(
     const float* __restrict__ kw, float eps, const int64_t* __restrict__ cu, int nseq, int64_t pos_offset,
     int H, int Hkv, int rot, const float* __restrict__ inv_freq, uint16_t* __restrict__ q_out,
     uint16_t* __restrict__ k_out, int64_t T) {
-  __shared__ float cs_tab[AP_WARPS][2][128];
+  __shared__ __align__(16) float cs_tab[AP_WARPS][2][128];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t t = (int64_t)blockIdx.x * AP_WARPS + warp;
   if (t >= T) return;
@@ -420,7 +420,18 @@ __global__ void __launch_bounds__(AP_WARPS * 32) attention_prologue_kernel(
   }
   __syncwarp();
   const int per = H + Hkv;
-  const int lane_half = half / 8;  // lanes covering the first half
+  const bool rl = lane < half / 4;  // a rotation lane
+  const int off0 = rl ? 4 * lane : rot + 8 * (lane - half / 4);
+  const int off1 = rl ? half + 4 * lane : off0 + 4;
+  // This lane's norm weights (q and k) and, on a rotation lane, cos/sin of
+  // frequencies 4l .. 4l + 3.
+  float wq[8], wk[8], cs[4], sn[4];
+  load4(qw + off0, wq), load4(qw + off1, wq + 4);
+  load4(kw + off0, wk), load4(kw + off1, wk + 4);
+  if (rl) {
+    load4(&cs_tab[warp][0][4 * lane], cs);
+    load4(&cs_tab[warp][1][4 * lane], sn);
+  }
   for (int h0 = 0; h0 < per; h0 += 4) {
     float xs[4][8];
 #pragma unroll
@@ -429,7 +440,8 @@ __global__ void __launch_bounds__(AP_WARPS * 32) attention_prologue_kernel(
       if (hh < per) {
         const In* src = hh < H ? proj + t * ldp + (int64_t)hh * 2 * d
                                : proj + t * ldp + (int64_t)2 * H * d + (int64_t)(hh - H) * d;
-        load8(src + lane * 8, xs[u]);
+        load4(src + off0, xs[u]);
+        load4(src + off1, xs[u] + 4);
       }
     }
 #pragma unroll
@@ -437,7 +449,6 @@ __global__ void __launch_bounds__(AP_WARPS * 32) attention_prologue_kernel(
       const int hh = h0 + u;
       if (hh >= per) break;
       const bool isq = hh < H;
-      const float* wn = isq ? qw : kw;
       float x[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) x[i] = xs[u][i];
@@ -447,29 +458,20 @@ __global__ void __launch_bounds__(AP_WARPS * 32) attention_prologue_kernel(
       ss = warp_sum(ss);
       const float inv = 1.f / sqrtf(ss / (float)d + eps);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) x[i] = __fmul_rn(__fmul_rn(x[i], inv), wn[lane * 8 + i]);
-      // Partial NeoX rotation on features [0, rot): pairs (i, i + rot/2).
-      float partner[8];
+      for (int i = 0; i < 8; ++i) x[i] = __fmul_rn(__fmul_rn(x[i], inv), isq ? wq[i] : wk[i]);
+      if (rl) {
+        // Partial NeoX rotation: x cos + rotate_half(x) sin on the pairs
+        // (x[j], x[4 + j]) = features (4l + j, half + 4l + j).
 #pragma unroll
-      for (int i = 0; i < 8; ++i) partner[i] = __shfl_xor_sync(0xffffffffu, x[i], lane_half);
-      if (lane * 8 < rot) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int f = lane * 8 + i;
-          const int fi = f < half ? f : f - half;
-          const float c = cs_tab[warp][0][fi], sn = cs_tab[warp][1][fi];
-          // rotation * cos + rotate_half(rotation) * sin
-          const float rotated = f < half ? -partner[i] : partner[i];
-          x[i] = __fadd_rn(__fmul_rn(x[i], c), __fmul_rn(rotated, sn));
+        for (int j = 0; j < 4; ++j) {
+          const float lo = x[j], hi = x[4 + j];
+          x[j] = __fadd_rn(__fmul_rn(lo, cs[j]), __fmul_rn(-hi, sn[j]));
+          x[4 + j] = __fadd_rn(__fmul_rn(hi, cs[j]), __fmul_rn(lo, sn[j]));
         }
       }
       uint16_t* dst = isq ? q_out + (t * H + hh) * (int64_t)d : k_out + (t * Hkv + (hh - H)) * (int64_t)d;
-      uint4 ov;
-      ov.x = pack_bf16x2(x[0], x[1]);
-      ov.y = pack_bf16x2(x[2], x[3]);
-      ov.z = pack_bf16x2(x[4], x[5]);
-      ov.w = pack_bf16x2(x[6], x[7]);
-      *reinterpret_cast<uint4*>(dst + lane * 8) = ov;
+      *reinterpret_cast<uint2*>(dst + off0) = make_uint2(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]));
+      *reinterpret_cast<uint2*>(dst + off1) = make_uint2(pack_bf16x2(x[4], x[5]), pack_bf16x2(x[6], x[7]));
     }
   }
 }

@@ -23,6 +23,11 @@ TAILS = [(1, 1, 1, 1), (33, 2, 4, 5), (33, 2, 32, 13), (257, 2, 64, 13), (257, 2
 # Beyond the reference's tails: the widest head count (two value columns per warp) and
 # an odd value width at that head count.
 WIDE = [(65, 32, 128, 128), (40, 32, 64, 127)]
+# Every register layout of the kernel (lanes per value column x keys per lane, with the
+# paired key loads used for an even dv and the single ones for an odd dv) not covered
+# above.
+LAYOUTS = [(37, 3, 2, 6), (37, 3, 2, 7), (37, 3, 4, 6), (37, 3, 8, 10), (37, 3, 8, 9), (37, 3, 16, 24),
+           (37, 3, 16, 3), (37, 3, 32, 40), (37, 3, 64, 66)]
 
 
 def l2(x):
@@ -44,7 +49,7 @@ def pack(q, k, v, g, beta):
                                 dtype=np.float32)
 
 
-@pytest.mark.parametrize("T,H,dk,dv", TAILS + WIDE)
+@pytest.mark.parametrize("T,H,dk,dv", TAILS + WIDE + LAYOUTS)
 def test_packed_recurrence_matches_oracle(T, H, dk, dv):
     import clef_b200 as cb
     q, k, v, g, beta = reference_inputs(T, H, dk, dv)
@@ -58,7 +63,7 @@ def test_packed_recurrence_matches_oracle(T, H, dk, dv):
     assert err < 1e-5
 
 
-@pytest.mark.parametrize("dk,dv", [(4, 5), (128, 128), (128, 13)])
+@pytest.mark.parametrize("dk,dv", [(4, 5), (128, 128), (128, 13), (64, 64), (8, 8)])
 def test_packed_capture_and_resume_are_exact(dk, dv):
     import clef_b200 as cb
     T, H = 257, 2

@@ -463,7 +463,10 @@ __global__ void transpose_v_kernel(const In* __restrict__ v, int64_t v_ts, int64
                                    const int64_t* __restrict__ cu, const int64_t* __restrict__ cu_vt,
                                    const int32_t* __restrict__ cu_kb, int nseq, int64_t total,
                                    uint16_t* __restrict__ vt, int64_t vt_pitch) {
-  __shared__ uint16_t tile[64][D + 8];
+  // tileT[e][w]: feature e of keys (2w, 2w + 1) as one 32-bit word; the word
+  // index is XOR-swizzled by (e & 7) << 2 so that both the column stores of
+  // the first phase and the 16-byte row reads of the second are conflict-free.
+  __shared__ __align__(16) uint32_t tileT[D][32];
   const int kvh = blockIdx.y;
   int s = 0;
   int64_t start = 0, len = total, off = 0;
@@ -476,26 +479,27 @@ __global__ void transpose_v_kernel(const In* __restrict__ v, int64_t v_ts, int64
     kb = blockIdx.x - cu_kb[s];
   }
   const int64_t j0 = (int64_t)kb * 64;
-  for (int idx = threadIdx.x; idx < 64 * (D / 8); idx += blockDim.x) {
-    const int j = idx / (D / 8), e8 = (idx % (D / 8)) * 8;
-    uint4 val = make_uint4(0, 0, 0, 0);
-    if (j0 + j < len) val = load_v8(v + (start + j0 + j) * v_ts + kvh * v_hs + e8);
-    const uint32_t w[4] = {val.x, val.y, val.z, val.w};
+  // Phase 1: lane = key pair, 8 features per thread from both keys' rows.
+  for (int idx = threadIdx.x; idx < 32 * (D / 8); idx += blockDim.x) {
+    const int jp = idx & 31, e8 = (idx >> 5) * 8;
+    const int64_t r0 = j0 + 2 * jp;
+    uint4 a = make_uint4(0, 0, 0, 0), b = a;
+    if (r0 < len) a = load_v8(v + (start + r0) * v_ts + kvh * v_hs + e8);
+    if (r0 + 1 < len) b = load_v8(v + (start + r0 + 1) * v_ts + kvh * v_hs + e8);
+    const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wb[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
-      tile[j][e8 + 2 * t] = (uint16_t)(w[t] & 0xffff);
-      tile[j][e8 + 2 * t + 1] = (uint16_t)(w[t] >> 16);
+      const int e = e8 + 2 * t;
+      tileT[e][jp ^ ((e & 7) << 2)] = __byte_perm(wa[t], wb[t], 0x5410);
+      tileT[e + 1][jp ^ (((e + 1) & 7) << 2)] = __byte_perm(wa[t], wb[t], 0x7632);
     }
   }
   __syncthreads();
+  // Phase 2: V^T row e, keys [8q, 8q + 8) as one 16-byte read and store.
   for (int idx = threadIdx.x; idx < D * 8; idx += blockDim.x) {
-    const int e = idx / 8, j8 = (idx % 8) * 8;
-    uint32_t w[4];
-#pragma unroll
-    for (int t = 0; t < 4; ++t)
-      w[t] = (uint32_t)tile[j8 + 2 * t][e] | ((uint32_t)tile[j8 + 2 * t + 1][e] << 16);
-    *reinterpret_cast<uint4*>(vt + (int64_t)(kvh * D + e) * vt_pitch + off + j0 + j8) =
-        make_uint4(w[0], w[1], w[2], w[3]);
+    const int e = idx >> 3, q = idx & 7, j8 = q * 8;
+    const uint4 w = *reinterpret_cast<const uint4*>(&tileT[e][(4 * q) ^ ((e & 7) << 2)]);
+    *reinterpret_cast<uint4*>(vt + (int64_t)(kvh * D + e) * vt_pitch + off + j0 + j8) = w;
   }
 }
 

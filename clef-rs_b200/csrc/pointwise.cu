@@ -352,14 +352,28 @@ __global__ void __launch_bounds__(256) delta_epilogue_kernel(const float* __rest
         zr[u] = *reinterpret_cast<const ZV*>(z + t * ldz + (h0 + u) * 128 + lane * 4);
       }
     }
+    // Row sums of the HB = 4 heads by reduce-scatter: after the xor-16 and
+    // xor-8 exchanges lane l holds the partial of head 2 ((l >> 4) & 1) +
+    // ((l >> 3) & 1) over four lanes, the xor-4/2/1 tree completes it (the
+    // same pairings as a full butterfly per head, so the same sums), and lane
+    // 8u hands head u's normaliser to the warp.
+    float ss[HB];
+#pragma unroll
+    for (int u = 0; u < HB; ++u)
+      ss[u] = h0 + u < Hv ? a[u].x * a[u].x + a[u].y * a[u].y + a[u].z * a[u].z + a[u].w * a[u].w : 0.f;
+    const bool b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1;
+    const float k0 = (b4 ? ss[2] : ss[0]) + __shfl_xor_sync(0xffffffffu, b4 ? ss[0] : ss[2], 16);
+    const float k1 = (b4 ? ss[3] : ss[1]) + __shfl_xor_sync(0xffffffffu, b4 ? ss[1] : ss[3], 16);
+    float part = (b3 ? k1 : k0) + __shfl_xor_sync(0xffffffffu, b3 ? k0 : k1, 8);
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    const float inv_mine = 1.f / sqrtf(part / 128.f + eps);
 #pragma unroll
     for (int u = 0; u < HB; ++u) {
+      const float inv = __shfl_sync(0xffffffffu, inv_mine, 8 * u);
       if (h0 + u >= Hv) break;
       const float4 zv = ProIn<ZIn>::f4(zr[u]);
       const float4 b = a[u];
-      float ss = b.x * b.x + b.y * b.y + b.z * b.z + b.w * b.w;
-      ss = warp_sum(ss);
-      const float inv = 1.f / sqrtf(ss / 128.f + eps);
       const float y0 = __fmul_rn(__fmul_rn(__fmul_rn(b.x, inv), wv.x), silu_f(zv.x));
       const float y1 = __fmul_rn(__fmul_rn(__fmul_rn(b.y, inv), wv.y), silu_f(zv.y));
       const float y2 = __fmul_rn(__fmul_rn(__fmul_rn(b.z, inv), wv.z), silu_f(zv.z));

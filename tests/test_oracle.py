@@ -214,3 +214,30 @@ def test_chunk_form_capture_and_gqa(capture):
     assert np.abs(o - ref_o).max() < 2e-6
     assert np.abs(s - ref_s).max() < 2e-6
     assert np.abs(c - ref_c).max() < 2e-6
+
+
+def test_rounding_sites_partition_the_coarse_switches(golden, fixture_model):
+    """The oracle's per-site BF16 rounding switches (a measuring aid for device
+    precisions) split the two coarse ones exactly: the five GEMM-operand sites
+    together reproduce ROUND_OPERAND and the four projection-output sites
+    ROUND_PROJ, bit for bit; every site alone moves the result; 0 is the F32 path."""
+    m, ids = fixture_model, golden["ids"]
+    ops = [oracle.ROUND_OP_MIX_IN, oracle.ROUND_OP_MLP_IN, oracle.ROUND_OP_DOWN, oracle.ROUND_OP_DELTA_OUT,
+           oracle.ROUND_OP_ATTN_OUT]
+    projs = [oracle.ROUND_PROJ_DELTA_QKV, oracle.ROUND_PROJ_ATTN, oracle.ROUND_PROJ_DELTA_Z,
+             oracle.ROUND_PROJ_DELTA_AB]
+    base, _ = m.prefill(ids)
+
+    def run(mask):
+        oracle.set_rounding(mask)
+        try:
+            return m.prefill(ids)[0]
+        finally:
+            oracle.set_rounding(0)
+
+    assert np.array_equal(run(oracle.ROUND_OPERAND), run(sum(ops)))
+    assert np.array_equal(run(oracle.ROUND_PROJ), run(sum(projs)))
+    for bit in ops + projs:
+        assert not np.array_equal(run(bit), base), bit
+    assert np.array_equal(m.prefill(ids)[0], base)
+    assert_close(base, golden["expected"])

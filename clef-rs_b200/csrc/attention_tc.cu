@@ -121,20 +121,23 @@ __global__ void __launch_bounds__(THREADS, 1)
   float* l_part = reinterpret_cast<float*>(sm + OFF_LSUM);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.y;
+  // Grid (heads, query blocks): the heads vary fastest, so the blocks of every
+  // head go out in the order below, heaviest (last) query block first.
+  const int h = blockIdx.x;
+  const int bx = blockIdx.y;
   const int kvh = h / (p.H / p.Hkv);
   int s = 0;
   int64_t start = 0, len = p.total, vt0 = 0;
   int qb;
   if (p.cu) {
-    s = find_seq(p.cu_qb, p.nseq, blockIdx.x);
+    s = find_seq(p.cu_qb, p.nseq, bx);
     start = p.cu[s];
     len = p.cu[s + 1] - start;
     vt0 = p.cu_vt ? p.cu_vt[s] : start;
     const int nqb = p.cu_qb[s + 1] - p.cu_qb[s];
-    qb = nqb - 1 - (blockIdx.x - p.cu_qb[s]);
+    qb = nqb - 1 - (bx - p.cu_qb[s]);
   } else {
-    qb = (int)((len + BQ - 1) / BQ) - 1 - blockIdx.x;
+    qb = (int)((len + BQ - 1) / BQ) - 1 - bx;
   }
   const int64_t q0 = (int64_t)qb * BQ;
   const int64_t P = p.prefix_len;
@@ -617,7 +620,8 @@ int launch_attention_tc(const AttnTcArgs& a, const SeqPackVT& pk, cudaStream_t s
     attr[dev] = true;
   }
   const unsigned blocks = pk.cu ? (unsigned)pk.qblocks : (unsigned)ceil_div(pk.total, BQ);
-  attention_tc_kernel<<<dim3(blocks, (unsigned)a.H), THREADS, SMEM, s>>>(mq, mk, mvt, mpk, mpvt, mg, p);
+  CLEF_CHECK(blocks <= 65535u, CLEF_ERR_UNSUPPORTED, "attention_tc: more than 65535 query blocks in one call");
+  attention_tc_kernel<<<dim3((unsigned)a.H, blocks), THREADS, SMEM, s>>>(mq, mk, mvt, mpk, mpvt, mg, p);
   return launch_status("attention_tc");
 }
 
